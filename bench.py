@@ -1,0 +1,367 @@
+#!/usr/bin/env python
+"""Benchmark of the fused MorphoAttention forward + backward on B200.
+
+Default workload: the long-sequence layer (B=4, N=4096, D=1024, H=16, cube_m=32,
+scale=0.5, non-causal; fp16), one forward plus the backward of ``out.sum()`` per step.
+With ``--gpus N`` (launched under torchrun) every rank runs that per-rank batch on its own
+batch shard (weak scaling) and the fp32 weight-gradient bucket is all-reduced with NCCL.
+
+Prints ONE JSON line on rank 0.  ``--impl reference`` times the reference path's CPU
+formulation instead (the oracle restatement; the reference itself ships only CUDA code)
+on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fused fwd+bwd tokens/sec per B200 and whole-box at 1/2/4/8 GPUs; % of roofline"
+UNIT = "tokens/s"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p["bf16_tflops_sustained"]), "sm_max_mhz": float(p["sm_max_mhz"]),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0,
+                "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampler running during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(cfg, seconds: float = 12.0, max_reps: int = 5):
+    """Time the fp32 CPU oracle (a restatement of the reference path) on one sequence of
+    the workload: forward + backward of out.sum(), all host threads."""
+    import torch
+    from morphottention_b200.configs import make_inputs
+    from oracle import morpho_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    one = cfg.with_(B=1)
+    inp = make_inputs(one)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max_reps and (time.perf_counter() - t_start) < seconds or len(times) < 2:
+        t0 = time.perf_counter()
+        O.forward_backward(inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], one.H, one.cube_m,
+                           one.scale, one.causal)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times[1:]) if len(times) > 2 else times[-1]
+    return {"value": one.N / t, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 of {cfg.B} sequences (N={cfg.N}, all {cfg.H} heads), fwd+bwd, fp32 torch CPU, "
+                      f"median of {len(times) - 1 if len(times) > 2 else 1} timed reps",
+            "seconds_per_sequence": t}
+
+
+def run_reference(args):
+    """--impl reference: the CPU formulation of the reference path on the host cores."""
+    import torch
+    from morphottention_b200.configs import CONFIGS, make_inputs
+    from oracle import morpho_oracle as O
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    one = cfg.with_(B=1)
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = make_inputs(one)
+
+    def step():
+        O.forward_backward(inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], one.H, one.cube_m,
+                           one.scale, one.causal)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = one.N * args.steps / dt
+    cores = torch.get_num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: x~N(0,1) seeded, module default init",
+            "config": _config_dict(cfg, args.gpus, per_step_note="each step = 1 sequence of the workload"),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"1 of {cfg.B} sequences per step (N={cfg.N}, all {cfg.H} heads), fwd+bwd"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _config_dict(cfg, world, per_step_note=None):
+    d = {"workload": f"{cfg.name}: single MorphoAttention layer fwd + backward(out.sum())",
+         "B_per_gpu": cfg.B, "N": cfg.N, "D": cfg.D, "H": cfg.H, "cube_m": cfg.cube_m, "head_dim": cfg.head_dim,
+         "scale": cfg.scale, "causal": cfg.causal, "global_batch": cfg.B * world, "seq_len": cfg.N,
+         "parallelism": f"dp{world}", "l2": "inputs larger than L2 (>300 MB touched per step), no flush"}
+    if per_step_note:
+        d["step"] = per_step_note
+    return d
+
+
+def algorithmic_flops(cfg):
+    """Dense-contraction FLOPs per launch of each kernel (recompute included per launch)."""
+    m, hd, T = cfg.cube_m, cfg.head_dim, cfg.tokens
+    nn = cfg.pairs()
+    gemm = 2.0 * T * cfg.D * (cfg.H * m + cfg.D)
+    return {"attn_bwd": 2.0 * nn * (3 * m + 2 * hd), "attn_fwd": 2.0 * nn * (m + hd), "proj": gemm,
+            "dx_gemm": gemm, "dw_gemm": gemm}
+
+
+def run_ours(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import morphottention_b200 as M
+    from morphottention_b200 import capi
+    from morphottention_b200.configs import CONFIGS, make_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = CONFIGS[args.config]
+    w = make_inputs(cfg, device="cpu")  # weights: identical on every rank
+    if world > 1:
+        g = torch.Generator().manual_seed(cfg.seed * 1000 + rank)
+        w["x"] = torch.empty(cfg.B, cfg.N, cfg.D).normal_(0.0, 1.0, generator=g).half()
+    t = {k: v.to(dev) for k, v in w.items()}
+    x, W_phi, gq, gk, W_V = t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"]
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    grad = torch.ones_like(x)  # d out.sum() / d out
+    out = torch.empty_like(x)
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
+    dX = torch.empty_like(x)
+    dW_phi, dW_V = torch.empty_like(W_phi), torch.empty_like(W_V)
+    dgq, dgk = torch.empty_like(gq), torch.empty_like(gk)
+    bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev) if world > 1 else None
+
+    def step():
+        capi.forward(p, x, W_phi, gq, gk, W_V, out, lse)
+        if world > 1:
+            capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, None, None, None, None, dweights_f32=bucket)
+            dist.all_reduce(bucket)
+            capi.finalize_weight_grads(p, bucket, 1.0 / world, dW_phi, dgq, dgk, dW_V)
+        else:
+            capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    status = capi.device_status(reset=True)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    capi.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    prof = capi.profile_collect()
+    capi.profile_enable(False)
+    ms = ev0.elapsed_time(ev1)
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    status |= capi.device_status(reset=True)
+    tokens_total = cfg.tokens * world * args.steps
+    value = tokens_total / (ms / 1000.0)
+
+    # ---- end to end through the public module API: pinned host x -> device, fwd, bwd, loss.item()
+    e2e = None
+    if not args.no_e2e:
+        mod = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=dev)
+        with torch.no_grad():
+            mod.W_phi.copy_(W_phi)
+            mod.W_V.copy_(W_V)
+            mod.gate_q.copy_(gq)
+            mod.gate_k.copy_(gk)
+        x_host = x.cpu().pin_memory()
+        params = list(mod.parameters())
+
+        def e2e_step():
+            xd = x_host.to(dev, non_blocking=True)
+            o = mod(xd)
+            loss = o.sum(dtype=torch.float32)
+            for q in params:
+                q.grad = None
+            loss.backward()
+            if world > 1:
+                flat = torch.cat([q.grad.float().reshape(-1) for q in params])
+                dist.all_reduce(flat)
+                flat.div_(world)
+                off = 0
+                for q in params:
+                    n = q.numel()
+                    q.grad.copy_(flat[off:off + n].view_as(q.grad))
+                    off += n
+            return loss.item()
+
+        for _ in range(max(2, args.warmup)):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens_total / (float(ems.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+               "api": "morphottention_b200.MorphoAttention(x).sum().backward(); loss.item()"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = _peaks()
+    flops = algorithmic_flops(cfg)
+    kernels = {}
+    total_ms = sum(v[0] for v in prof.values()) or 1.0
+    for name, (kms, cnt) in prof.items():
+        kernels[name] = {"ms_per_launch": kms / cnt, "launches_per_step": cnt / args.steps, "share": kms / total_ms}
+    dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+    roof = None
+    if dom is not None:
+        per_launch_s = prof[dom][0] / prof[dom][1] / 1000.0
+        achieved = flops.get(dom, 0.0) / per_launch_s / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None,
+                "peak_note": f"{peaks['source']} dense bf16 (sustained, kernel timed inside a step); fp16 rate equal",
+                "flops_per_launch": flops.get(dom, 0.0)}
+        if dom in ("attn_bwd", "attn_fwd"):
+            sm_mhz = clocks.get("sm_mhz") or peaks["sm_max_mhz"]
+            mufu_peak = torch.cuda.get_device_properties(dev).multi_processor_count * 16 * sm_mhz * 1e6
+            exps = cfg.pairs()
+            roof["mufu_ex2_per_s"] = exps / per_launch_s
+            roof["mufu_frac"] = exps / per_launch_s / mufu_peak
+            roof["mufu_peak_note"] = f"{torch.cuda.get_device_properties(dev).multi_processor_count} SMs x 16 ex2/clk x {sm_mhz:.0f} MHz"
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic: x~N(0,1) seeded, module default init",
+            "config": _config_dict(cfg, world), "roofline": roof, "e2e": e2e,
+            "gpu_launches": int(sum(v[1] for v in prof.values())), "clocks": clocks, "kernels": kernels,
+            "tensor_tflops_step": cfg.tensor_flops_fwd_bwd() / (ms / args.steps / 1000.0) / 1e12,
+            "step_roofline_frac": (cfg.tensor_flops_fwd_bwd() / (peaks["bf16_tflops_sustained"] * 1e12))
+            / (ms / args.steps / 1000.0),
+            "device_status": status}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * morpho_sm100.h -- C ABI of the B200 (sm_100a) MorphoAttention kernels.
+ *
+ * Plain C: no torch, no CUDA C++ types.  fp16 buffers are passed as void*, and the
+ * CUDA stream as a void* holding a cudaStream_t (NULL = legacy default stream).
+ * Every entry point is asynchronous on that stream and returns a status code; on
+ * failure morpho_sm100_last_error() returns a message for the calling thread.
+ *
+ * Layouts (all row-major, contiguous, on the current CUDA device):
+ *   X, out, grad_out, dX   fp16 [B, N, D]
+ *   W_phi, dW_phi          fp16 [D, H*cube_m]   (used as X @ W_phi)
+ *   W_V, dW_V              fp16 [D, D]          (used as X @ W_V)
+ *   gate_q, gate_k, d_*    fp16 [H, cube_m]
+ *   lse                    fp32 [B*H, N]        log2 domain: max_j s_ij + log2(sum_j 2^(s_ij - max))
+ *
+ * The two compute entry points replace the reference launchers
+ *   attention_forward_kernel_launcher   (packages/morphottention/csrc/cuda/attention/attention.cuh:28-31,
+ *                                         attention.cu:485-522)
+ *   attention_backward_kernel_launcher  (attention.cuh:33-38, attention.cu:524-576)
+ * with the same pointer arguments plus a caller-owned workspace.  Unlike the reference
+ * launchers, cube_m and head_dim are run-time values and `causal` is honoured.
+ */
+#ifndef MORPHO_SM100_H
+#define MORPHO_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MORPHO_API __attribute__((visibility("default")))
+#else
+#define MORPHO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MORPHO_OK 0
+#define MORPHO_ERR_INVALID 1   /* bad shape, null pointer or unsupported (cube_m, head_dim) */
+#define MORPHO_ERR_CUDA 2      /* a CUDA runtime or driver call failed */
+#define MORPHO_ERR_WORKSPACE 3 /* workspace_bytes smaller than the *_workspace_size() answer */
+#define MORPHO_ERR_DEVICE 4    /* current device is not sm_100 */
+#define MORPHO_ERR_TIMEOUT 5   /* a kernel's bounded wait expired (see morpho_sm100_device_status) */
+
+/* Gradient semantics of the backward. */
+#define MORPHO_GRAD_FULL 0      /* true gradient of the forward (default) */
+#define MORPHO_GRAD_REFERENCE 1 /* reference kernel semantics: query-code and query-bias
+                                   terms are not propagated (attention.cu:447-451, :473-482) */
+
+typedef struct morpho_problem {
+    int32_t B;      /* batch */
+    int32_t N;      /* tokens per sequence */
+    int32_t D;      /* model dim, = H * head_dim */
+    int32_t H;      /* heads */
+    int32_t cube_m; /* hypercube width per head: 16, 32 or 64 */
+    float scale;    /* softmax temperature */
+    int32_t causal; /* 0 or 1 */
+    int32_t grad_mode; /* MORPHO_GRAD_FULL or MORPHO_GRAD_REFERENCE (backward only) */
+} morpho_problem_t;
+
+/* Bytes of device workspace the forward / backward need for problem p (0 on invalid p). */
+MORPHO_API size_t morpho_sm100_forward_workspace_size(const morpho_problem_t* p);
+MORPHO_API size_t morpho_sm100_backward_workspace_size(const morpho_problem_t* p);
+
+/* Forward: out = MorphoAttention(X), lse as above.
+ * Replaces attention_forward_kernel_launcher (attention.cu:485-522). */
+MORPHO_API int morpho_sm100_forward(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,
+                         const void* gate_k, const void* W_V, void* out, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Backward of sum(out * grad_out): writes dX, dW_phi, d_gate_q, d_gate_k, dW_V (fp16).
+ * The outputs are overwritten, not accumulated (no zero-fill needed, unlike
+ * attention.cpp:93-98).  If dweights_f32 is non-NULL the weight gradients are written
+ * there in fp32 instead -- layout [dW_phi (D*H*m) | dW_V (D*D) | d_gate_q (H*m) |
+ * d_gate_k (H*m)] -- and dW_phi/dW_V/d_gate_q/d_gate_k may be NULL; a data-parallel
+ * caller all-reduces that bucket and then calls morpho_sm100_finalize_weight_grads.
+ * Replaces attention_backward_kernel_launcher (attention.cu:524-576). */
+MORPHO_API int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const void* X, const void* W_phi,
+                          const void* gate_q, const void* gate_k, const void* W_V, const void* out,
+                          const float* lse, void* dX, void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V,
+                          float* dweights_f32, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Projection only (one GEMM with a fused epilogue): the per-head hypercube codes and
+ * values the attention kernels consume.  Replaces the per-tile project_phi
+ * (packages/morphottention/csrc/cuda/sm120/project.cuh:16-47) and the value projection
+ * (attention.cu:106-111), which the reference recomputes for every query block.
+ * Outputs, with BH = B*H and Npad = N rounded up to a multiple of 128:
+ *   qc, kc  fp16 [BH, N, cube_m]   gate_q*phi, gate_k*phi with phi = sigmoid(X @ W_phi_h)
+ *   v       fp16 [BH, N, D/H]      X @ W_V_h
+ *   qb, cb  fp32 [BH, Npad]        scale*log2(e) * sum_c gate_k q_c, resp. sum_c gate_q k_c
+ *   phi     fp32 [BH, N, cube_m]   optional (may be NULL)
+ * All buffers 16-byte aligned. */
+MORPHO_API int morpho_sm100_project(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,
+                                    const void* gate_k, const void* W_V, void* qc, void* kc, void* v, float* qb,
+                                    float* cb, float* phi, void* stream);
+
+/* Number of fp32 elements of the dweights_f32 bucket for problem p. */
+MORPHO_API size_t morpho_sm100_weight_grad_elems(const morpho_problem_t* p);
+
+/* fp16 weight gradients = alpha * bucket (alpha = 1/world for a mean).  No reference
+ * counterpart: the reference has no data-parallel path. */
+MORPHO_API int morpho_sm100_finalize_weight_grads(const morpho_problem_t* p, const float* dweights_f32, float alpha,
+                                       void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, void* stream);
+
+/* Message of the last failure on the calling thread ("" if none). */
+MORPHO_API const char* morpho_sm100_last_error(void);
+
+/* Device status word of the current device: 0 when every bounded wait of every kernel
+ * finished in time, else a code naming the kernel and wait that expired.  Synchronises
+ * the stream.  reset != 0 clears the word after reading it. */
+MORPHO_API int morpho_sm100_device_status(void* stream, int reset, uint32_t* status_out);
+
+/* Number of kernels the last forward / backward call on this thread launched. */
+MORPHO_API int morpho_sm100_last_launch_count(void);
+
+/* Per-kernel timing for benchmarks (no reference counterpart).  While enabled, every
+ * launch of this library records a CUDA event pair on its stream.  collect() waits for
+ * the recorded events, writes up to max_kernels entries (kernel name into
+ * names[i*name_len], summed milliseconds, launch count), clears the records and returns
+ * the number of entries.  Process-wide switch; records are kept per host thread. */
+MORPHO_API void morpho_sm100_profile_enable(int on);
+MORPHO_API int morpho_sm100_profile_collect(char* names, int name_len, float* total_ms, int* counts,
+                                            int max_kernels);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MORPHO_SM100_H */

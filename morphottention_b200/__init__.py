@@ -1,0 +1,12 @@
+"""B200 (sm_100a) MorphoAttention: drop-in for the reference ``morphottention`` package.
+
+``MorphoAttention``, ``MorphoAttentionFunction`` and ``morpho_attention`` keep the
+reference's signatures and call ``torch.ops.morphottention.forward/backward``, which are
+backed by hand-written tcgen05/TMA kernels behind the C ABI in ``include/morpho_sm100.h``.
+"""
+
+from .autograd import (MorphoAttention, MorphoAttentionFunction, get_grad_mode, grad_mode, morpho_attention,
+                       set_grad_mode)
+
+__all__ = ["MorphoAttention", "MorphoAttentionFunction", "morpho_attention", "set_grad_mode", "get_grad_mode",
+           "grad_mode"]

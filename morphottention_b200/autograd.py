@@ -1,0 +1,136 @@
+"""Autograd wrapper and ``nn.Module`` around the sm_100a MorphoAttention kernels.
+
+Drop-in for the reference's ``torch-ext/morphottention/autograd.py``: the same
+``MorphoAttention`` constructor (``:101-135``), the same ``MorphoAttentionFunction``
+(``:34-88``) and ``morpho_attention`` (``:143-162``), calling the same
+``torch.ops.morphottention.forward/backward`` schemas.  Additions: a fake (meta)
+implementation for ``backward`` and :func:`set_grad_mode`.
+"""
+
+from __future__ import annotations
+
+import contextlib
+
+import torch
+from torch import nn
+
+from ._ops import add_op_namespace_prefix, ops
+
+GRAD_MODES = {"full": 0, "reference": 1}
+
+
+@torch.library.register_fake(add_op_namespace_prefix("forward"))
+def _morpho_forward_fake(X, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool):
+    B, N, _D = X.shape
+    out = torch.empty_like(X)
+    lse = X.new_empty((B * H, N), dtype=torch.float32)
+    return [out, lse]
+
+
+@torch.library.register_fake(add_op_namespace_prefix("backward"))
+def _morpho_backward_fake(grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, H: int, cube_m: int, scale: float,
+                          causal: bool):
+    return [torch.empty_like(X), torch.empty_like(W_phi), torch.empty_like(gate_q), torch.empty_like(gate_k),
+            torch.empty_like(W_V)]
+
+
+def set_grad_mode(mode: str) -> str:
+    """Select the backward's gradient semantics process-wide and return the previous one.
+
+    ``"full"`` (default): the true gradient of the forward.  ``"reference"``: the
+    reference kernel's semantics, which never propagate the query-code and query-bias
+    gradients (reference ``csrc/cuda/attention/attention.cu:447-451``, ``:473-482``), so
+    ``dX``, ``dW_phi`` and the gate gradients lack every term through the query side.
+    """
+    if mode not in GRAD_MODES:
+        raise ValueError(f"grad mode must be one of {sorted(GRAD_MODES)}")
+    prev = int(ops.set_grad_mode(GRAD_MODES[mode]))
+    return {v: k for k, v in GRAD_MODES.items()}[prev]
+
+
+def get_grad_mode() -> str:
+    return {v: k for k, v in GRAD_MODES.items()}[int(ops.get_grad_mode())]
+
+
+@contextlib.contextmanager
+def grad_mode(mode: str):
+    prev = set_grad_mode(mode)
+    try:
+        yield
+    finally:
+        set_grad_mode(prev)
+
+
+class MorphoAttentionFunction(torch.autograd.Function):
+    """Bridges the CUDA attention kernels into autograd."""
+
+    @staticmethod
+    def forward(ctx, x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool):
+        if not x.is_cuda:
+            raise ValueError("MorphoAttention expects a CUDA tensor")
+        x = x.contiguous()
+        out, lse = ops.forward(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
+        ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse)
+        ctx.H = H
+        ctx.cube_m = cube_m
+        ctx.scale = scale
+        ctx.causal = causal
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, W_phi, gate_q, gate_k, W_V, out, lse = ctx.saved_tensors
+        grad_out = grad_out.contiguous()
+        dX, dW_phi, d_gate_q, d_gate_k, dW_V = ops.backward(
+            grad_out, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal)
+        return dX, dW_phi, d_gate_q, d_gate_k, dW_V, None, None, None, None
+
+
+class MorphoAttention(nn.Module):
+    """Morphological hypercube attention.
+
+    :param dim: model dimension ``D`` (must be divisible by ``num_heads``).
+    :param num_heads: number of attention heads ``H``.
+    :param cube_m: hypercube width per head ``m`` (the score-GEMM contraction dim).
+    :param scale: softmax temperature.
+    :param causal: whether to apply causal masking.
+    """
+
+    def __init__(self, dim: int, num_heads: int, cube_m: int, *, scale: float = 1.0, causal: bool = False,
+                 dtype: torch.dtype = torch.float16, device=None) -> None:
+        super().__init__()
+        if dim % num_heads != 0:
+            raise ValueError(f"dim ({dim}) must be divisible by num_heads ({num_heads})")
+        self.dim = dim
+        self.num_heads = num_heads
+        self.cube_m = cube_m
+        self.scale = scale
+        self.causal = causal
+        head_dim_v = dim // num_heads
+        self.W_phi = nn.Parameter(torch.empty(dim, num_heads * cube_m, dtype=dtype, device=device))
+        self.gate_q = nn.Parameter(torch.empty(num_heads, cube_m, dtype=dtype, device=device))
+        self.gate_k = nn.Parameter(torch.empty(num_heads, cube_m, dtype=dtype, device=device))
+        self.W_V = nn.Parameter(torch.empty(dim, num_heads * head_dim_v, dtype=dtype, device=device))
+        self.reset_parameters()
+
+    def reset_parameters(self) -> None:
+        std = self.dim ** -0.5
+        with torch.no_grad():
+            for w in (self.W_phi, self.W_V):
+                w.copy_(torch.empty(w.shape, dtype=torch.float32, device=w.device).normal_(0.0, std))
+            self.gate_q.fill_(1.0)
+            self.gate_k.fill_(1.0)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return MorphoAttentionFunction.apply(
+            x, self.W_phi, self.gate_q, self.gate_k, self.W_V, self.num_heads, self.cube_m, self.scale, self.causal)
+
+
+def morpho_attention(x, W_phi, gate_q, gate_k, W_V, num_heads: int, cube_m: int, *, scale: float = 1.0,
+                     causal: bool = False):
+    """Apply the Morphottention attention mechanism with autograd support.
+
+    :param x: input activations of shape (B, N, D) on a CUDA device.
+    :returns: the attention output, differentiable w.r.t. ``x`` and the parameters.
+    """
+    return MorphoAttentionFunction.apply(x, W_phi, gate_q, gate_k, W_V, num_heads, cube_m, scale, causal)

@@ -1,0 +1,201 @@
+"""ctypes binding of the C ABI in ``include/morpho_sm100.h`` (``libmorpho_sm100.so``).
+
+This is the binding a non-torch host (or a test) uses; the torch ops in ``_C.so`` call
+the same entry points.  Tensors passed in must be contiguous CUDA tensors on the
+current device; the workspace is allocated by the caller (here: torch).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(_PKG_DIR, "libmorpho_sm100.so")
+
+MORPHO_OK = 0
+MORPHO_ERR_INVALID = 1
+MORPHO_ERR_CUDA = 2
+MORPHO_ERR_WORKSPACE = 3
+MORPHO_ERR_DEVICE = 4
+MORPHO_ERR_TIMEOUT = 5
+MORPHO_GRAD_FULL = 0
+MORPHO_GRAD_REFERENCE = 1
+
+EXPORTED = (
+    "morpho_sm100_forward_workspace_size",
+    "morpho_sm100_backward_workspace_size",
+    "morpho_sm100_forward",
+    "morpho_sm100_backward",
+    "morpho_sm100_project",
+    "morpho_sm100_weight_grad_elems",
+    "morpho_sm100_finalize_weight_grads",
+    "morpho_sm100_last_error",
+    "morpho_sm100_device_status",
+    "morpho_sm100_last_launch_count",
+    "morpho_sm100_profile_enable",
+    "morpho_sm100_profile_collect",
+)
+
+
+class MorphoProblem(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("N", ctypes.c_int32), ("D", ctypes.c_int32), ("H", ctypes.c_int32),
+                ("cube_m", ctypes.c_int32), ("scale", ctypes.c_float), ("causal", ctypes.c_int32),
+                ("grad_mode", ctypes.c_int32)]
+
+
+class MorphoError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"morpho_sm100 error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load ``libmorpho_sm100.so`` once and declare the prototypes."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIBRARY_PATH):
+        raise ImportError(f"{LIBRARY_PATH} is missing; build it with `python -m morphottention_b200.build`")
+    L = ctypes.CDLL(LIBRARY_PATH)
+    P = ctypes.POINTER(MorphoProblem)
+    vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+    L.morpho_sm100_forward_workspace_size.argtypes = [P]
+    L.morpho_sm100_forward_workspace_size.restype = sz
+    L.morpho_sm100_backward_workspace_size.argtypes = [P]
+    L.morpho_sm100_backward_workspace_size.restype = sz
+    L.morpho_sm100_weight_grad_elems.argtypes = [P]
+    L.morpho_sm100_weight_grad_elems.restype = sz
+    L.morpho_sm100_forward.argtypes = [P] + [vp] * 7 + [vp, sz, vp]
+    L.morpho_sm100_forward.restype = i32
+    L.morpho_sm100_backward.argtypes = [P] + [vp] * 14 + [vp, sz, vp]
+    L.morpho_sm100_backward.restype = i32
+    L.morpho_sm100_project.argtypes = [P] + [vp] * 11 + [vp]
+    L.morpho_sm100_project.restype = i32
+    L.morpho_sm100_finalize_weight_grads.argtypes = [P, vp, ctypes.c_float, vp, vp, vp, vp, vp]
+    L.morpho_sm100_finalize_weight_grads.restype = i32
+    L.morpho_sm100_last_error.argtypes = []
+    L.morpho_sm100_last_error.restype = ctypes.c_char_p
+    L.morpho_sm100_device_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_uint32)]
+    L.morpho_sm100_device_status.restype = i32
+    L.morpho_sm100_last_launch_count.argtypes = []
+    L.morpho_sm100_last_launch_count.restype = i32
+    L.morpho_sm100_profile_enable.argtypes = [i32]
+    L.morpho_sm100_profile_enable.restype = None
+    L.morpho_sm100_profile_collect.argtypes = [ctypes.c_char_p, i32, ctypes.POINTER(ctypes.c_float),
+                                               ctypes.POINTER(ctypes.c_int), i32]
+    L.morpho_sm100_profile_collect.restype = i32
+    _lib = L
+    return L
+
+
+def problem(B, N, D, H, cube_m, scale=1.0, causal=False, grad_mode=MORPHO_GRAD_FULL) -> MorphoProblem:
+    return MorphoProblem(B, N, D, H, cube_m, float(scale), 1 if causal else 0, int(grad_mode))
+
+
+def last_error() -> str:
+    return lib().morpho_sm100_last_error().decode()
+
+
+def _check(rc: int) -> None:
+    if rc != MORPHO_OK:
+        raise MorphoError(rc, last_error())
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    import torch
+    s = torch.cuda.current_stream() if stream is None else stream
+    return s.cuda_stream
+
+
+def forward(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, out, lse, stream=None) -> None:
+    """Run the forward through the C ABI, with a torch-allocated workspace."""
+    import torch
+    L = lib()
+    ws_bytes = L.morpho_sm100_forward_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        raise MorphoError(MORPHO_ERR_INVALID, last_error())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
+    _check(L.morpho_sm100_forward(ctypes.byref(p), _ptr(X), _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V),
+                                  _ptr(out), _ptr(lse), _ptr(ws), ws_bytes, _stream(stream)))
+
+
+def backward(p: MorphoProblem, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
+             dW_V, dweights_f32=None, stream=None) -> None:
+    """Run the backward through the C ABI, with a torch-allocated workspace."""
+    import torch
+    L = lib()
+    ws_bytes = L.morpho_sm100_backward_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        raise MorphoError(MORPHO_ERR_INVALID, last_error())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
+    _check(L.morpho_sm100_backward(ctypes.byref(p), _ptr(grad_out), _ptr(X), _ptr(W_phi), _ptr(gate_q),
+                                   _ptr(gate_k), _ptr(W_V), _ptr(out), _ptr(lse), _ptr(dX), _ptr(dW_phi),
+                                   _ptr(d_gate_q), _ptr(d_gate_k), _ptr(dW_V), _ptr(dweights_f32), _ptr(ws),
+                                   ws_bytes, _stream(stream)))
+
+
+def project(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, stream=None, with_phi=True) -> dict:
+    """Projection only; returns {qc, kc, v, qb, cb, phi} (layouts of morpho_sm100_project)."""
+    import torch
+    BH, N, m, hd = p.B * p.H, p.N, p.cube_m, p.D // p.H
+    npad = (N + 127) // 128 * 128
+    dev = X.device
+    o = {"qc": torch.empty(BH, N, m, dtype=torch.float16, device=dev),
+         "kc": torch.empty(BH, N, m, dtype=torch.float16, device=dev),
+         "v": torch.empty(BH, N, hd, dtype=torch.float16, device=dev),
+         "qb": torch.empty(BH, npad, dtype=torch.float32, device=dev),
+         "cb": torch.empty(BH, npad, dtype=torch.float32, device=dev),
+         "phi": torch.empty(BH, N, m, dtype=torch.float32, device=dev) if with_phi else None}
+    _check(lib().morpho_sm100_project(ctypes.byref(p), _ptr(X), _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V),
+                                      _ptr(o["qc"]), _ptr(o["kc"]), _ptr(o["v"]), _ptr(o["qb"]), _ptr(o["cb"]),
+                                      _ptr(o["phi"]), _stream(stream)))
+    return o
+
+
+def finalize_weight_grads(p: MorphoProblem, bucket, alpha, dW_phi, d_gate_q, d_gate_k, dW_V, stream=None) -> None:
+    _check(lib().morpho_sm100_finalize_weight_grads(ctypes.byref(p), _ptr(bucket), float(alpha), _ptr(dW_phi),
+                                                    _ptr(d_gate_q), _ptr(d_gate_k), _ptr(dW_V), _stream(stream)))
+
+
+def device_status(reset: bool = True, stream=None) -> int:
+    """Read (and by default clear) the device status word; raises on a timed-out wait."""
+    v = ctypes.c_uint32(0)
+    rc = lib().morpho_sm100_device_status(_stream(stream), 1 if reset else 0, ctypes.byref(v))
+    if rc != MORPHO_OK:
+        raise MorphoError(rc, last_error())
+    return v.value
+
+
+def last_launch_count() -> int:
+    return int(lib().morpho_sm100_last_launch_count())
+
+
+def weight_grad_elems(p: MorphoProblem) -> int:
+    return int(lib().morpho_sm100_weight_grad_elems(ctypes.byref(p)))
+
+
+def profile_enable(on: bool) -> None:
+    """Record a CUDA event pair around every kernel launch of the library."""
+    lib().morpho_sm100_profile_enable(1 if on else 0)
+
+
+def profile_collect(max_kernels: int = 32) -> dict:
+    """{kernel name: (total ms, launches)} of the launches recorded on this thread."""
+    name_len = 64
+    names = ctypes.create_string_buffer(name_len * max_kernels)
+    ms = (ctypes.c_float * max_kernels)()
+    cnt = (ctypes.c_int * max_kernels)()
+    n = lib().morpho_sm100_profile_collect(names, name_len, ms, cnt, max_kernels)
+    out = {}
+    for i in range(n):
+        nm = names.raw[i * name_len:(i + 1) * name_len].split(b"\0", 1)[0].decode()
+        out[nm] = (float(ms[i]), int(cnt[i]))
+    return out

@@ -1,0 +1,520 @@
+// attn_bwd.cu -- MorphoAttention attention backward on sm_100a, KV-stationary.
+//
+// One CTA = one 128-key tile (kv0 .. kv0+127) of one (batch, head); it loops over the
+// query tiles.  TMEM lane j = key row j.  Per query tile i:
+//   S^T  = Kc . Qc_i^T          (M=128 keys, N=128 queries, K=cube_m)   TMEM [0,128)
+//   dP^T = V . dO_i^T           (K=head_dim)                              TMEM [128,256)
+//   softmax warps: P^T = 2^(2*scale*log2e*S - cb'_j - L_i), L = lse + qb' (recompute
+//       from lse as attention.cu:351-368 does), written back as fp16 into the S columns;
+//       dS^T = P^T (dP^T - delta_i) (attention.cu:409-421), fp16 into the dP columns and
+//       into a 128B-swizzled shared buffer; dcb_j += sum_i dS (attention.cu:430-437).
+//   dV += P^T . dO_i            (A = P^T from TMEM)                       TMEM [256, +hd)
+//   dK += dS^T . Qc_i           (A = dS^T from TMEM, B = Qc MN-major)      TMEM [.., +m)
+//   dQ_i = dS . Kc              (A = dS from smem, MN-major)               TMEM [.., +m)
+//   dQ warps: dq[b,h,q,:] += 2*scale * dQ_i  (fp32 atomics into a workspace)
+// Scale factors: dL/dS_raw = 2*scale*dS and dL/dcbias = -scale*sum_i dS (attention.cu:425,
+// :436, :442).  Unlike the reference there are no fp16 global atomics: dV and dK are
+// complete per CTA and stored once; only dq is accumulated, in fp32.
+//
+// Warps (448 threads): 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 softmax for
+// queries [0,64) of the tile, 6..9 softmax for queries [64,128), 10..13 dQ epilogue.
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace morpho {
+namespace {
+
+constexpr int kBwdThreads = 448;
+constexpr int kTile = 128;
+constexpr int kQStages = 2;
+
+template <int MC, int HD>
+struct BwdCfg {
+    static constexpr int KC_BYTES = kTile * MC * 2;  // one code tile (K or Q)
+    static constexpr int V_BYTES = kTile * HD * 2;   // one V or dO tile
+    static constexpr int KC_STRIDE = (KC_BYTES + 1023) / 1024 * 1024;
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_V = OFF_K + KC_STRIDE;
+    static constexpr int OFF_Q = OFF_V + V_BYTES;
+    static constexpr int OFF_DO = OFF_Q + kQStages * KC_STRIDE;
+    static constexpr int OFF_DS = OFF_DO + kQStages * V_BYTES;  // 2 chunks x 128 rows x 128 B
+    static constexpr int DS_BYTES = 2 * kTile * 128;
+    static constexpr int OFF_L = OFF_DS + DS_BYTES;
+    static constexpr int OFF_DELTA = OFF_L + kQStages * kTile * 4;
+    static constexpr int OFF_DCB = OFF_DELTA + kQStages * kTile * 4;
+    static constexpr int OFF_BAR = OFF_DCB + kTile * 4;
+    static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+    static constexpr int STAGE_TX = KC_BYTES + V_BYTES + 2 * kTile * 4;
+    static constexpr uint32_t TM_S = 0;
+    static constexpr uint32_t TM_DP = 128;
+    static constexpr uint32_t TM_DV = 256;
+    static constexpr uint32_t TM_DK = 256 + HD;
+    static constexpr uint32_t TM_DQ = 256 + HD + MC;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t KC_ROW = MC * 2;
+    static constexpr uint32_t V_ROW = (HD > 64 ? 64 : HD) * 2;
+    static_assert(TM_DQ + MC <= TMEM_COLS, "TMEM budget");
+    static_assert(SMEM_BYTES <= 227 * 1024, "smem budget");
+};
+
+struct BwdArgs {
+    int N, Npad, H, D, Hp, Cp, n_qtiles;
+    float c2;     // 2 * scale * log2(e)
+    float two_scale;
+    float neg_scale;
+    const float* cb;  // [BH, Npad] scaled column bias
+    __half* dcat;
+    float* dk;   // [BH, N, MC]
+    float* dcb;  // [BH, Npad]
+    float* dq;   // [BH, N, MC]
+    uint32_t* status;
+};
+
+// A-operand descriptor for a K-major tile of 128 rows whose K extent may span two
+// 64-element chunks (head_dim 128).
+template <uint32_t ROW_BYTES>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks) {
+    constexpr uint32_t sw = swizzle_code_for_row_bytes(ROW_BYTES);
+    constexpr int per_chunk = ROW_BYTES / 32;  // K steps of 16 elements per 64-element chunk
+    const uint32_t addr = base + (ks / per_chunk) * (kTile * ROW_BYTES) + (ks % per_chunk) * 32;
+    return make_sdesc(addr, 16, 8 * ROW_BYTES, sw);
+}
+
+template <int MC, int HD, bool CAUSAL>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmDelta,
+                    const BwdArgs args) {
+    using Cfg = BwdCfg<MC, HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+    // bars: [0,2) q_full, [2,4) q_empty, 4 kv_full, 5 s_full, 6 dp_full, 7 p_full, 8 ds_full,
+    //       9 dq_full, 10 dq_free, 11 ds_smem_free, 12 all_done, 13 drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = warp_id();
+    const int lane = threadIdx.x & 31;
+    const int kt = blockIdx.x;
+    const int bh = blockIdx.y;
+    const int b = bh / args.H;
+    const int h = bh - b * args.H;
+    const int kv0 = kt * kTile;
+    const int i_begin = CAUSAL ? kt : 0;
+    const int n_it = args.n_qtiles - i_begin;
+
+    const uint32_t q_full0 = smem_u32(bars);
+    const uint32_t q_empty0 = smem_u32(bars + 2);
+    const uint32_t kv_full = smem_u32(bars + 4);
+    const uint32_t s_full = smem_u32(bars + 5);
+    const uint32_t dp_full = smem_u32(bars + 6);
+    const uint32_t p_full = smem_u32(bars + 7);
+    const uint32_t ds_full = smem_u32(bars + 8);
+    const uint32_t dq_full = smem_u32(bars + 9);
+    const uint32_t dq_free = smem_u32(bars + 10);
+    const uint32_t ds_smem_free = smem_u32(bars + 11);
+    const uint32_t all_done = smem_u32(bars + 12);
+    const uint32_t drain = smem_u32(bars + 13);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kQStages; ++s) {
+            mbar_init(q_full0 + 8 * s, 1);
+            mbar_init(q_empty0 + 8 * s, 1);
+        }
+        mbar_init(kv_full, 1);
+        mbar_init(s_full, 1);
+        mbar_init(dp_full, 1);
+        mbar_init(p_full, 8);
+        mbar_init(ds_full, 8);
+        mbar_init(dq_full, 1);
+        mbar_init(dq_free, 4);
+        mbar_init(ds_smem_free, 1);
+        mbar_init(all_done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        tma_prefetch_desc(&tmDO);
+        tma_prefetch_desc(&tmL);
+        tma_prefetch_desc(&tmDelta);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
+            const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
+            mbar_arrive_expect_tx(kv_full, Cfg::KC_BYTES + Cfg::V_BYTES);
+            tma_load_3d(sK, &tmK, kv_full, 0, kv0, bh);
+            tma_load_3d(sV, &tmV, kv_full, 0, kv0, bh);
+            if (HD > 64) tma_load_3d(sV + kTile * 128, &tmV, kv_full, 64, kv0, bh);
+            int issued = 0;
+            for (int it = 0; it < n_it; ++it) {
+                const int s = it % kQStages;
+                if (it >= kQStages &&
+                    !mbar_wait(q_empty0 + 8 * s, ((it / kQStages) & 1) ^ 1, args.status, K_ATTN_BWD, 1)) {
+                    *abort_flag = 1u;
+                    break;
+                }
+                if (*abort_flag) break;
+                const int q0 = (i_begin + it) * kTile;
+                const uint32_t fb = q_full0 + 8 * s;
+                const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q + s * Cfg::KC_STRIDE);
+                const uint32_t sDO = smem_u32(smem + Cfg::OFF_DO + s * Cfg::V_BYTES);
+                mbar_arrive_expect_tx(fb, Cfg::STAGE_TX);
+                tma_load_3d(sQ, &tmQ, fb, 0, q0, bh);
+                tma_load_3d(sDO, &tmDO, fb, h * HD, q0, b);
+                if (HD > 64) tma_load_3d(sDO + kTile * 128, &tmDO, fb, h * HD + 64, q0, b);
+                tma_load_2d(smem_u32(smem + Cfg::OFF_L + s * kTile * 4), &tmL, fb, q0, bh);
+                tma_load_2d(smem_u32(smem + Cfg::OFF_DELTA + s * kTile * 4), &tmDelta, fb, q0, bh);
+                ++issued;
+            }
+            mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 2);
+            if (*abort_flag) {
+                for (int i = max(0, issued - kQStages); i < issued; ++i)
+                    mbar_wait(q_full0 + 8 * (i % kQStages), (i / kQStages) & 1, args.status, K_ATTN_BWD, 2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);   // S^T, dP^T
+            constexpr uint32_t id_dv = make_idesc_f16(128, HD, false, true);    // dV
+            constexpr uint32_t id_mc = make_idesc_f16(128, MC, false, true);    // dK (A in TMEM)
+            constexpr uint32_t id_dq = make_idesc_f16(128, MC, true, true);     // dQ (A MN-major smem)
+            constexpr uint32_t kc_sw = swizzle_code_for_row_bytes(Cfg::KC_ROW);
+            constexpr uint32_t v_sw = swizzle_code_for_row_bytes(Cfg::V_ROW);
+            const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
+            const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
+            const uint32_t sDS = smem_u32(smem + Cfg::OFF_DS);
+            bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int s = it % kQStages;
+                const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q + s * Cfg::KC_STRIDE);
+                const uint32_t sDO = smem_u32(smem + Cfg::OFF_DO + s * Cfg::V_BYTES);
+                if (!mbar_wait(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 4) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // S^T = Kc . Qc^T
+#pragma unroll
+                for (int ks = 0; ks < MC / 16; ++ks)
+                    umma_ss(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
+                            id_s, ks > 0 ? 1u : 0u);
+                umma_commit(s_full);
+                // dP^T = V . dO^T
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ++ks)
+                    umma_ss(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
+                            id_s, ks > 0 ? 1u : 0u);
+                umma_commit(dp_full);
+                // dV += P^T . dO  (P^T halves live in S columns [0,32) and [64,96))
+                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kTile / 16; ++ks) {
+                    const uint32_t a = tmem + Cfg::TM_S + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
+                    const uint64_t bd = make_sdesc(sDO + ks * 16 * Cfg::V_ROW, kTile * 128, 8 * Cfg::V_ROW, v_sw);
+                    umma_ts(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
+                }
+                // dK += dS^T . Qc ;  dQ = dS . Kc
+                if (!mbar_wait(ds_full, it & 1, args.status, K_ATTN_BWD, 6) ||
+                    (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kTile / 16; ++ks) {
+                    const uint32_t a = tmem + Cfg::TM_DP + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
+                    const uint64_t bd = make_sdesc(sQ + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
+                    umma_ts(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
+                }
+#pragma unroll
+                for (int ks = 0; ks < kTile / 16; ++ks) {
+                    const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
+                    const uint64_t bd = make_sdesc(sK + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
+                    umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, ks > 0 ? 1u : 0u);
+                }
+                umma_commit(dq_full);
+                umma_commit(ds_smem_free);
+                umma_commit(q_empty0 + 8 * s);
+            }
+            if (ok) {
+                umma_commit(all_done);
+            } else {
+                *abort_flag = 1u;
+                umma_commit(drain);
+                mbar_wait(drain, 0, args.status, K_ATTN_BWD, 8);
+                umma_commit(all_done);  // release the epilogue waits
+            }
+        }
+    } else if (warp < 10) {
+        // ---------------- softmax warps (2..9) ----------------
+        const int wg = (warp - 2) >> 2;   // 0: queries [0,64), 1: queries [64,128)
+        const int quad = warp & 3;
+        const int j = quad * 32 + lane;   // key row within the tile
+        const int kv = kv0 + j;
+        const bool kv_ok = kv < args.N;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const float cbj = kv_ok ? args.cb[static_cast<size_t>(bh) * args.Npad + kv] : 0.f;
+        const float c2 = args.c2;
+        uint8_t* ds_row = smem + Cfg::OFF_DS + wg * (kTile * 128) + j * 128;
+        const int sw = j & 7;
+        float dcb = 0.f;
+        bool ok = true;
+        for (int it = 0; it < n_it; ++it) {
+            const int s = it % kQStages;
+            const int q0 = (i_begin + it) * kTile;
+            const int qc0 = q0 + wg * 64;  // first query of this warp group's half
+            if (!mbar_wait_warp(s_full, it & 1, args.status, K_ATTN_BWD, 9) ||
+                !mbar_wait_warp(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 10)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const float4* Lv = reinterpret_cast<const float4*>(smem + Cfg::OFF_L + s * kTile * 4) + wg * 16;
+            const float4* Dv = reinterpret_cast<const float4*>(smem + Cfg::OFF_DELTA + s * kTile * 4) + wg * 16;
+            const bool need_mask = !kv_ok || (qc0 + 64 > args.N) || (CAUSAL && qc0 < kv0 + kTile);
+            float p[64];
+#pragma unroll
+            for (int c = 0; c < 64; c += 32) {
+                uint32_t rr[32];
+                tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + c, rr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 L = Lv[(c + i) / 4];
+                    p[c + i] = ex2(fmaf(u2f(rr[i]), c2, -cbj) - L.x);
+                    p[c + i + 1] = ex2(fmaf(u2f(rr[i + 1]), c2, -cbj) - L.y);
+                    p[c + i + 2] = ex2(fmaf(u2f(rr[i + 2]), c2, -cbj) - L.z);
+                    p[c + i + 3] = ex2(fmaf(u2f(rr[i + 3]), c2, -cbj) - L.w);
+                }
+            }
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) {
+                    const int qi = qc0 + c;
+                    const bool keep = kv_ok && qi < args.N && (!CAUSAL || kv <= qi);
+                    p[c] = keep ? p[c] : 0.f;
+                }
+            }
+            {
+                uint32_t pk[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) pk[i] = pack_half2(p[2 * i], p[2 * i + 1]);
+                tmem_st16(lane_base + Cfg::TM_S + wg * 64, pk);
+                tmem_st16(lane_base + Cfg::TM_S + wg * 64 + 16, pk + 16);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+
+            if (!mbar_wait_warp(dp_full, it & 1, args.status, K_ATTN_BWD, 11) ||
+                (it > 0 && !mbar_wait_warp(ds_smem_free, (it - 1) & 1, args.status, K_ATTN_BWD, 12))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 64; c += 32) {
+                uint32_t rr[32];
+                tmem_ld32(lane_base + Cfg::TM_DP + wg * 64 + c, rr);
+                tmem_ld_wait();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 dl = Dv[(c + i) / 4];
+                    const float d0 = p[c + i] * (u2f(rr[i]) - dl.x);
+                    const float d1 = p[c + i + 1] * (u2f(rr[i + 1]) - dl.y);
+                    const float d2 = p[c + i + 2] * (u2f(rr[i + 2]) - dl.z);
+                    const float d3 = p[c + i + 3] * (u2f(rr[i + 3]) - dl.w);
+                    dcb += (d0 + d1) + (d2 + d3);
+                    pk[i / 2] = pack_half2(d0, d1);
+                    pk[i / 2 + 1] = pack_half2(d2, d3);
+                }
+                tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + c / 2, pk);
+                // smem copy for the dQ MMA: row j, 16-byte units u = c/8 .. c/8+3, 128B swizzle
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int u = c / 8 + k;
+                    *reinterpret_cast<uint4*>(ds_row + ((u ^ sw) << 4)) =
+                        make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+                }
+            }
+            tmem_st_wait();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+        }
+        // ---- epilogue: dV (group 0), dK + dcb (group 1)
+        float* dcb_x = reinterpret_cast<float*>(smem + Cfg::OFF_DCB);
+        if (wg == 1) dcb_x[j] = dcb;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        const bool fin = ok && mbar_wait_warp(all_done, 0, args.status, K_ATTN_BWD, 13) && !*abort_flag;
+        if (fin) {
+            tc_fence_after();
+            const size_t tok = static_cast<size_t>(b) * args.N + kv;
+            if (wg == 0) {
+                __half* dst = args.dcat + tok * args.Cp + args.Hp + h * HD;
+#pragma unroll
+                for (int c = 0; c < HD; c += 16) {
+                    uint32_t rr[16];
+                    tmem_ld16(lane_base + Cfg::TM_DV + c, rr);
+                    tmem_ld_wait();
+                    if (kv_ok) {
+                        uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+                        d4[0] = make_uint4(pack_half2(u2f(rr[0]), u2f(rr[1])), pack_half2(u2f(rr[2]), u2f(rr[3])),
+                                           pack_half2(u2f(rr[4]), u2f(rr[5])), pack_half2(u2f(rr[6]), u2f(rr[7])));
+                        d4[1] = make_uint4(pack_half2(u2f(rr[8]), u2f(rr[9])), pack_half2(u2f(rr[10]), u2f(rr[11])),
+                                           pack_half2(u2f(rr[12]), u2f(rr[13])),
+                                           pack_half2(u2f(rr[14]), u2f(rr[15])));
+                    }
+                }
+                if (kv_ok) args.dcb[static_cast<size_t>(bh) * args.Npad + kv] = args.neg_scale * (dcb + dcb_x[j]);
+            } else {
+                float* dst = args.dk + (static_cast<size_t>(bh) * args.N + kv) * MC;
+#pragma unroll
+                for (int c = 0; c < MC; c += 16) {
+                    uint32_t rr[16];
+                    tmem_ld16(lane_base + Cfg::TM_DK + c, rr);
+                    tmem_ld_wait();
+                    if (kv_ok) {
+                        float4* d4 = reinterpret_cast<float4*>(dst + c);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            d4[i] = make_float4(u2f(rr[4 * i]) * args.two_scale, u2f(rr[4 * i + 1]) * args.two_scale,
+                                                u2f(rr[4 * i + 2]) * args.two_scale,
+                                                u2f(rr[4 * i + 3]) * args.two_scale);
+                    }
+                }
+            }
+        } else {
+            *abort_flag = 1u;
+        }
+    } else {
+        // ---------------- dQ warps (10..13) ----------------
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // query row within the tile
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        for (int it = 0; it < n_it; ++it) {
+            if (!mbar_wait_warp(dq_full, it & 1, args.status, K_ATTN_BWD, 14) || *abort_flag) break;
+            tc_fence_after();
+            float v[MC];
+#pragma unroll
+            for (int c = 0; c < MC; c += 16) {
+                uint32_t rr[16];
+                tmem_ld16(lane_base + Cfg::TM_DQ + c, rr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[c + i] = u2f(rr[i]) * args.two_scale;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
+            const int q = (i_begin + it) * kTile + r;
+            if (q < args.N) {
+                float4* dst = reinterpret_cast<float4*>(args.dq + (static_cast<size_t>(bh) * args.N + q) * MC);
+#pragma unroll
+                for (int i = 0; i < MC / 4; ++i)
+                    atomicAdd(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+template <int MC, int HD, bool CAUSAL>
+int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io, cudaStream_t stream) {
+    using Cfg = BwdCfg<MC, HD>;
+    const int BH = s.B * s.H;
+    const int Npad = (s.N + kTile - 1) / kTile * kTile;
+    CUtensorMap tQ, tK, tV, tDO, tL, tDl;
+    MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tV, p.v, HD, s.N, BH, HD, static_cast<uint64_t>(s.N) * HD, HD > 64 ? 64 : HD,
+                                kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tDO, io.dO, s.D, s.N, s.B, s.D, static_cast<uint64_t>(s.N) * s.D,
+                                HD > 64 ? 64 : HD, kTile));
+    MORPHO_TRY(make_tmap_2d_f32(&tL, io.L, BH, Npad, Npad, 1, kTile));
+    MORPHO_TRY(make_tmap_2d_f32(&tDl, io.delta, BH, Npad, Npad, 1, kTile));
+    BwdArgs a;
+    a.N = s.N;
+    a.Npad = Npad;
+    a.H = s.H;
+    a.D = s.D;
+    a.Hp = s.Hp();
+    a.Cp = s.Cp();
+    a.n_qtiles = Npad / kTile;
+    a.c2 = 2.0f * s.scale * kLog2e;
+    a.two_scale = 2.0f * s.scale;
+    a.neg_scale = -s.scale;
+    a.cb = p.cb;
+    a.dcat = io.dcat;
+    a.dk = io.dk;
+    a.dcb = io.dcb;
+    a.dq = io.dq;
+    a.status = dev.status;
+    auto kern = attn_bwd_kernel<MC, HD, CAUSAL>;
+    MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    dim3 grid(a.n_qtiles, BH);
+    prof_begin(stream);
+    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, tDO, tL, tDl, a);
+    MORPHO_LAUNCH_CHECK("attn_bwd");
+    return MORPHO_OK;
+}
+
+template <int MC, int HD>
+int run_bwd_c(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io, cudaStream_t st) {
+    return s.causal ? run_bwd<MC, HD, true>(dev, s, p, io, st) : run_bwd<MC, HD, false>(dev, s, p, io, st);
+}
+
+template <int MC>
+int run_bwd_hd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io, cudaStream_t st) {
+    switch (s.hd) {
+        case 32: return run_bwd_c<MC, 32>(dev, s, p, io, st);
+        case 64: return run_bwd_c<MC, 64>(dev, s, p, io, st);
+        case 128: return run_bwd_c<MC, 128>(dev, s, p, io, st);
+        default: return set_error(MORPHO_ERR_INVALID, "head_dim %d not supported (32, 64 or 128)", s.hd);
+    }
+}
+
+}  // namespace
+
+int launch_attn_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io,
+                    cudaStream_t stream) {
+    switch (s.m) {
+        case 16: return run_bwd_hd<16>(dev, s, p, io, stream);
+        case 32: return run_bwd_hd<32>(dev, s, p, io, stream);
+        case 64: return run_bwd_hd<64>(dev, s, p, io, stream);
+        default: return set_error(MORPHO_ERR_INVALID, "cube_m %d not supported (16, 32 or 64)", s.m);
+    }
+}
+
+}  // namespace morpho

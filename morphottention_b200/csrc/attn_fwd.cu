@@ -1,0 +1,416 @@
+// attn_fwd.cu -- MorphoAttention forward on sm_100a over the projected codes.
+//
+// One CTA = one 128-row query tile of one (batch, head).  The reference re-projects
+// K and V from x for every (query block, KV tile) pair (attention.cu:91-111); here the
+// codes and V come from the projection GEMM, and each KV tile is one TMA box.
+//
+// Per KV tile j (128 keys):
+//   MMA warp   : S = Qc . Kc^T   (M=128, N=128, K=cube_m)         -> TMEM cols [0,128)
+//   softmax    : t = 2*scale*log2e * S - cb'_j  (cb' = scale*log2e*cbias, attention.cu:125
+//                with the row-constant query bias moved into lse), masks, row max,
+//                p = 2^(t - m) -> fp16 P                          -> TMEM cols [128,192)
+//   MMA warp   : O += P . V_j    (A = P from TMEM, B = V MN-major) -> TMEM cols [192, ..)
+// The running max is rescaled lazily: O and l are only corrected when the max grows by
+// more than 2^8, so P stays <= 256 (exact in fp16 range) and most tiles skip the O
+// round trip.  The reference keeps O in shared memory and rescales it every tile
+// (attention.cu:166-169).
+//
+// lse (log2 domain, attention.cu:186) = m + log2(l) - qb', qb' = scale*log2e*qbias.
+//
+// Warps (192 threads): 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 = softmax
+// and epilogue (warp w owns TMEM lanes / query rows 32*(w%4) .. +31).
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace morpho {
+namespace {
+
+constexpr int kFwdThreads = 192;
+constexpr int kTile = 128;
+constexpr int kKvStages = 3;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int MC, int HD>
+struct FwdCfg {
+    static constexpr int Q_BYTES = kTile * MC * 2;
+    static constexpr int K_BYTES = kTile * MC * 2;
+    static constexpr int V_BYTES = kTile * HD * 2;
+    static constexpr int CB_BYTES = kTile * 4;
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = (Q_BYTES + 1023) / 1024 * 1024;
+    static constexpr int K_STRIDE = (K_BYTES + 1023) / 1024 * 1024;
+    static constexpr int OFF_V = OFF_K + kKvStages * K_STRIDE;
+    static constexpr int OFF_CB = OFF_V + kKvStages * V_BYTES;
+    static constexpr int OFF_BAR = OFF_CB + kKvStages * CB_BYTES;
+    static constexpr int USED = OFF_BAR + 256;
+    // hd = 128 needs 512 TMEM columns: keep those CTAs alone on their SM.
+    static constexpr int SMEM_BYTES = (HD > 64 && USED + 1024 < 120 * 1024) ? 120 * 1024 : USED + 1024;
+    static constexpr uint32_t TMEM_S = 0;
+    static constexpr uint32_t TMEM_P = 128;
+    static constexpr uint32_t TMEM_O = HD > 64 ? 256 : 192;
+    static constexpr uint32_t TMEM_COLS = HD > 64 ? 512 : 256;
+    static constexpr uint32_t QK_ROW_BYTES = MC * 2;
+    static constexpr uint32_t V_ROW_BYTES = (HD > 64 ? 64 : HD) * 2;
+};
+
+struct FwdArgs {
+    int N, Npad, H, D, n_qtiles;
+    float c2;  // 2 * scale * log2(e)
+    const float* qb;
+    __half* out;
+    float* lse;
+    uint32_t* status;
+};
+
+template <int MC, int HD, bool CAUSAL>
+__global__ void __launch_bounds__(kFwdThreads, 2)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCB,
+                    const FwdArgs args) {
+    using Cfg = FwdCfg<MC, HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+    // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, 2S+1 s_full, 2S+2 p_full, 2S+3 o_done, 2S+4 drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kKvStages + 5);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = warp_id();
+    const int lane = threadIdx.x & 31;
+    const int bh = blockIdx.y;
+    const int qt = CAUSAL ? (args.n_qtiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+    const int q0 = qt * kTile;
+    const int n_kv_all = (args.N + kTile - 1) / kTile;
+    const int n_kv = CAUSAL ? min(n_kv_all, qt + 1) : n_kv_all;
+
+    const uint32_t kv_full0 = smem_u32(bars);
+    const uint32_t kv_empty0 = smem_u32(bars + kKvStages);
+    const uint32_t q_full = smem_u32(bars + 2 * kKvStages);
+    const uint32_t s_full = q_full + 8;
+    const uint32_t p_full = q_full + 16;
+    const uint32_t o_done = q_full + 24;
+    const uint32_t drain = q_full + 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kKvStages; ++s) {
+            mbar_init(kv_full0 + 8 * s, 1);
+            mbar_init(kv_empty0 + 8 * s, 1 + 4);  // MMA commit + 4 softmax warps (cb' read)
+        }
+        mbar_init(q_full, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(o_done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        tma_prefetch_desc(&tmCB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q);
+            mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
+            tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+            int issued = 0;
+            for (int j = 0; j < n_kv; ++j) {
+                const int s = j % kKvStages;
+                if (j >= kKvStages &&
+                    !mbar_wait(kv_empty0 + 8 * s, ((j / kKvStages) & 1) ^ 1, args.status, K_ATTN_FWD, 1)) {
+                    *abort_flag = 1u;
+                    break;
+                }
+                if (*abort_flag) break;
+                const int kv0 = j * kTile;
+                const uint32_t fb = kv_full0 + 8 * s;
+                const uint32_t sK = smem_u32(smem + Cfg::OFF_K + s * Cfg::K_STRIDE);
+                const uint32_t sV = smem_u32(smem + Cfg::OFF_V + s * Cfg::V_BYTES);
+                const uint32_t sC = smem_u32(smem + Cfg::OFF_CB + s * Cfg::CB_BYTES);
+                mbar_arrive_expect_tx(fb, Cfg::K_BYTES + Cfg::V_BYTES + Cfg::CB_BYTES);
+                tma_load_3d(sK, &tmK, fb, 0, kv0, bh);
+                if (HD > 64) {
+                    tma_load_3d(sV, &tmV, fb, 0, kv0, bh);
+                    tma_load_3d(sV + kTile * 128, &tmV, fb, 64, kv0, bh);
+                } else {
+                    tma_load_3d(sV, &tmV, fb, 0, kv0, bh);
+                }
+                tma_load_2d(sC, &tmCB, fb, kv0, bh);
+                ++issued;
+            }
+            // Bounded drain of loads still in flight (abort path, and the Q tile).
+            mbar_wait(q_full, 0, args.status, K_ATTN_FWD, 2);
+            if (*abort_flag) {
+                for (int i = max(0, issued - kKvStages); i < issued; ++i)
+                    mbar_wait(kv_full0 + 8 * (i % kKvStages), (i / kKvStages) & 1, args.status, K_ATTN_FWD, 2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
+            constexpr uint32_t idesc_pv = make_idesc_f16(128, HD, false, true);
+            constexpr uint32_t qk_sw = swizzle_code_for_row_bytes(Cfg::QK_ROW_BYTES);
+            constexpr uint32_t qk_sbo = 8 * Cfg::QK_ROW_BYTES;
+            constexpr uint32_t v_sw = swizzle_code_for_row_bytes(Cfg::V_ROW_BYTES);
+            constexpr uint32_t v_sbo = 8 * Cfg::V_ROW_BYTES;
+            const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q);
+            bool ok = mbar_wait(q_full, 0, args.status, K_ATTN_FWD, 3);
+            auto issue_s = [&](int j) {
+                const uint32_t sK = smem_u32(smem + Cfg::OFF_K + (j % kKvStages) * Cfg::K_STRIDE);
+#pragma unroll
+                for (int ks = 0; ks < MC / 16; ++ks) {
+                    const uint64_t ad = make_sdesc(sQ + ks * 32, 16, qk_sbo, qk_sw);
+                    const uint64_t bd = make_sdesc(sK + ks * 32, 16, qk_sbo, qk_sw);
+                    umma_ss(tmem + Cfg::TMEM_S, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+                }
+                umma_commit(s_full);
+            };
+            if (ok && n_kv > 0) {
+                ok = mbar_wait(kv_full0, 0, args.status, K_ATTN_FWD, 4);
+                if (ok) {
+                    tc_fence_after();
+                    issue_s(0);
+                }
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+                const int s = j % kKvStages;
+                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (j + 1 < n_kv) {
+                    const int s1 = (j + 1) % kKvStages;
+                    if (!mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+                const uint32_t sV = smem_u32(smem + Cfg::OFF_V + s * Cfg::V_BYTES);
+#pragma unroll
+                for (int ks = 0; ks < kTile / 16; ++ks) {
+                    const uint64_t bd = make_sdesc(sV + ks * 16 * Cfg::V_ROW_BYTES, kTile * 128, v_sbo, v_sw);
+                    umma_ts(tmem + Cfg::TMEM_O, tmem + Cfg::TMEM_P + ks * 8, bd, idesc_pv,
+                            (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(o_done);
+                umma_commit(kv_empty0 + 8 * s);
+            }
+            if (!ok) {
+                *abort_flag = 1u;
+                umma_commit(drain);
+                mbar_wait(drain, 0, args.status, K_ATTN_FWD, 7);
+            }
+        }
+    } else {
+        // ---------------- softmax + epilogue (warps 2..5) ----------------
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;  // query row within the tile
+        const int q = q0 + r;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const float c2 = args.c2;
+        float m_ref = -INFINITY;
+        float l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            const int s = j % kKvStages;
+            const int kv0 = j * kTile;
+            if (!mbar_wait_warp(s_full, j & 1, args.status, K_ATTN_FWD, 8) ||
+                !mbar_wait_warp(kv_full0 + 8 * s, (j / kKvStages) & 1, args.status, K_ATTN_FWD, 9)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float t[kTile];
+#pragma unroll
+            for (int c = 0; c < kTile; c += 32) {
+                uint32_t rr[32];
+                tmem_ld32(lane_base + Cfg::TMEM_S + c, rr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[c + i] = u2f(rr[i]);
+            }
+            const float4* cbv = reinterpret_cast<const float4*>(smem + Cfg::OFF_CB + s * Cfg::CB_BYTES);
+#pragma unroll
+            for (int c = 0; c < kTile; c += 4) {
+                const float4 cb = cbv[c / 4];
+                t[c] = fmaf(t[c], c2, -cb.x);
+                t[c + 1] = fmaf(t[c + 1], c2, -cb.y);
+                t[c + 2] = fmaf(t[c + 2], c2, -cb.z);
+                t[c + 3] = fmaf(t[c + 3], c2, -cb.w);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(kv_empty0 + 8 * s);  // cb' of this stage consumed
+            const bool need_mask = (kv0 + kTile > args.N) || (CAUSAL && j == qt);
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < kTile; ++c) {
+                    const int kv = kv0 + c;
+                    const bool drop = kv >= args.N || (CAUSAL && kv > q);
+                    t[c] = drop ? -INFINITY : t[c];
+                }
+            }
+            float mt = t[0];
+#pragma unroll
+            for (int c = 1; c < kTile; ++c) mt = fmaxf(mt, t[c]);
+            // Lazy rescale: move the reference max only when the row max grew by > 2^8.
+            const bool grow = mt > m_ref + kRescaleThreshold;
+            const float m_new = grow ? mt : m_ref;
+            const float alpha = grow ? ex2(m_ref - m_new) : 1.0f;  // 0 when m_ref = -inf
+            if (j > 0) {
+                // P and O are both used by the previous P.V MMA: wait for it.
+                if (!mbar_wait_warp(o_done, (j - 1) & 1, args.status, K_ATTN_FWD, 10)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+                    for (int c = 0; c < HD; c += 16) {
+                        uint32_t rr[16];
+                        tmem_ld16(lane_base + Cfg::TMEM_O + c, rr);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(u2f(rr[i]) * alpha);
+                        tmem_st16(lane_base + Cfg::TMEM_O + c, rr);
+                    }
+                    tmem_st_wait();
+                }
+            }
+            l *= alpha;
+            m_ref = m_new;
+            // m_ref is finite here: every row has at least one unmasked key.
+            float lsum = 0.f;
+#pragma unroll
+            for (int c = 0; c < kTile; c += 32) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = ex2(t[c + 2 * i] - m_ref);
+                    const float p1 = ex2(t[c + 2 * i + 1] - m_ref);
+                    lsum += p0 + p1;
+                    pk[i] = pack_half2(p0, p1);
+                }
+                tmem_st16(lane_base + Cfg::TMEM_P + c / 2, pk);
+            }
+            l += lsum;
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        // ---- epilogue: O / l -> out, lse
+        if (ok && n_kv > 0 && mbar_wait_warp(o_done, (n_kv - 1) & 1, args.status, K_ATTN_FWD, 11)) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            const int b = bh / args.H;
+            const int h = bh - b * args.H;
+            __half* orow = args.out + (static_cast<size_t>(b) * args.N + q) * args.D + h * HD;
+#pragma unroll
+            for (int c = 0; c < HD; c += 16) {
+                uint32_t rr[16];
+                tmem_ld16(lane_base + Cfg::TMEM_O + c, rr);
+                tmem_ld_wait();
+                if (q < args.N) {
+                    uint4* dst = reinterpret_cast<uint4*>(orow + c);
+                    dst[0] = make_uint4(pack_half2(u2f(rr[0]) * inv, u2f(rr[1]) * inv),
+                                        pack_half2(u2f(rr[2]) * inv, u2f(rr[3]) * inv),
+                                        pack_half2(u2f(rr[4]) * inv, u2f(rr[5]) * inv),
+                                        pack_half2(u2f(rr[6]) * inv, u2f(rr[7]) * inv));
+                    dst[1] = make_uint4(pack_half2(u2f(rr[8]) * inv, u2f(rr[9]) * inv),
+                                        pack_half2(u2f(rr[10]) * inv, u2f(rr[11]) * inv),
+                                        pack_half2(u2f(rr[12]) * inv, u2f(rr[13]) * inv),
+                                        pack_half2(u2f(rr[14]) * inv, u2f(rr[15]) * inv));
+                }
+            }
+            if (q < args.N) {
+                const float qb = args.qb[static_cast<size_t>(bh) * args.Npad + q];
+                args.lse[static_cast<size_t>(bh) * args.N + q] = l > 0.f ? m_ref + log2f(l) - qb : -3.402823466e38f;
+            }
+        } else if (!ok) {
+            *abort_flag = 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+template <int MC, int HD, bool CAUSAL>
+int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse, cudaStream_t stream) {
+    using Cfg = FwdCfg<MC, HD>;
+    const int BH = s.B * s.H;
+    const int Npad = (s.N + kTile - 1) / kTile * kTile;
+    CUtensorMap tQ, tK, tV, tC;
+    MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tV, p.v, HD, s.N, BH, HD, static_cast<uint64_t>(s.N) * HD, HD > 64 ? 64 : HD,
+                                kTile));
+    MORPHO_TRY(make_tmap_2d_f32(&tC, p.cb, BH, Npad, Npad, 1, kTile));
+    FwdArgs a;
+    a.N = s.N;
+    a.Npad = Npad;
+    a.H = s.H;
+    a.D = s.D;
+    a.n_qtiles = Npad / kTile;
+    a.c2 = 2.0f * s.scale * kLog2e;
+    a.qb = p.qb;
+    a.out = out;
+    a.lse = lse;
+    a.status = dev.status;
+    auto kern = attn_fwd_kernel<MC, HD, CAUSAL>;
+    MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    dim3 grid(a.n_qtiles, BH);
+    prof_begin(stream);
+    kern<<<grid, kFwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, tC, a);
+    MORPHO_LAUNCH_CHECK("attn_fwd");
+    return MORPHO_OK;
+}
+
+template <int MC, int HD>
+int run_fwd_c(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse, cudaStream_t st) {
+    return s.causal ? run_fwd<MC, HD, true>(dev, s, p, out, lse, st) : run_fwd<MC, HD, false>(dev, s, p, out, lse, st);
+}
+
+template <int MC>
+int run_fwd_hd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse, cudaStream_t st) {
+    switch (s.hd) {
+        case 32: return run_fwd_c<MC, 32>(dev, s, p, out, lse, st);
+        case 64: return run_fwd_c<MC, 64>(dev, s, p, out, lse, st);
+        case 128: return run_fwd_c<MC, 128>(dev, s, p, out, lse, st);
+        default: return set_error(MORPHO_ERR_INVALID, "head_dim %d not supported (32, 64 or 128)", s.hd);
+    }
+}
+
+}  // namespace
+
+int launch_attn_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse,
+                    cudaStream_t stream) {
+    switch (s.m) {
+        case 16: return run_fwd_hd<16>(dev, s, p, out, lse, stream);
+        case 32: return run_fwd_hd<32>(dev, s, p, out, lse, stream);
+        case 64: return run_fwd_hd<64>(dev, s, p, out, lse, stream);
+        default: return set_error(MORPHO_ERR_INVALID, "cube_m %d not supported (16, 32 or 64)", s.m);
+    }
+}
+
+}  // namespace morpho

@@ -1,0 +1,329 @@
+// capi.cu -- the extern "C" entry points of libmorpho_sm100.so (declared in
+// include/morpho_sm100.h): argument validation, workspace planning and the kernel
+// sequence of the forward and backward passes.
+//
+// Forward  (2 launches): projection GEMM+epilogue -> attention forward.
+// Backward (7 launches + 1 memset): projection recompute (+phi) -> delta/L ->
+//   zero dq -> attention backward -> dZ + gate partials -> dX GEMM -> dW GEMM (split-K)
+//   -> deterministic reduction of dW / gate partials.
+#include <string.h>
+
+#include "kernels.h"
+
+using namespace morpho;
+
+namespace {
+
+constexpr int kTile = 128;
+
+int validate(const morpho_problem_t* p, Shape* s) {
+    if (p == nullptr) return set_error(MORPHO_ERR_INVALID, "problem is NULL");
+    if (p->B <= 0 || p->N <= 0 || p->D <= 0 || p->H <= 0)
+        return set_error(MORPHO_ERR_INVALID, "Invalid dimensions: B=%d N=%d D=%d H=%d", p->B, p->N, p->D, p->H);
+    if (p->D % p->H != 0) return set_error(MORPHO_ERR_INVALID, "D must be divisible by H (D=%d, H=%d)", p->D, p->H);
+    const int hd = p->D / p->H;
+    if (hd != 32 && hd != 64 && hd != 128)
+        return set_error(MORPHO_ERR_INVALID, "head_dim D/H = %d not supported (32, 64 or 128)", hd);
+    if (p->cube_m != 16 && p->cube_m != 32 && p->cube_m != 64)
+        return set_error(MORPHO_ERR_INVALID, "cube_m = %d not supported (16, 32 or 64)", p->cube_m);
+    if (p->grad_mode != MORPHO_GRAD_FULL && p->grad_mode != MORPHO_GRAD_REFERENCE)
+        return set_error(MORPHO_ERR_INVALID, "grad_mode %d unknown", p->grad_mode);
+    const long long T = static_cast<long long>(p->B) * p->N;
+    if (T > (1LL << 30) || static_cast<long long>(p->B) * p->H * p->N * 128 > (1LL << 40))
+        return set_error(MORPHO_ERR_INVALID, "problem too large: B*N = %lld", T);
+    if (static_cast<long long>(p->B) * p->H > 65535)
+        return set_error(MORPHO_ERR_INVALID, "B*H = %lld exceeds the grid limit 65535",
+                         static_cast<long long>(p->B) * p->H);
+    s->B = p->B;
+    s->N = p->N;
+    s->D = p->D;
+    s->H = p->H;
+    s->m = p->cube_m;
+    s->hd = hd;
+    s->scale = p->scale;
+    s->causal = p->causal != 0;
+    s->grad_mode = p->grad_mode;
+    return MORPHO_OK;
+}
+
+int check_ptr(const void* ptr, const char* name) {
+    if (ptr == nullptr) return set_error(MORPHO_ERR_INVALID, "%s is NULL", name);
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0)
+        return set_error(MORPHO_ERR_INVALID, "%s is not 16-byte aligned", name);
+    return MORPHO_OK;
+}
+
+// Bump allocator over the caller's workspace (256-byte aligned sub-buffers).
+struct Carve {
+    uint8_t* base;
+    size_t off = 0;
+    explicit Carve(void* b) : base(static_cast<uint8_t*>(b)) {}
+    template <class T>
+    T* take(size_t count) {
+        off = (off + 255) / 256 * 256;
+        T* ptr = base ? reinterpret_cast<T*>(base + off) : nullptr;
+        off += count * sizeof(T);
+        return ptr;
+    }
+};
+
+struct FwdPlan {
+    ProjOut proj;
+};
+
+void plan_proj(Carve& c, const Shape& s, ProjOut* o) {
+    const size_t BH = static_cast<size_t>(s.B) * s.H;
+    const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
+    o->qc = c.take<__half>(BH * s.N * s.m);
+    o->kc = c.take<__half>(BH * s.N * s.m);
+    o->v = c.take<__half>(BH * s.N * s.hd);
+    o->qb = c.take<float>(BH * Npad);
+    o->cb = c.take<float>(BH * Npad);
+}
+
+struct BwdPlan {
+    ProjOut proj;
+    float* delta;
+    float* L;
+    float* dq;
+    float* dk;
+    float* dcb;
+    __half* dcat;
+    float* dw_part;
+    float* gate_part;
+    int splits;
+    int gate_blocks;
+};
+
+void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
+    const size_t BH = static_cast<size_t>(s.B) * s.H;
+    const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
+    plan_proj(c, s, &b->proj);
+    b->proj.phi = c.take<float>(BH * s.N * s.m);
+    b->delta = c.take<float>(BH * Npad);
+    b->L = c.take<float>(BH * Npad);
+    b->dq = c.take<float>(BH * s.N * s.m);
+    b->dk = c.take<float>(BH * s.N * s.m);
+    b->dcb = c.take<float>(BH * Npad);
+    b->dcat = c.take<__half>(static_cast<size_t>(s.tokens()) * s.Cp());
+    DeviceInfo d;
+    d.sms = sms;
+    b->splits = dw_splits(d, s);
+    b->dw_part = c.take<float>(static_cast<size_t>(b->splits) * s.D * s.Cp());
+    b->gate_blocks = dz_gate_blocks(s);
+    b->gate_part = c.take<float>(static_cast<size_t>(b->gate_blocks) * 2 * s.Hm());
+}
+
+// The workspace size depends on the SM count (split-K factor); query the current
+// device when there is one, else assume a full B200.
+int sms_for_sizing() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) ==
+                                                  cudaSuccess && sms > 0)
+        return sms;
+    cudaGetLastError();
+    return 148;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t morpho_sm100_forward_workspace_size(const morpho_problem_t* p) {
+    Shape s;
+    if (validate(p, &s) != MORPHO_OK) return 0;
+    Carve c(nullptr);
+    FwdPlan f;
+    plan_proj(c, s, &f.proj);
+    return c.off + 256;
+}
+
+size_t morpho_sm100_backward_workspace_size(const morpho_problem_t* p) {
+    Shape s;
+    if (validate(p, &s) != MORPHO_OK) return 0;
+    Carve c(nullptr);
+    BwdPlan b;
+    plan_bwd(c, s, sms_for_sizing(), &b);
+    return c.off + 256;
+}
+
+size_t morpho_sm100_weight_grad_elems(const morpho_problem_t* p) {
+    Shape s;
+    if (validate(p, &s) != MORPHO_OK) return 0;
+    return static_cast<size_t>(s.D) * (s.Hm() + s.D) + 2u * static_cast<size_t>(s.Hm());
+}
+
+int morpho_sm100_forward(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,
+                         const void* gate_k, const void* W_V, void* out, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(X, "X"));
+    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
+    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
+    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
+    MORPHO_TRY(check_ptr(W_V, "W_V"));
+    MORPHO_TRY(check_ptr(out, "out"));
+    MORPHO_TRY(check_ptr(lse, "lse"));
+    MORPHO_TRY(check_ptr(workspace, "workspace"));
+    const size_t need = morpho_sm100_forward_workspace_size(p);
+    if (workspace_bytes < need)
+        return set_error(MORPHO_ERR_WORKSPACE, "forward workspace too small: %zu < %zu bytes", workspace_bytes, need);
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    Carve c(workspace);
+    FwdPlan f;
+    plan_proj(c, s, &f.proj);
+    const __half* x = static_cast<const __half*>(X);
+    MORPHO_TRY(launch_proj(dev, s, x, static_cast<const __half*>(W_phi), static_cast<const __half*>(W_V),
+                           static_cast<const __half*>(gate_q), static_cast<const __half*>(gate_k), f.proj, st));
+    MORPHO_TRY(launch_attn_fwd(dev, s, f.proj, static_cast<__half*>(out), lse, st));
+    return MORPHO_OK;
+}
+
+int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const void* X, const void* W_phi,
+                          const void* gate_q, const void* gate_k, const void* W_V, const void* out,
+                          const float* lse, void* dX, void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V,
+                          float* dweights_f32, void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(grad_out, "grad_out"));
+    MORPHO_TRY(check_ptr(X, "X"));
+    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
+    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
+    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
+    MORPHO_TRY(check_ptr(W_V, "W_V"));
+    MORPHO_TRY(check_ptr(out, "out"));
+    MORPHO_TRY(check_ptr(lse, "lse"));
+    MORPHO_TRY(check_ptr(dX, "dX"));
+    if (dweights_f32 != nullptr) {
+        MORPHO_TRY(check_ptr(dweights_f32, "dweights_f32"));
+    } else {
+        MORPHO_TRY(check_ptr(dW_phi, "dW_phi"));
+        MORPHO_TRY(check_ptr(d_gate_q, "d_gate_q"));
+        MORPHO_TRY(check_ptr(d_gate_k, "d_gate_k"));
+        MORPHO_TRY(check_ptr(dW_V, "dW_V"));
+    }
+    MORPHO_TRY(check_ptr(workspace, "workspace"));
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    Carve need_c(nullptr);
+    BwdPlan need_plan;
+    plan_bwd(need_c, s, dev.sms, &need_plan);
+    if (workspace_bytes < need_c.off + 256)
+        return set_error(MORPHO_ERR_WORKSPACE, "backward workspace too small: %zu < %zu bytes", workspace_bytes,
+                         need_c.off + 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    Carve c(workspace);
+    BwdPlan b;
+    plan_bwd(c, s, dev.sms, &b);
+    const __half* x = static_cast<const __half*>(X);
+    const __half* wphi = static_cast<const __half*>(W_phi);
+    const __half* wv = static_cast<const __half*>(W_V);
+    const __half* gq = static_cast<const __half*>(gate_q);
+    const __half* gk = static_cast<const __half*>(gate_k);
+    MORPHO_TRY(launch_proj(dev, s, x, wphi, wv, gq, gk, b.proj, st));
+    MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse, b.proj.qb,
+                            b.delta, b.L, st));
+    MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
+    AttnBwdIO io;
+    io.dO = static_cast<const __half*>(grad_out);
+    io.L = b.L;
+    io.delta = b.delta;
+    io.dcat = b.dcat;
+    io.dk = b.dk;
+    io.dcb = b.dcb;
+    io.dq = b.dq;
+    MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
+    MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
+    MORPHO_TRY(launch_dx(dev, s, b.dcat, wphi, wv, static_cast<__half*>(dX), st));
+    MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
+    MORPHO_TRY(launch_reduce_weights(s, b.dw_part, b.splits, b.gate_part, b.gate_blocks, dweights_f32,
+                                     static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
+                                     static_cast<__half*>(d_gate_q), static_cast<__half*>(d_gate_k), st));
+    return MORPHO_OK;
+}
+
+int morpho_sm100_project(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,
+                         const void* gate_k, const void* W_V, void* qc, void* kc, void* v, float* qb, float* cb,
+                         float* phi, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(X, "X"));
+    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
+    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
+    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
+    MORPHO_TRY(check_ptr(W_V, "W_V"));
+    MORPHO_TRY(check_ptr(qc, "qc"));
+    MORPHO_TRY(check_ptr(kc, "kc"));
+    MORPHO_TRY(check_ptr(v, "v"));
+    MORPHO_TRY(check_ptr(qb, "qb"));
+    MORPHO_TRY(check_ptr(cb, "cb"));
+    if (phi != nullptr) MORPHO_TRY(check_ptr(phi, "phi"));
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    ProjOut o;
+    o.qc = static_cast<__half*>(qc);
+    o.kc = static_cast<__half*>(kc);
+    o.v = static_cast<__half*>(v);
+    o.qb = qb;
+    o.cb = cb;
+    o.phi = phi;
+    return launch_proj(dev, s, static_cast<const __half*>(X), static_cast<const __half*>(W_phi),
+                       static_cast<const __half*>(W_V), static_cast<const __half*>(gate_q),
+                       static_cast<const __half*>(gate_k), o, static_cast<cudaStream_t>(stream));
+}
+
+int morpho_sm100_finalize_weight_grads(const morpho_problem_t* p, const float* dweights_f32, float alpha,
+                                       void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(dweights_f32, "dweights_f32"));
+    MORPHO_TRY(check_ptr(dW_phi, "dW_phi"));
+    MORPHO_TRY(check_ptr(d_gate_q, "d_gate_q"));
+    MORPHO_TRY(check_ptr(d_gate_k, "d_gate_k"));
+    MORPHO_TRY(check_ptr(dW_V, "dW_V"));
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    return launch_finalize_weights(s, dweights_f32, alpha, static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
+                                   static_cast<__half*>(d_gate_q), static_cast<__half*>(d_gate_k),
+                                   static_cast<cudaStream_t>(stream));
+}
+
+const char* morpho_sm100_last_error(void) { return last_error(); }
+
+int morpho_sm100_last_launch_count(void) { return launch_count(); }
+
+void morpho_sm100_profile_enable(int on) { prof_enable(on != 0); }
+
+int morpho_sm100_profile_collect(char* names, int name_len, float* total_ms, int* counts, int max_kernels) {
+    if (names == nullptr || total_ms == nullptr || counts == nullptr || name_len <= 0 || max_kernels <= 0) return 0;
+    return prof_collect(names, name_len, total_ms, counts, max_kernels);
+}
+
+int morpho_sm100_device_status(void* stream, int reset, uint32_t* status_out) {
+    clear_error();
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t v = 0;
+    MORPHO_CUDA_TRY(cudaMemcpyAsync(&v, dev.status, sizeof(v), cudaMemcpyDeviceToHost, st));
+    MORPHO_CUDA_TRY(cudaStreamSynchronize(st));
+    if (reset) MORPHO_CUDA_TRY(cudaMemsetAsync(dev.status, 0, sizeof(uint32_t), st));
+    if (status_out) *status_out = v;
+    if (v != 0)
+        return set_error(MORPHO_ERR_TIMEOUT, "device status 0x%08x: kernel %u wait site %u timed out", v, v & 0xFFu,
+                         (v >> 8) & 0xFFu);
+    return MORPHO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,480 @@
+// gemm.cu -- one warp-specialised tcgen05 GEMM kernel (128 x BN tiles, K blocks of 64,
+// TMA-fed multi-stage shared-memory ring, fp32 accumulator in TMEM) with three
+// epilogues:
+//   * EpiProj  : X @ [W_phi | W_V]   -> sigmoid, gating, bias sums, fp16 codes and V
+//                (replaces the per-tile re-projection of project.cuh:16-47 and
+//                attention.cu:102-111, which the reference repeats for every Q block)
+//   * EpiHalf  : dcat @ [W_phi | W_V]^T -> dX fp16  (replaces the fp16 atomics of
+//                attention.cu:393-402, :462-468 and project.cuh:99)
+//   * EpiF32   : X^T @ dcat -> fp32 split-K partials of [dW_phi | dW_V]  (replaces the
+//                fp16 atomics of attention.cu:382-390 and project.cuh:89-96)
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, one output row per
+// thread).  Operands are fp16 with 128-byte swizzle; A and B may each be K-major or
+// MN-major, which the instruction descriptor's transpose bits express, so no operand
+// is ever transposed in memory.
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace morpho {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kGemmThreads = 192;
+
+enum BMode : int { B_SINGLE = 0, B_SPLIT_N = 1, B_SPLIT_K = 2 };
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int STAGES = BN == 128 ? 3 : 4;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024;  // barriers + 1 KB alignment slack
+    static constexpr uint32_t TMEM_COLS = BN;
+};
+
+struct GemmArgs {
+    int M, N;
+    int k_blocks;      // ceil(K / BK)
+    int kb_per_split;  // K blocks handled by one blockIdx.z
+    int b_split;       // B_SPLIT_N: first column of B1; B_SPLIT_K: first K index of B1
+    uint32_t* status;
+};
+
+// ---- epilogues ----------------------------------------------------------------------
+
+template <int NC>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
+    static_assert(NC % 16 == 0, "columns in multiples of 16");
+#pragma unroll
+    for (int c = 0; c < NC; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) out[c + i] = u2f(r[i]);
+    }
+}
+
+struct ProjParams {
+    int T, N, H, hd, Hp, D;
+    float c;  // scale * log2(e)
+    const __half* gq;
+    const __half* gk;
+    ProjOut o;
+};
+
+// Projection epilogue for cube width MC.  Tile columns [n0, n0+BN) of the padded
+// output space [0, Hp) -> heads' z values, [Hp, Hp + D) -> V columns.
+template <int MC>
+struct EpiProj {
+    using Params = ProjParams;
+    template <int BN>
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/) {
+        const bool live = row < p.T;
+        const int b = live ? row / p.N : 0;
+        const int n = live ? row - b * p.N : 0;
+        if (n0 < p.Hp) {
+#pragma unroll 1
+            for (int hc = 0; hc < BN / MC; ++hc) {
+                const int h = n0 / MC + hc;
+                if (h >= p.H) break;  // pad columns of the last phi tile
+                float zr[MC];
+                tmem_load_cols<MC>(tacc + hc * MC, zr);
+                const __half2* gq2 = reinterpret_cast<const __half2*>(p.gq + h * MC);
+                const __half2* gk2 = reinterpret_cast<const __half2*>(p.gk + h * MC);
+                float qb = 0.f, cb = 0.f;
+                uint32_t qpk[MC / 2], kpk[MC / 2];
+#pragma unroll
+                for (int c = 0; c < MC; c += 2) {
+                    const float2 gq = __half22float2(gq2[c / 2]);
+                    const float2 gk = __half22float2(gk2[c / 2]);
+                    const float p0 = 1.0f / (1.0f + __expf(-zr[c]));
+                    const float p1 = 1.0f / (1.0f + __expf(-zr[c + 1]));
+                    zr[c] = p0;
+                    zr[c + 1] = p1;
+                    const float q0 = gq.x * p0, q1 = gq.y * p1;
+                    const float k0 = gk.x * p0, k1 = gk.y * p1;
+                    qb = fmaf(gk.x, q0, fmaf(gk.y, q1, qb));
+                    cb = fmaf(gq.x, k0, fmaf(gq.y, k1, cb));
+                    qpk[c / 2] = pack_half2(q0, q1);
+                    kpk[c / 2] = pack_half2(k0, k1);
+                }
+                if (live) {
+                    const size_t base = static_cast<size_t>(b * p.H + h) * p.N + n;
+                    uint4* dq = reinterpret_cast<uint4*>(p.o.qc + base * MC);
+                    uint4* dk = reinterpret_cast<uint4*>(p.o.kc + base * MC);
+#pragma unroll
+                    for (int i = 0; i < MC / 8; ++i) {
+                        dq[i] = make_uint4(qpk[4 * i], qpk[4 * i + 1], qpk[4 * i + 2], qpk[4 * i + 3]);
+                        dk[i] = make_uint4(kpk[4 * i], kpk[4 * i + 1], kpk[4 * i + 2], kpk[4 * i + 3]);
+                    }
+                    p.o.qb[base] = qb * p.c;
+                    p.o.cb[base] = cb * p.c;
+                    if (p.o.phi != nullptr) {
+                        float4* dp = reinterpret_cast<float4*>(p.o.phi + base * MC);
+#pragma unroll
+                        for (int i = 0; i < MC / 4; ++i)
+                            dp[i] = make_float4(zr[4 * i], zr[4 * i + 1], zr[4 * i + 2], zr[4 * i + 3]);
+                    }
+                }
+            }
+        } else {
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc) {
+                const int g = n0 - p.Hp + cc * 32;  // V column
+                if (g >= p.D) break;
+                uint32_t r[32];
+                tmem_ld32(tacc + cc * 32, r);
+                tmem_ld_wait();
+                if (live) {
+                    const int h = g / p.hd;
+                    const int e = g - h * p.hd;
+                    uint4* dv = reinterpret_cast<uint4*>(p.o.v + (static_cast<size_t>(b * p.H + h) * p.N + n) * p.hd + e);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        dv[i] = make_uint4(pack_half2(u2f(r[8 * i]), u2f(r[8 * i + 1])),
+                                           pack_half2(u2f(r[8 * i + 2]), u2f(r[8 * i + 3])),
+                                           pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
+                                           pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
+                }
+            }
+        }
+    }
+};
+
+struct HalfParams {
+    int M, N, ld;
+    __half* out;
+};
+
+struct EpiHalf {
+    using Params = HalfParams;
+    template <int BN>
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/) {
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+            const int col = n0 + cc * 32;
+            if (col >= p.N) break;
+            uint32_t r[32];
+            tmem_ld32(tacc + cc * 32, r);
+            tmem_ld_wait();
+            if (row < p.M) {
+                uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ld + col);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    dst[i] = make_uint4(pack_half2(u2f(r[8 * i]), u2f(r[8 * i + 1])),
+                                        pack_half2(u2f(r[8 * i + 2]), u2f(r[8 * i + 3])),
+                                        pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
+                                        pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
+            }
+        }
+    }
+};
+
+struct F32Params {
+    int M, N, ld;
+    float* out;  // [splits, M, ld]
+};
+
+struct EpiF32 {
+    using Params = F32Params;
+    template <int BN>
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int z) {
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+            const int col = n0 + cc * 32;
+            if (col >= p.N) break;
+            uint32_t r[32];
+            tmem_ld32(tacc + cc * 32, r);
+            tmem_ld_wait();
+            if (row < p.M) {
+                float4* dst = reinterpret_cast<float4*>(p.out + (static_cast<size_t>(z) * p.M + row) * p.ld + col);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_float4(u2f(r[4 * i]), u2f(r[4 * i + 1]), u2f(r[4 * i + 2]), u2f(r[4 * i + 3]));
+            }
+        }
+    }
+};
+
+// ---- the kernel ---------------------------------------------------------------------
+
+// A is M x K, B is K x N (logical).  A_MN: A stored [K, M] (M contiguous), else [M, K].
+// B_MN: B stored [K, N] (N contiguous), else [N, K].
+template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 2)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                const __grid_constant__ CUtensorMap tmB1, const GemmArgs args, const typename Epi::Params ep) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFFSET);
+    // bars[0..S) full, bars[S..2S) empty, bars[2S] accumulator ready, bars[2S+1] drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int warp = warp_id();
+    const int lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+    const int kb0 = blockIdx.z * args.kb_per_split;
+    const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+    const int nkb = kb1 - kb0;
+
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + STAGES);
+    const uint32_t acc_bar = smem_u32(bars + 2 * STAGES);
+    const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 1);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(acc_bar, 1);
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB0);
+        if (BMODE != B_SINGLE) tma_prefetch_desc(&tmB1);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES) {
+                    if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) & 1) ^ 1, args.status, K_GEMM, 1)) {
+                        *abort_flag = 1u;
+                        break;
+                    }
+                }
+                if (*abort_flag) break;
+                const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                const uint32_t sB = sA + Cfg::A_BYTES;
+                const uint32_t fb = full0 + 8 * s;
+                const int k0 = (kb0 + i) * BK;
+                mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                if (A_MN) {
+                    tma_load_2d(sA, &tmA, fb, m0, k0);
+                    tma_load_2d(sA + 64 * 128, &tmA, fb, m0 + 64, k0);
+                } else {
+                    tma_load_2d(sA, &tmA, fb, k0, m0);
+                }
+                const CUtensorMap* tb = &tmB0;
+                int bn = n0, bk = k0;
+                if (BMODE == B_SPLIT_N && n0 >= args.b_split) {
+                    tb = &tmB1;
+                    bn = n0 - args.b_split;
+                }
+                if (BMODE == B_SPLIT_K && k0 >= args.b_split) {
+                    tb = &tmB1;
+                    bk = k0 - args.b_split;
+                }
+                if (B_MN) {
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c) tma_load_2d(sB + c * 64 * 128, tb, fb, bn + 64 * c, bk);
+                } else {
+                    tma_load_2d(sB, tb, fb, bk, bn);
+                }
+                ++issued;
+            }
+            // Drain: wait (bounded) for this thread's loads still in flight.
+            if (*abort_flag) {
+                for (int i = max(0, issued - STAGES); i < issued; ++i)
+                    mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, args.status, K_GEMM, 2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN);
+            bool ok = true;
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, args.status, K_GEMM, 3) || *abort_flag) {
+                    *abort_flag = 1u;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                const uint32_t sB = sA + Cfg::A_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < BK / 16; ++ks) {
+                    const uint64_t ad = A_MN ? make_sdesc(sA + ks * 2048, 64 * 128, 1024, SW_128)
+                                             : make_sdesc(sA + ks * 32, 16, 1024, SW_128);
+                    const uint64_t bd = B_MN ? make_sdesc(sB + ks * 2048, 64 * 128, 1024, SW_128)
+                                             : make_sdesc(sB + ks * 32, 16, 1024, SW_128);
+                    umma_ss(tmem, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(empty0 + 8 * s);
+            }
+            if (ok) {
+                umma_commit(acc_bar);
+            } else {
+                umma_commit(drain_bar);
+                mbar_wait(drain_bar, 0, args.status, K_GEMM, 4);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quad = warp & 3;
+        const int row = m0 + quad * 32 + lane;
+        const bool ok = mbar_wait_warp(acc_bar, 0, args.status, K_GEMM, 5);
+        if (ok && nkb > 0) {
+            tc_fence_after();
+            Epi::template run<BN>(ep, tmem + (static_cast<uint32_t>(quad * 32) << 16), row, n0, blockIdx.z);
+        } else if (!ok) {
+            *abort_flag = 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
+int run_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1, const GemmArgs& args,
+             const typename Epi::Params& ep, int splits, cudaStream_t stream, const char* name) {
+    auto kern = gemm_kernel<BN, A_MN, B_MN, BMODE, Epi>;
+    constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+    MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dim3 grid((args.M + BM - 1) / BM, (args.N + BN - 1) / BN, splits);
+    prof_begin(stream);
+    kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB0, tmB1, args, ep);
+    MORPHO_LAUNCH_CHECK(name);
+    return MORPHO_OK;
+}
+
+}  // namespace
+
+// ---- launchers ----------------------------------------------------------------------
+
+int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __half* W_phi, const __half* W_V,
+                const __half* gate_q, const __half* gate_k, const ProjOut& o, cudaStream_t stream) {
+    const long long T = s.tokens();
+    const int Hp = s.Hp();
+    const int BN = (Hp % 128 == 0 && s.D % 128 == 0) ? 128 : 64;
+    CUtensorMap tA, tB0, tB1;
+    MORPHO_TRY(make_tmap_2d_f16(&tA, X, T, s.D, s.D, BM, BK));
+    MORPHO_TRY(make_tmap_2d_f16(&tB0, W_phi, s.D, s.Hm(), s.Hm(), BK, 64));
+    MORPHO_TRY(make_tmap_2d_f16(&tB1, W_V, s.D, s.D, s.D, BK, 64));
+    GemmArgs a;
+    a.M = static_cast<int>(T);
+    a.N = s.Cp();
+    a.k_blocks = (s.D + BK - 1) / BK;
+    a.kb_per_split = a.k_blocks;
+    a.b_split = Hp;
+    a.status = dev.status;
+    ProjParams p;
+    p.T = static_cast<int>(T);
+    p.N = s.N;
+    p.H = s.H;
+    p.hd = s.hd;
+    p.Hp = Hp;
+    p.D = s.D;
+    p.c = s.scale * kLog2e;
+    p.gq = gate_q;
+    p.gk = gate_k;
+    p.o = o;
+    switch (s.m) {
+        case 16:
+            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, stream, "proj")
+                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+        case 32:
+            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, stream, "proj")
+                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+        case 64:
+            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, stream, "proj")
+                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+        default:
+            return set_error(MORPHO_ERR_INVALID, "cube_m %d not supported (16, 32 or 64)", s.m);
+    }
+}
+
+int launch_dx(const DeviceInfo& dev, const Shape& s, const __half* dcat, const __half* W_phi, const __half* W_V,
+              __half* dX, cudaStream_t stream) {
+    const long long T = s.tokens();
+    constexpr int BN = 128;
+    CUtensorMap tA, tB0, tB1;
+    MORPHO_TRY(make_tmap_2d_f16(&tA, dcat, T, s.Cp(), s.Cp(), BM, BK));
+    // B^T = [W_phi | W_V] viewed as K-major [D rows, K cols]
+    MORPHO_TRY(make_tmap_2d_f16(&tB0, W_phi, s.D, s.Hm(), s.Hm(), BN, BK));
+    MORPHO_TRY(make_tmap_2d_f16(&tB1, W_V, s.D, s.D, s.D, BN, BK));
+    GemmArgs a;
+    a.M = static_cast<int>(T);
+    a.N = s.D;
+    a.k_blocks = (s.Cp() + BK - 1) / BK;
+    a.kb_per_split = a.k_blocks;
+    a.b_split = s.Hp();
+    a.status = dev.status;
+    HalfParams p;
+    p.M = a.M;
+    p.N = s.D;
+    p.ld = s.D;
+    p.out = dX;
+    return run_gemm<BN, false, false, B_SPLIT_K, EpiHalf>(tA, tB0, tB1, a, p, 1, stream, "dx_gemm");
+}
+
+int dw_splits(const DeviceInfo& dev, const Shape& s) {
+    const int tiles = ((s.D + BM - 1) / BM) * ((s.Cp() + 127) / 128);
+    const int kblocks = static_cast<int>((s.tokens() + BK - 1) / BK);
+    // Aim for about two co-resident CTAs per SM, at least 8 K blocks per split.
+    int splits = (2 * dev.sms + tiles - 1) / tiles;
+    splits = max(1, min(splits, kblocks / 8));
+    return splits;
+}
+
+int launch_dw(const DeviceInfo& dev, const Shape& s, const __half* X, const __half* dcat, float* part, int splits,
+              cudaStream_t stream) {
+    const long long T = s.tokens();
+    constexpr int BN = 128;
+    CUtensorMap tA, tB0;
+    // A = X^T: stored [T (K), D (M)] -> MN-major boxes of 64 x 64.
+    MORPHO_TRY(make_tmap_2d_f16(&tA, X, T, s.D, s.D, BK, 64));
+    // B = dcat: stored [T (K), Cp (N)] -> MN-major boxes of 64 x 64.
+    MORPHO_TRY(make_tmap_2d_f16(&tB0, dcat, T, s.Cp(), s.Cp(), BK, 64));
+    GemmArgs a;
+    a.M = s.D;
+    a.N = s.Cp();
+    a.k_blocks = static_cast<int>((T + BK - 1) / BK);
+    a.kb_per_split = (a.k_blocks + splits - 1) / splits;
+    a.b_split = 0;
+    a.status = dev.status;
+    const int real_splits = (a.k_blocks + a.kb_per_split - 1) / a.kb_per_split;
+    if (real_splits != splits)
+        return set_error(MORPHO_ERR_INVALID, "internal: dW split count %d does not cover %d K blocks", splits,
+                         a.k_blocks);
+    F32Params p;
+    p.M = s.D;
+    p.N = s.Cp();
+    p.ld = s.Cp();
+    p.out = part;
+    return run_gemm<BN, true, true, B_SINGLE, EpiF32>(tA, tB0, tB0, a, p, splits, stream, "dw_gemm");
+}
+
+}  // namespace morpho

@@ -1,0 +1,93 @@
+// kernels.h -- internal launcher interface between the C ABI (capi.cu) and the sm_100a
+// kernels (gemm.cu, attn_fwd.cu, attn_bwd.cu, pointwise.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "host_common.h"
+
+namespace morpho {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Shape {
+    int B, N, D, H, m, hd;
+    float scale;
+    bool causal;
+    int grad_mode;
+    long long tokens() const { return static_cast<long long>(B) * N; }
+    int Hm() const { return H * m; }
+    // dZ columns are padded to a multiple of 64 so that no 64-wide K block of the dX
+    // GEMM straddles W_phi and W_V; the pad columns of dcat hold zeros.
+    int Hp() const { return (H * m + 63) / 64 * 64; }
+    int Cp() const { return Hp() + D; }  // width of dcat = [dZ | 0 | dV]
+};
+
+// Per-(b, h) intermediates written by the projection GEMM epilogue.  Head-major so an
+// attention tile is one contiguous box: codes [B*H, N, m], V [B*H, N, hd], biases
+// [B*H, N] pre-multiplied by scale*log2(e).
+struct ProjOut {
+    __half* qc = nullptr;   // gate_q * phi
+    __half* kc = nullptr;   // gate_k * phi
+    __half* v = nullptr;    // x @ W_V head slice
+    float* qb = nullptr;    // scale*log2e * sum_c gate_k q_c
+    float* cb = nullptr;    // scale*log2e * sum_c gate_q k_c
+    float* phi = nullptr;   // optional fp32 phi [B*H, N, m] (backward recompute)
+};
+
+// X [T, D] @ [W_phi | W_V] with the sigmoid / gating / bias epilogue.
+int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __half* W_phi, const __half* W_V,
+                const __half* gate_q, const __half* gate_k, const ProjOut& o, cudaStream_t stream);
+
+// dX [T, D] = dcat [T, Cp] @ [W_phi | 0 | W_V]^T.
+int launch_dx(const DeviceInfo& dev, const Shape& s, const __half* dcat, const __half* W_phi, const __half* W_V,
+              __half* dX, cudaStream_t stream);
+
+// part[z] [D, Cp] = X^T [D, T] @ dcat [T, Cp] over the z-th slice of tokens.
+int launch_dw(const DeviceInfo& dev, const Shape& s, const __half* X, const __half* dcat, float* part, int splits,
+              cudaStream_t stream);
+int dw_splits(const DeviceInfo& dev, const Shape& s);
+
+// Attention forward over the projected codes: out fp16 [B, N, D], lse fp32 [B*H, N].
+int launch_attn_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse,
+                    cudaStream_t stream);
+
+// Attention backward (KV-stationary).  Inputs: codes/V/biases, dO, L = lse + qb
+// (log2 domain, without the query bias), delta = rowsum(dO * O).  Outputs: dV into
+// dcat[:, Hp + h*hd + e] (fp16), dk (fp32 [B*H, N, m], = 2*scale * dS^T q),
+// dcb (fp32 [B*H, N], = -scale * sum_i dS_ij), and dq (fp32 [B*H, N, m], accumulated
+// with atomics, = 2*scale * dS k; must be zeroed first).
+struct AttnBwdIO {
+    const __half* dO;
+    const float* L;
+    const float* delta;
+    __half* dcat;
+    float* dk;
+    float* dcb;
+    float* dq;
+};
+int launch_attn_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io,
+                    cudaStream_t stream);
+
+// delta[bh, n] = sum_e dO * O over the head slice; L[bh, n] = lse + qb.
+int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* delta,
+                 float* L, cudaStream_t stream);
+
+// dZ = dL/dphi * phi (1 - phi) into dcat[:, h*m + c] and per-block gate partials.
+int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,
+              const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part, int gate_blocks,
+              cudaStream_t stream);
+int dz_gate_blocks(const Shape& s);
+
+// Sum the dW split partials and gate partials: either into an fp32 bucket (layout of
+// morpho_sm100_backward's dweights_f32) or straight to fp16 outputs.
+int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, const float* gate_part, int gate_blocks,
+                          float* bucket, __half* dW_phi, __half* dW_V, __half* d_gate_q, __half* d_gate_k,
+                          cudaStream_t stream);
+
+// fp16 outputs = alpha * bucket.
+int launch_finalize_weights(const Shape& s, const float* bucket, float alpha, __half* dW_phi, __half* dW_V,
+                            __half* d_gate_q, __half* d_gate_k, cudaStream_t stream);
+
+}  // namespace morpho

@@ -1,0 +1,270 @@
+// pointwise.cu -- the memory-bound helpers of the backward:
+//   * delta_kernel  : delta = rowsum(dO * O) per head (attention.cu:294-311) and
+//                     L = lse + qb' (the query bias the forward folded into lse)
+//   * dz_kernel     : dZ = dL/dphi * phi (1 - phi) for the shared q/k projection and the
+//                     per-block gate-gradient partials (project.cuh:70-85, applied to
+//                     both the key and -- in full mode -- the query side)
+//   * reduce kernel : deterministic sums of the dW split-K partials and gate partials
+//                     (the reference uses fp16 atomics: project.cuh:80-96,
+//                     attention.cu:386-390)
+//   * finalize      : fp32 weight-gradient bucket -> fp16 outputs (data parallel)
+// All accesses are 16-byte vectors along the contiguous dimension.
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace morpho {
+namespace {
+
+constexpr int kTile = 128;
+
+inline int npad_of(int N) { return (N + kTile - 1) / kTile * kTile; }
+
+// One warp per token row of D = H * hd elements.  Lanes hold 8 consecutive elements;
+// a head spans hd/8 lanes.
+__global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ dO, const __half* __restrict__ O,
+                                                    const float* __restrict__ lse, const float* __restrict__ qb,
+                                                    float* __restrict__ delta, float* __restrict__ L, int T, int N,
+                                                    int Npad, int D, int H, int hd) {
+    const int lane = threadIdx.x & 31;
+    const int warps_total = gridDim.x * (blockDim.x >> 5);
+    const int lanes_per_head = hd / 8;
+    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps_total) {
+        const int b = t / N;
+        const int n = t - b * N;
+        const uint4* d4 = reinterpret_cast<const uint4*>(dO + static_cast<size_t>(t) * D);
+        const uint4* o4 = reinterpret_cast<const uint4*>(O + static_cast<size_t>(t) * D);
+        for (int base = 0; base < D / 8; base += 32) {
+            const int chunk = base + lane;  // 8-element chunk index within the row
+            float acc = 0.f;
+            if (chunk < D / 8) {
+                const uint4 a = d4[chunk];
+                const uint4 c = o4[chunk];
+                const __half2* ah = reinterpret_cast<const __half2*>(&a);
+                const __half2* ch = reinterpret_cast<const __half2*>(&c);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 x = __half22float2(ah[i]);
+                    const float2 y = __half22float2(ch[i]);
+                    acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+                }
+            }
+            for (int off = 1; off < lanes_per_head; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (chunk < D / 8 && (chunk % lanes_per_head) == 0) {
+                const int h = chunk / lanes_per_head;
+                const size_t bh = static_cast<size_t>(b) * H + h;
+                delta[bh * Npad + n] = acc;
+                L[bh * Npad + n] = lse[bh * N + n] + qb[bh * Npad + n];
+            }
+        }
+    }
+    // zero the padded tail [N, Npad) of every (b, h) row
+    const int pad = Npad - N;
+    if (pad > 0) {
+        const int total = (T / N) * H * pad;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+            const int bh = i / pad;
+            const int n = N + (i - bh * pad);
+            delta[static_cast<size_t>(bh) * Npad + n] = 0.f;
+            L[static_cast<size_t>(bh) * Npad + n] = 0.f;
+        }
+    }
+}
+
+// Block = 256 threads, a contiguous run of tokens.  Thread k owns columns
+// 4k .. 4k+3 (+1024 per loop) of the padded dZ space [0, Hp).  Writes dcat[:, 0:Hp) and
+// the block's gate partials gate_part[blk][0|1][H*m].
+template <bool FULL>
+__global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, const float* __restrict__ dq,
+                                                 const float* __restrict__ dk, const float* __restrict__ dcb,
+                                                 const __half* __restrict__ gq, const __half* __restrict__ gk,
+                                                 __half* __restrict__ dcat, float* __restrict__ gate_part, int T,
+                                                 int N, int Npad, int H, int m, int Hp, int Cp, int tokens_per_block) {
+    const int Hm = H * m;
+    const int t0 = blockIdx.x * tokens_per_block;
+    const int t1 = min(T, t0 + tokens_per_block);
+    for (int col0 = threadIdx.x * 4; col0 < Hp; col0 += blockDim.x * 4) {
+        const bool live = col0 < Hm;  // m is a multiple of 16, so 4 columns never straddle heads
+        const int h = live ? col0 / m : 0;
+        const int c = col0 - h * m;
+        float g_q[4] = {0.f, 0.f, 0.f, 0.f}, g_k[4] = {0.f, 0.f, 0.f, 0.f};
+        float aq[4] = {0.f, 0.f, 0.f, 0.f}, ak[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                g_q[i] = __half2float(gq[col0 + i]);
+                g_k[i] = __half2float(gk[col0 + i]);
+            }
+        }
+        for (int t = t0; t < t1; ++t) {
+            uint2 out = make_uint2(0u, 0u);
+            if (live) {
+                const int b = t / N;
+                const int n = t - b * N;
+                const size_t row = static_cast<size_t>(b) * H + h;
+                const size_t off = (row * N + n) * m + c;
+                const float4 f = *reinterpret_cast<const float4*>(phi + off);
+                const float4 kk = *reinterpret_cast<const float4*>(dk + off);
+                const float db = dcb[row * Npad + n];
+                float4 qq = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (FULL) qq = *reinterpret_cast<const float4*>(dq + off);
+                const float fv[4] = {f.x, f.y, f.z, f.w};
+                const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
+                const float qv[4] = {qq.x, qq.y, qq.z, qq.w};
+                float dz[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    // dL/dphi = dq*gq + dk*gk + dcb*gq*gk  (query-bias term is identically 0)
+                    float dphi = fmaf(kv[i], g_k[i], db * g_q[i] * g_k[i]);
+                    if (FULL) dphi = fmaf(qv[i], g_q[i], dphi);
+                    dz[i] = dphi * fv[i] * (1.0f - fv[i]);
+                    // d gate_q += dq*phi + dcb*gk*phi ; d gate_k += dk*phi + dcb*gq*phi
+                    float gqi = db * g_k[i] * fv[i];
+                    if (FULL) gqi = fmaf(qv[i], fv[i], gqi);
+                    aq[i] += gqi;
+                    ak[i] += fmaf(kv[i], fv[i], db * g_q[i] * fv[i]);
+                }
+                out = make_uint2(pack_half2(dz[0], dz[1]), pack_half2(dz[2], dz[3]));
+            }
+            *reinterpret_cast<uint2*>(dcat + static_cast<size_t>(t) * Cp + col0) = out;
+        }
+        if (live) {
+            float* pq = gate_part + (static_cast<size_t>(blockIdx.x) * 2) * Hm + col0;
+            float* pk = pq + Hm;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                pq[i] = aq[i];
+                pk[i] = ak[i];
+            }
+        }
+    }
+}
+
+// Sum split partials.  Output index space: [dW_phi D*Hm | dW_V D*D | gq Hm | gk Hm].
+__global__ void __launch_bounds__(256) reduce_weights_kernel(const float* __restrict__ part, int splits,
+                                                             const float* __restrict__ gate_part, int gate_blocks,
+                                                             float* __restrict__ bucket, __half* __restrict__ dW_phi,
+                                                             __half* __restrict__ dW_V, __half* __restrict__ dgq,
+                                                             __half* __restrict__ dgk, int D, int Hm, int Hp, int Cp) {
+    const long long n_phi = static_cast<long long>(D) * Hm;
+    const long long n_v = static_cast<long long>(D) * D;
+    const long long total = n_phi + n_v + 2LL * Hm;
+    const long long plane = static_cast<long long>(D) * Cp;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float acc = 0.f;
+        if (i < n_phi + n_v) {
+            long long src;
+            if (i < n_phi) {
+                const long long d = i / Hm;
+                src = d * Cp + (i - d * Hm);
+            } else {
+                const long long k = i - n_phi;
+                const long long d = k / D;
+                src = d * Cp + Hp + (k - d * D);
+            }
+            for (int z = 0; z < splits; ++z) acc += part[z * plane + src];
+        } else {
+            const long long k = i - n_phi - n_v;
+            const int g = k < Hm ? 0 : 1;
+            const long long col = k - g * Hm;
+            for (int blk = 0; blk < gate_blocks; ++blk) acc += gate_part[(static_cast<long long>(blk) * 2 + g) * Hm + col];
+        }
+        if (bucket != nullptr) {
+            bucket[i] = acc;
+        } else if (i < n_phi) {
+            dW_phi[i] = __float2half_rn(acc);
+        } else if (i < n_phi + n_v) {
+            dW_V[i - n_phi] = __float2half_rn(acc);
+        } else if (i < n_phi + n_v + Hm) {
+            dgq[i - n_phi - n_v] = __float2half_rn(acc);
+        } else {
+            dgk[i - n_phi - n_v - Hm] = __float2half_rn(acc);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ bucket, float alpha,
+                                                       __half* __restrict__ dW_phi, __half* __restrict__ dW_V,
+                                                       __half* __restrict__ dgq, __half* __restrict__ dgk, int D,
+                                                       int Hm) {
+    const long long n_phi = static_cast<long long>(D) * Hm;
+    const long long n_v = static_cast<long long>(D) * D;
+    const long long total = n_phi + n_v + 2LL * Hm;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const __half v = __float2half_rn(alpha * bucket[i]);
+        if (i < n_phi)
+            dW_phi[i] = v;
+        else if (i < n_phi + n_v)
+            dW_V[i - n_phi] = v;
+        else if (i < n_phi + n_v + Hm)
+            dgq[i - n_phi - n_v] = v;
+        else
+            dgk[i - n_phi - n_v - Hm] = v;
+    }
+}
+
+int grid_for(long long work, int per_block, int cap) {
+    long long g = (work + per_block - 1) / per_block;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return static_cast<int>(g);
+}
+
+}  // namespace
+
+int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* delta,
+                 float* L, cudaStream_t stream) {
+    const int T = static_cast<int>(s.tokens());
+    const int grid = grid_for(T, 8, 148 * 16);
+    prof_begin(stream);
+    delta_kernel<<<grid, 256, 0, stream>>>(dO, O, lse, qb, delta, L, T, s.N, npad_of(s.N), s.D, s.H, s.hd);
+    MORPHO_LAUNCH_CHECK("delta");
+    return MORPHO_OK;
+}
+
+int dz_gate_blocks(const Shape& s) {
+    const long long T = s.tokens();
+    // ~64 tokens per block keeps the partial buffer small and the grid several waves deep
+    return grid_for(T, 64, 4096);
+}
+
+int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,
+              const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part, int gate_blocks,
+              cudaStream_t stream) {
+    const int T = static_cast<int>(s.tokens());
+    const int tpb = (T + gate_blocks - 1) / gate_blocks;
+    prof_begin(stream);
+    if (s.grad_mode == MORPHO_GRAD_FULL)
+        dz_kernel<true><<<gate_blocks, 256, 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+                                                         npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
+    else
+        dz_kernel<false><<<gate_blocks, 256, 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+                                                          npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
+    MORPHO_LAUNCH_CHECK("dz");
+    return MORPHO_OK;
+}
+
+int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, const float* gate_part, int gate_blocks,
+                          float* bucket, __half* dW_phi, __half* dW_V, __half* d_gate_q, __half* d_gate_k,
+                          cudaStream_t stream) {
+    const long long total = static_cast<long long>(s.D) * (s.Hm() + s.D) + 2LL * s.Hm();
+    prof_begin(stream);
+    reduce_weights_kernel<<<grid_for(total, 256, 148 * 8), 256, 0, stream>>>(
+        dw_part, splits, gate_part, gate_blocks, bucket, dW_phi, dW_V, d_gate_q, d_gate_k, s.D, s.Hm(), s.Hp(),
+        s.Cp());
+    MORPHO_LAUNCH_CHECK("reduce_weights");
+    return MORPHO_OK;
+}
+
+int launch_finalize_weights(const Shape& s, const float* bucket, float alpha, __half* dW_phi, __half* dW_V,
+                            __half* d_gate_q, __half* d_gate_k, cudaStream_t stream) {
+    const long long total = static_cast<long long>(s.D) * (s.Hm() + s.D) + 2LL * s.Hm();
+    prof_begin(stream);
+    finalize_kernel<<<grid_for(total, 256, 148 * 8), 256, 0, stream>>>(bucket, alpha, dW_phi, dW_V, d_gate_q,
+                                                                       d_gate_k, s.D, s.Hm());
+    MORPHO_LAUNCH_CHECK("finalize_weights");
+    return MORPHO_OK;
+}
+
+}  // namespace morpho

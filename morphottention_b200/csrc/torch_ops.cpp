@@ -1,0 +1,146 @@
+// torch_ops.cpp -- registers the reference's torch op schemas (namespace morphottention)
+// on the CUDA dispatch key and forwards them to the C ABI of libmorpho_sm100.so.
+//
+// Schemas, argument checks and their messages follow the reference host layer
+// (packages/morphottention/csrc/cuda/binder.cpp:6-15, csrc/cuda/dispatch.cpp:3-15,
+// csrc/cuda/attention/attention.cpp:9-118).  Differences: a device guard (the reference
+// has none), workspace from the torch caching allocator on the current stream, no
+// zero-fill of the gradient outputs (the kernels overwrite them), and two extra ops:
+// set_grad_mode / get_grad_mode select full gradients (default) or the reference
+// kernel's gradient semantics.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <atomic>
+#include <vector>
+
+#include "../../include/morpho_sm100.h"
+
+namespace {
+
+std::atomic<int> g_grad_mode{MORPHO_GRAD_FULL};
+
+void check(const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.scalar_type() == at::kHalf, name, " must be float16");
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double scale, bool causal) {
+    morpho_problem_t p;
+    p.B = static_cast<int32_t>(X.size(0));
+    p.N = static_cast<int32_t>(X.size(1));
+    p.D = static_cast<int32_t>(X.size(2));
+    p.H = static_cast<int32_t>(H);
+    p.cube_m = static_cast<int32_t>(cube_m);
+    p.scale = static_cast<float>(scale);
+    p.causal = causal ? 1 : 0;
+    p.grad_mode = g_grad_mode.load();
+    return p;
+}
+
+void check_shapes(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q, const at::Tensor& gate_k,
+                  const at::Tensor& W_V, int64_t H, int64_t cube_m) {
+    TORCH_CHECK(X.dim() == 3, "X must be [B, N, D]");
+    const int64_t D = X.size(2);
+    TORCH_CHECK(H > 0 && D % H == 0, "D must be divisible by H");
+    const int64_t head_dim_v = D / H;
+    TORCH_CHECK(W_phi.dim() == 2 && W_phi.size(0) == D && W_phi.size(1) == H * cube_m, "W_phi must be [D, H*cube_m]");
+    TORCH_CHECK(W_V.dim() == 2 && W_V.size(0) == D && W_V.size(1) == H * head_dim_v, "W_V must be [D, H*head_dim_v]");
+    TORCH_CHECK(gate_q.dim() == 2 && gate_q.size(0) == H && gate_q.size(1) == cube_m, "gate_q must be [H, cube_m]");
+    TORCH_CHECK(gate_k.dim() == 2 && gate_k.size(0) == H && gate_k.size(1) == cube_m, "gate_k must be [H, cube_m]");
+}
+
+std::vector<at::Tensor> morpho_forward(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
+                                       const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
+                                       double scale, bool causal) {
+    check(X, "X");
+    check(W_phi, "W_phi");
+    check(gate_q, "gate_q");
+    check(gate_k, "gate_k");
+    check(W_V, "W_V");
+    check_shapes(X, W_phi, gate_q, gate_k, W_V, H, cube_m);
+    const c10::cuda::CUDAGuard guard(X.device());
+    const int64_t B = X.size(0), N = X.size(1);
+    auto out = at::empty_like(X);
+    auto lse = at::empty({B * H, N}, X.options().dtype(at::kFloat));
+    morpho_problem_t p = problem(X, H, cube_m, scale, causal);
+    const size_t ws_bytes = morpho_sm100_forward_workspace_size(&p);
+    TORCH_CHECK(ws_bytes > 0, "morphottention forward: unsupported problem: ", morpho_sm100_last_error());
+    auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
+    auto stream = at::cuda::getCurrentCUDAStream(X.device().index());
+    const int rc = morpho_sm100_forward(&p, X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(),
+                                        W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(), ws.data_ptr(),
+                                        ws_bytes, static_cast<void*>(stream.stream()));
+    TORCH_CHECK(rc == MORPHO_OK, "morphottention forward failed (", rc, "): ", morpho_sm100_last_error());
+    return {out, lse};
+}
+
+std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Tensor& X, const at::Tensor& W_phi,
+                                        const at::Tensor& gate_q, const at::Tensor& gate_k, const at::Tensor& W_V,
+                                        const at::Tensor& out, const at::Tensor& lse, int64_t H, int64_t cube_m,
+                                        double scale, bool causal) {
+    TORCH_CHECK(grad_out.is_cuda() && X.is_cuda(), "Gradient output and X must be a CUDA tensors");
+    check(grad_out, "grad_out");
+    check(X, "X");
+    check(W_phi, "W_phi");
+    check(gate_q, "gate_q");
+    check(gate_k, "gate_k");
+    check(W_V, "W_V");
+    check(out, "out");
+    TORCH_CHECK(lse.is_cuda(), "lse must be a CUDA tensor");
+    TORCH_CHECK(lse.scalar_type() == at::kFloat, "lse must be float32");
+    TORCH_CHECK(lse.is_contiguous(), "lse must be contiguous");
+    TORCH_CHECK(X.dim() == 3, "X must be [B, N, D]");
+    const int64_t B = X.size(0), N = X.size(1), D = X.size(2);
+    TORCH_CHECK(H > 0 && D % H == 0, "D must be divisible by H");
+    TORCH_CHECK(grad_out.sizes() == X.sizes(), "grad_out must match X shape [B, N, D]");
+    TORCH_CHECK(out.sizes() == X.sizes(), "out must match X shape [B, N, D]");
+    check_shapes(X, W_phi, gate_q, gate_k, W_V, H, cube_m);
+    TORCH_CHECK(lse.dim() == 2 && lse.size(0) == B * H && lse.size(1) == N, "lse must be [B*H, N]");
+    const c10::cuda::CUDAGuard guard(X.device());
+    auto dX = at::empty_like(X);
+    auto dW_phi = at::empty_like(W_phi);
+    auto d_gate_q = at::empty_like(gate_q);
+    auto d_gate_k = at::empty_like(gate_k);
+    auto dW_V = at::empty_like(W_V);
+    morpho_problem_t p = problem(X, H, cube_m, scale, causal);
+    const size_t ws_bytes = morpho_sm100_backward_workspace_size(&p);
+    TORCH_CHECK(ws_bytes > 0, "morphottention backward: unsupported problem: ", morpho_sm100_last_error());
+    auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
+    auto stream = at::cuda::getCurrentCUDAStream(X.device().index());
+    const int rc = morpho_sm100_backward(&p, grad_out.data_ptr(), X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(),
+                                         gate_k.data_ptr(), W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(),
+                                         dX.data_ptr(), dW_phi.data_ptr(), d_gate_q.data_ptr(), d_gate_k.data_ptr(),
+                                         dW_V.data_ptr(), nullptr, ws.data_ptr(), ws_bytes,
+                                         static_cast<void*>(stream.stream()));
+    TORCH_CHECK(rc == MORPHO_OK, "morphottention backward failed (", rc, "): ", morpho_sm100_last_error());
+    return {dX, dW_phi, d_gate_q, d_gate_k, dW_V};
+}
+
+int64_t set_grad_mode(int64_t mode) {
+    TORCH_CHECK(mode == MORPHO_GRAD_FULL || mode == MORPHO_GRAD_REFERENCE, "grad mode must be 0 (full) or 1 (reference)");
+    return g_grad_mode.exchange(static_cast<int>(mode));
+}
+
+int64_t get_grad_mode() { return g_grad_mode.load(); }
+
+}  // namespace
+
+TORCH_LIBRARY(morphottention, m) {
+    m.def(
+        "forward(Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, Tensor W_V, "
+        "int H, int cube_m, float scale, bool causal) -> Tensor[]");
+    m.def(
+        "backward(Tensor grad_out, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
+        "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
+    m.def("set_grad_mode(int mode) -> int", &set_grad_mode);
+    m.def("get_grad_mode() -> int", &get_grad_mode);
+}
+
+TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {
+    m.impl("forward", &morpho_forward);
+    m.impl("backward", &morpho_backward);
+}

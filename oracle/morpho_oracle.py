@@ -1,0 +1,163 @@
+"""CPU oracle for the MorphoAttention forward and backward.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker for the CUDA product path.
+Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl
+reference`` legs of ``bench.py`` may import it.  The product package never does.
+
+It is an fp32 (or fp64) eager restatement of the reference algorithm.  The reference
+ships no eager formulation: its only implementation is the WMMA CUDA kernel pair, so
+every step below cites the line of that kernel it restates.  Paths are relative to
+the reference project root (``packages/morphottention/...``).
+
+Math, per head ``h`` with token features ``x`` [N, D]:
+
+* ``z = x @ W_phi[:, h*m:(h+1)*m]`` and ``phi = sigmoid(z)``
+  (``csrc/cuda/sm120/project.cuh:26-34``, ``csrc/cuda/morfology/cube.cuh:12-14``)
+* ``q = gate_q[h] * phi``, ``k = gate_k[h] * phi`` (``project.cuh:36-37``)
+* ``qbias_i = sum_c gate_k[c] q_ic`` and ``cbias_j = sum_c gate_q[c] k_jc``
+  (``project.cuh:39-44``; called with swapped gates at ``attention.cu:78-79``, ``:102-103``)
+* ``S_ij = scale * (2 q_i.k_j - qbias_i - cbias_j)`` (``attention.cu:125``), causal mask
+  ``j > i`` (``attention.cu:129-130``), softmax over j (``attention.cu:138-158``)
+* ``V = x @ W_V[:, h*hd:(h+1)*hd]`` (``attention.cu:106-111``) and
+  ``out[:, :, h*hd:(h+1)*hd] = P @ V`` (``attention.cu:163-183``)
+* ``lse[b*H+h, i]`` in the log2 domain: ``max_j(s_ij) + log2(sum_j 2^(s_ij - max))``
+  with ``s = S * log2(e)`` (``attention.cu:186``), i.e. ``logsumexp(S_i) * log2(e)``.
+
+Gradient modes:
+
+* ``"full"``: true autograd of the math above.  This is the accuracy target.
+* ``"reference"``: the reference backward kernel's semantics.  That kernel
+  accumulates the query-side code gradient (``attention.cu:447-451``) and the
+  query-bias gradient (``attention.cu:425``) but never propagates them: no
+  ``project_phi_bwd`` runs for the query rows and the query-row ``dX`` accumulator
+  stays zero (``attention.cu:265-267``, ``:473-482``).  So ``dX``, ``dW_phi``,
+  ``d_gate_q`` and ``d_gate_k`` miss every term that flows through ``q`` and
+  ``qbias``.  Detaching ``q`` and ``qbias`` reproduces that exactly; ``out``, ``lse``
+  and ``dW_V`` are the same in both modes.
+"""
+
+from __future__ import annotations
+
+import torch
+
+LOG2E = 1.4426950408889634  # csrc/cuda/utils/declarations.cuh:7
+
+GRAD_MODES = ("full", "reference")
+
+
+def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int):
+    """Per-head hypercube codes, biases and values.
+
+    Restates ``project_phi`` (``csrc/cuda/sm120/project.cuh:16-47``) and the value
+    projection (``csrc/cuda/attention/attention.cu:106-111``).
+    Returns ``phi, q, k, qbias, cbias, v`` with shapes
+    ``[B,H,N,m] x3, [B,H,N] x2, [B,H,N,hd]``.
+    """
+    B, N, D = x.shape
+    hd = D // H
+    z = (x @ W_phi).view(B, N, H, cube_m).permute(0, 2, 1, 3)  # [B,H,N,m]
+    phi = torch.sigmoid(z)
+    gq = gate_q.view(1, H, 1, cube_m)
+    gk = gate_k.view(1, H, 1, cube_m)
+    q = gq * phi
+    k = gk * phi
+    qbias = (gk * q).sum(-1)
+    cbias = (gq * k).sum(-1)
+    v = (x @ W_V).view(B, N, H, hd).permute(0, 2, 1, 3)  # [B,H,N,hd]
+    return phi, q, k, qbias, cbias, v
+
+
+def _attend(q, k, qbias, cbias, v, scale: float, causal: bool):
+    """Score, mask, softmax and P.V; ``attention.cu:113-188``."""
+    N = q.shape[2]
+    s = scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))
+    if causal:
+        mask = torch.ones(N, N, dtype=torch.bool, device=q.device).triu(1)
+        s = s.masked_fill(mask, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = p @ v  # [B,H,N,hd]
+    lse2 = torch.logsumexp(s, dim=-1) * LOG2E  # [B,H,N], log2 domain
+    return o, lse2
+
+
+def forward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+            causal: bool = False, grad_mode: str = "full"):
+    """Eager forward.  Returns ``(out [B,N,D], lse [B*H,N])`` like ``morphottention::forward``
+    (``csrc/cuda/binder.cpp:7-8``, ``csrc/cuda/attention/attention.cpp:40-56``).
+
+    ``grad_mode="reference"`` detaches the query codes and the query bias so that a
+    later ``backward`` matches the reference kernel's gradient semantics.
+    """
+    if grad_mode not in GRAD_MODES:
+        raise ValueError(f"grad_mode must be one of {GRAD_MODES}")
+    B, N, D = x.shape
+    _, q, k, qbias, cbias, v = project(x, W_phi, gate_q, gate_k, W_V, H, cube_m)
+    if grad_mode == "reference":
+        q = q.detach()
+        qbias = qbias.detach()
+    o, lse2 = _attend(q, k, qbias, cbias, v, scale, causal)
+    out = o.permute(0, 2, 1, 3).reshape(B, N, D)
+    return out, lse2.reshape(B * H, N)
+
+
+def forward_backward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+                     causal: bool = False, grad_out=None, grad_mode: str = "full",
+                     dtype=torch.float32):
+    """Forward plus the backward of ``sum(out * grad_out)`` (``out.sum()`` when
+    ``grad_out`` is None).  Returns a dict with ``out, lse, dX, dW_phi, d_gate_q,
+    d_gate_k, dW_V`` in ``dtype`` on the inputs' device.
+    """
+    leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in (x, W_phi, gate_q, gate_k, W_V)]
+    with torch.enable_grad():
+        out, lse = forward(*leaves, H, cube_m, scale, causal, grad_mode)
+        g = torch.ones_like(out) if grad_out is None else grad_out.detach().to(dtype)
+        grads = torch.autograd.grad(out, leaves, grad_outputs=g)
+    names = ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V")
+    res = {"out": out.detach(), "lse": lse.detach()}
+    res.update({n: gr.detach() for n, gr in zip(names, grads)})
+    return res
+
+
+def forward_chunked(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+                    causal: bool = False, heads_per_chunk: int = 1):
+    """Forward only, looping over heads so that the ``N x N`` score matrix of one head is
+    the largest temporary.  Used for CPU timing at long sequence lengths."""
+    B, N, D = x.shape
+    hd = D // H
+    out = torch.empty(B, N, D, dtype=x.dtype)
+    lse = torch.empty(B * H, N, dtype=torch.float32)
+    for h0 in range(0, H, heads_per_chunk):
+        h1 = min(H, h0 + heads_per_chunk)
+        cols = slice(h0 * cube_m, h1 * cube_m)
+        sub_phi = W_phi[:, cols]
+        sub_v = W_V[:, h0 * hd:h1 * hd]
+        _, q, k, qb, cb, v = project(x, sub_phi, gate_q[h0:h1], gate_k[h0:h1], sub_v, h1 - h0, cube_m)
+        o, l2 = _attend(q, k, qb, cb, v, scale, causal)
+        out[:, :, h0 * hd:h1 * hd] = o.permute(0, 2, 1, 3).reshape(B, N, (h1 - h0) * hd)
+        lse.view(B, H, N)[:, h0:h1] = l2
+    return out, lse
+
+
+def rel_l2(a, b) -> float:
+    """Relative L2 error ``||a - b|| / ||b||`` in fp64 (``b`` is the reference)."""
+    a = a.detach().double().cpu()
+    b = b.detach().double().cpu()
+    den = b.norm().item()
+    num = (a - b).norm().item()
+    if den == 0.0:
+        return num
+    return num / den
+
+
+def soft_hamming_score(phi_i, phi_j, gate_q, gate_k, scale: float):
+    """Closed form of the score as a gated soft-Hamming (XOR) distance:
+    ``-scale * sum_c gq_c gk_c (phi_ic (1 - phi_jc) + phi_jc (1 - phi_ic))``.
+    Used by the tests to check the dot-product form of ``attention.cu:125``."""
+    w = gate_q * gate_k
+    a = phi_i.unsqueeze(-2)
+    b = phi_j.unsqueeze(-3)
+    return -scale * (w * (a * (1 - b) + b * (1 - a))).sum(-1)
+
+
+__all__ = ["LOG2E", "GRAD_MODES", "project", "forward", "forward_backward", "forward_chunked",
+           "rel_l2", "soft_hamming_score"]

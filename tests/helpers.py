@@ -1,0 +1,64 @@
+"""Shared test helpers: run the CUDA path through the C ABI and the oracle on the same
+seeded fp16 inputs, and compare with the stated tolerances."""
+
+from __future__ import annotations
+
+import torch
+
+from morphottention_b200 import capi
+from morphottention_b200.configs import MorphoConfig, make_inputs
+from oracle import morpho_oracle as O
+
+# Tolerances (rel-L2 against the fp32 oracle) stated by the project's accuracy target.
+TOL_OUT = 1e-3
+TOL_GRAD = 5e-3
+TOL_LSE = 1e-3  # lse (log2 units) inherits the fp16 rounding of the codes
+
+
+def run_cuda(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", backward: bool = True):
+    """Forward (+ backward) through libmorpho_sm100.so.  Inputs are fp16 CUDA tensors."""
+    dev = inp["x"].device
+    mode = capi.MORPHO_GRAD_FULL if grad_mode == "full" else capi.MORPHO_GRAD_REFERENCE
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, mode)
+    x = inp["x"]
+    out = torch.empty_like(x)
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
+    capi.forward(p, x, inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse)
+    res = {"out": out, "lse": lse}
+    if backward:
+        g = torch.ones_like(x) if grad_out is None else grad_out
+        dX = torch.empty_like(x)
+        dW_phi = torch.empty_like(inp["W_phi"])
+        dgq = torch.empty_like(inp["gate_q"])
+        dgk = torch.empty_like(inp["gate_k"])
+        dW_V = torch.empty_like(inp["W_V"])
+        capi.backward(p, g, x, inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse, dX, dW_phi, dgq,
+                      dgk, dW_V)
+        res.update({"dX": dX, "dW_phi": dW_phi, "d_gate_q": dgq, "d_gate_k": dgk, "dW_V": dW_V})
+    torch.cuda.synchronize()
+    status = capi.device_status(reset=True)
+    assert status == 0, f"device status word 0x{status:08x}"
+    return res
+
+
+def run_oracle(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", device="cpu"):
+    t = {k: v.to(device) for k, v in inp.items()}
+    g = None if grad_out is None else grad_out.to(device)
+    return O.forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m, cfg.scale,
+                              cfg.causal, grad_out=g, grad_mode=grad_mode)
+
+
+def compare(ours: dict, ref: dict, keys=None, tol_out=TOL_OUT, tol_grad=TOL_GRAD, tol_lse=TOL_LSE):
+    """Return {name: rel_l2} and assert every tolerance."""
+    errs = {}
+    for k in keys or ours.keys():
+        errs[k] = O.rel_l2(ours[k].float(), ref[k].float())
+    for k, e in errs.items():
+        tol = tol_out if k == "out" else (tol_lse if k == "lse" else tol_grad)
+        assert e <= tol, f"{k}: rel-L2 {e:.3e} > {tol:.1e} (all: {errs})"
+        assert torch.isfinite(ours[k].float()).all(), f"{k} has non-finite values"
+    return errs
+
+
+def inputs(cfg: MorphoConfig, device, random_gates=False, with_grad_out=False):
+    return make_inputs(cfg, device=device, random_gates=random_gates, with_grad_out=with_grad_out)
