@@ -61,7 +61,7 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
 }
 
 struct ProjParams {
-    int T, N, H, hd, Hp, D;
+    int T, N, Npad, H, hd, Hp, D;
     float c;  // scale * log2(e)
     const __half* gq;
     const __half* gk;
@@ -113,8 +113,9 @@ struct EpiProj {
                         dq[i] = make_uint4(qpk[4 * i], qpk[4 * i + 1], qpk[4 * i + 2], qpk[4 * i + 3]);
                         dk[i] = make_uint4(kpk[4 * i], kpk[4 * i + 1], kpk[4 * i + 2], kpk[4 * i + 3]);
                     }
-                    p.o.qb[base] = qb * p.c;
-                    p.o.cb[base] = cb * p.c;
+                    const size_t brow = static_cast<size_t>(b * p.H + h) * p.Npad + n;  // padded bias rows
+                    p.o.qb[brow] = qb * p.c;
+                    p.o.cb[brow] = cb * p.c;
                     if (p.o.phi != nullptr) {
                         float4* dp = reinterpret_cast<float4*>(p.o.phi + base * MC);
 #pragma unroll
@@ -393,6 +394,7 @@ int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __
     ProjParams p;
     p.T = static_cast<int>(T);
     p.N = s.N;
+    p.Npad = (s.N + 127) / 128 * 128;
     p.H = s.H;
     p.hd = s.hd;
     p.Hp = Hp;

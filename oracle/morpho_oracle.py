@@ -53,8 +53,8 @@ def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int):
     Returns ``phi, q, k, qbias, cbias, v`` with shapes
     ``[B,H,N,m] x3, [B,H,N] x2, [B,H,N,hd]``.
     """
-    B, N, D = x.shape
-    hd = D // H
+    B, N, _ = x.shape
+    hd = W_V.shape[1] // H
     z = (x @ W_phi).view(B, N, H, cube_m).permute(0, 2, 1, 3)  # [B,H,N,m]
     phi = torch.sigmoid(z)
     gq = gate_q.view(1, H, 1, cube_m)

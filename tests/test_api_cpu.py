@@ -1,0 +1,78 @@
+"""The Python surface mirrors the reference package (no GPU needed for these checks)."""
+
+import inspect
+
+import pytest
+import torch
+
+import morphottention_b200 as M
+
+
+def test_exports():
+    for name in ("MorphoAttention", "MorphoAttentionFunction", "morpho_attention"):
+        assert hasattr(M, name)
+    assert hasattr(torch.ops.morphottention, "forward")
+    assert hasattr(torch.ops.morphottention, "backward")
+
+
+def test_schemas_match_reference():
+    fwd = str(torch.ops.morphottention.forward.default._schema)
+    bwd = str(torch.ops.morphottention.backward.default._schema)
+    assert fwd == ("morphottention::forward(Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, Tensor W_V, "
+                   "int H, int cube_m, float scale, bool causal) -> Tensor[]")
+    assert bwd == ("morphottention::backward(Tensor grad_out, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
+                   "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]")
+
+
+def test_module_constructor_and_init():
+    torch.manual_seed(0)
+    m = M.MorphoAttention(256, 8, 16, scale=0.5, causal=True)
+    assert m.W_phi.shape == (256, 128) and m.W_V.shape == (256, 256)
+    assert m.gate_q.shape == (8, 16) and m.gate_k.shape == (8, 16)
+    assert m.W_phi.dtype == torch.float16
+    assert torch.all(m.gate_q == 1) and torch.all(m.gate_k == 1)
+    std = m.W_V.float().std().item()
+    assert abs(std - 256 ** -0.5) < 0.1 * 256 ** -0.5
+    assert [n for n, _ in m.named_parameters()] == ["W_phi", "gate_q", "gate_k", "W_V"]
+    assert m.scale == 0.5 and m.causal is True
+
+
+def test_constructor_signature():
+    sig = inspect.signature(M.MorphoAttention.__init__)
+    assert list(sig.parameters) == ["self", "dim", "num_heads", "cube_m", "scale", "causal", "dtype", "device"]
+    assert sig.parameters["scale"].kind is inspect.Parameter.KEYWORD_ONLY
+    fsig = inspect.signature(M.morpho_attention)
+    assert list(fsig.parameters)[:7] == ["x", "W_phi", "gate_q", "gate_k", "W_V", "num_heads", "cube_m"]
+
+
+def test_dim_not_divisible():
+    with pytest.raises(ValueError, match="must be divisible"):
+        M.MorphoAttention(100, 3, 16)
+
+
+def test_cpu_input_rejected():
+    m = M.MorphoAttention(64, 2, 16)
+    with pytest.raises(ValueError, match="expects a CUDA tensor"):
+        m(torch.randn(1, 4, 64, dtype=torch.float16))
+
+
+def test_fake_kernels():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty(2, 5, 64, dtype=torch.float16, device="cuda")
+        wp = torch.empty(64, 32, dtype=torch.float16, device="cuda")
+        g = torch.empty(2, 16, dtype=torch.float16, device="cuda")
+        wv = torch.empty(64, 64, dtype=torch.float16, device="cuda")
+        out, lse = torch.ops.morphottention.forward(x, wp, g, g, wv, 2, 16, 1.0, False)
+        assert out.shape == x.shape and lse.shape == (4, 5) and lse.dtype == torch.float32
+        grads = torch.ops.morphottention.backward(out, x, wp, g, g, wv, out, lse, 2, 16, 1.0, False)
+        assert [t.shape for t in grads] == [x.shape, wp.shape, g.shape, g.shape, wv.shape]
+
+
+def test_grad_mode_switch():
+    assert M.get_grad_mode() == "full"
+    with M.grad_mode("reference"):
+        assert M.get_grad_mode() == "reference"
+    assert M.get_grad_mode() == "full"
+    with pytest.raises(ValueError):
+        M.set_grad_mode("bogus")

@@ -1,0 +1,71 @@
+"""The C ABI library loads, exports every entry point declared in include/*.h, and its
+argument validation works without a GPU (no compute call is made here)."""
+
+import ctypes
+import glob
+import os
+import re
+
+from morphottention_b200 import capi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names.update(re.findall(r"MORPHO_API\s+[\w\s\*]+?\b(morpho_\w+)\s*\(", src))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert {"morpho_sm100_forward", "morpho_sm100_backward", "morpho_sm100_project"} <= names
+    assert names == set(capi.EXPORTED), names ^ set(capi.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    L = capi.lib()
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+
+
+def test_workspace_sizes():
+    L = capi.lib()
+    p = capi.problem(4, 4096, 1024, 16, 32, 0.5, False)
+    fw = L.morpho_sm100_forward_workspace_size(ctypes.byref(p))
+    bw = L.morpho_sm100_backward_workspace_size(ctypes.byref(p))
+    assert 0 < fw < bw
+    # codes (2 x fp16 [BH,N,m]) + V (fp16 [BH,N,hd]) + two fp32 bias rows
+    assert fw >= 2 * 64 * 4096 * 32 * 2 + 64 * 4096 * 64 * 2 + 2 * 64 * 4096 * 4
+    assert capi.weight_grad_elems(p) == 1024 * (512 + 1024) + 2 * 512
+
+
+def test_invalid_problems_rejected():
+    L = capi.lib()
+    bad = [capi.problem(0, 16, 64, 2, 16), capi.problem(1, 16, 65, 2, 16), capi.problem(1, 16, 96, 2, 16),
+           capi.problem(1, 16, 64, 2, 24), capi.problem(1, 16, 64, 2, 16, grad_mode=7)]
+    for p in bad:
+        assert L.morpho_sm100_forward_workspace_size(ctypes.byref(p)) == 0
+        rc = L.morpho_sm100_forward(ctypes.byref(p), *([None] * 8), 0, None)
+        assert rc == capi.MORPHO_ERR_INVALID
+        assert capi.last_error()
+
+
+def test_null_pointer_rejected_before_device_use():
+    L = capi.lib()
+    p = capi.problem(1, 16, 64, 2, 16)
+    rc = L.morpho_sm100_forward(ctypes.byref(p), *([None] * 8), 0, None)
+    assert rc == capi.MORPHO_ERR_INVALID
+    assert "NULL" in capi.last_error()
+
+
+def test_misaligned_pointer_rejected():
+    L = capi.lib()
+    p = capi.problem(1, 16, 64, 2, 16)
+    ptrs = [ctypes.c_void_p(0x1000 + 16 * i) for i in range(8)]
+    ptrs[0] = ctypes.c_void_p(0x1002)
+    rc = L.morpho_sm100_forward(ctypes.byref(p), *ptrs, 1 << 30, None)
+    assert rc == capi.MORPHO_ERR_INVALID
+    assert "aligned" in capi.last_error()
