@@ -34,7 +34,9 @@ struct BwdCfg {
     static constexpr int V_BYTES = kTile * HD * 2;   // one V or dO tile
     static constexpr int KC_STRIDE = (KC_BYTES + 1023) / 1024 * 1024;
     static constexpr int OFF_K = 0;
-    static constexpr int OFF_V = OFF_K + KC_STRIDE;
+    static constexpr int OFF_KH = OFF_K + KC_STRIDE;   // centered key codes, hi part (dQ MMA)
+    static constexpr int OFF_KL = OFF_KH + KC_STRIDE;  // centered key codes, lo part
+    static constexpr int OFF_V = OFF_KL + KC_STRIDE;
     static constexpr int OFF_Q = OFF_V + V_BYTES;
     static constexpr int OFF_DO = OFF_Q + kQStages * KC_STRIDE;
     static constexpr int OFF_DS = OFF_DO + kQStages * V_BYTES;  // 2 chunks x 128 rows x 128 B
@@ -83,6 +85,7 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks) {
 template <int MC, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmKH, const __grid_constant__ CUtensorMap tmKL,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmDelta,
                     const BwdArgs args) {
@@ -139,6 +142,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmKH);
+        tma_prefetch_desc(&tmKL);
         tma_prefetch_desc(&tmV);
         tma_prefetch_desc(&tmDO);
         tma_prefetch_desc(&tmL);
@@ -158,8 +163,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (lane == 0) {
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
             const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
-            mbar_arrive_expect_tx(kv_full, Cfg::KC_BYTES + Cfg::V_BYTES);
+            mbar_arrive_expect_tx(kv_full, 3 * Cfg::KC_BYTES + Cfg::V_BYTES);
             tma_load_3d(sK, &tmK, kv_full, 0, kv0, bh);
+            tma_load_3d(smem_u32(smem + Cfg::OFF_KH), &tmKH, kv_full, 0, kv0, bh);
+            tma_load_3d(smem_u32(smem + Cfg::OFF_KL), &tmKL, kv_full, 0, kv0, bh);
             tma_load_3d(sV, &tmV, kv_full, 0, kv0, bh);
             if (HD > 64) tma_load_3d(sV + kTile * 128, &tmV, kv_full, 64, kv0, bh);
             int issued = 0;
@@ -199,6 +206,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             constexpr uint32_t kc_sw = swizzle_code_for_row_bytes(Cfg::KC_ROW);
             constexpr uint32_t v_sw = swizzle_code_for_row_bytes(Cfg::V_ROW);
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
+            const uint32_t sKH = smem_u32(smem + Cfg::OFF_KH);
+            const uint32_t sKL = smem_u32(smem + Cfg::OFF_KL);
             const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
             const uint32_t sDS = smem_u32(smem + Cfg::OFF_DS);
             bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
@@ -248,11 +257,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const uint64_t bd = make_sdesc(sQ + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
                     umma_ts(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
                 }
+                // dQ = dS . (k - gate_k/2) as hi + lo fp16 parts, both accumulated in TMEM
 #pragma unroll
-                for (int ks = 0; ks < kTile / 16; ++ks) {
-                    const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
-                    const uint64_t bd = make_sdesc(sK + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
-                    umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, ks > 0 ? 1u : 0u);
+                for (int part = 0; part < 2; ++part) {
+                    const uint32_t sKd = part == 0 ? sKH : sKL;
+#pragma unroll
+                    for (int ks = 0; ks < kTile / 16; ++ks) {
+                        const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
+                        const uint64_t bd = make_sdesc(sKd + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
+                        umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
+                    }
                 }
                 umma_commit(dq_full);
                 umma_commit(ds_smem_free);
@@ -455,9 +469,13 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     using Cfg = BwdCfg<MC, HD>;
     const int BH = s.B * s.H;
     const int Npad = (s.N + kTile - 1) / kTile * kTile;
-    CUtensorMap tQ, tK, tV, tDO, tL, tDl;
+    CUtensorMap tQ, tK, tKH, tKL, tV, tDO, tL, tDl;
+    if (p.kdq_hi == nullptr || p.kdq_lo == nullptr)
+        return set_error(MORPHO_ERR_INVALID, "internal: backward needs the centered key codes");
     MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tKH, p.kdq_hi, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tKL, p.kdq_lo, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tV, p.v, HD, s.N, BH, HD, static_cast<uint64_t>(s.N) * HD, HD > 64 ? 64 : HD,
                                 kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tDO, io.dO, s.D, s.N, s.B, s.D, static_cast<uint64_t>(s.N) * s.D,
@@ -485,7 +503,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream);
-    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, tDO, tL, tDl, a);
+    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKH, tKL, tV, tDO, tL, tDl, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");
     return MORPHO_OK;
 }

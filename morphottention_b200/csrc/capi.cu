@@ -100,6 +100,8 @@ void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
     plan_proj(c, s, &b->proj);
     b->proj.phi = c.take<float>(BH * s.N * s.m);
+    b->proj.kdq_hi = c.take<__half>(BH * s.N * s.m);
+    b->proj.kdq_lo = c.take<__half>(BH * s.N * s.m);
     b->delta = c.take<float>(BH * Npad);
     b->L = c.take<float>(BH * Npad);
     b->dq = c.take<float>(BH * s.N * s.m);

@@ -88,7 +88,7 @@ struct EpiProj {
                 const __half2* gq2 = reinterpret_cast<const __half2*>(p.gq + h * MC);
                 const __half2* gk2 = reinterpret_cast<const __half2*>(p.gk + h * MC);
                 float qb = 0.f, cb = 0.f;
-                uint32_t qpk[MC / 2], kpk[MC / 2];
+                uint32_t qpk[MC / 2], kpk[MC / 2], hpk[MC / 2], lpk[MC / 2];
 #pragma unroll
                 for (int c = 0; c < MC; c += 2) {
                     const float2 gq = __half22float2(gq2[c / 2]);
@@ -103,6 +103,11 @@ struct EpiProj {
                     cb = fmaf(gq.x, k0, fmaf(gq.y, k1, cb));
                     qpk[c / 2] = pack_half2(q0, q1);
                     kpk[c / 2] = pack_half2(k0, k1);
+                    const float c0 = k0 - 0.5f * gk.x, c1 = k1 - 0.5f * gk.y;  // centered key code
+                    const __half2 hi = __floats2half2_rn(c0, c1);
+                    const float2 hf = __half22float2(hi);
+                    hpk[c / 2] = *reinterpret_cast<const uint32_t*>(&hi);
+                    lpk[c / 2] = pack_half2(c0 - hf.x, c1 - hf.y);
                 }
                 if (live) {
                     const size_t base = static_cast<size_t>(b * p.H + h) * p.N + n;
@@ -116,6 +121,15 @@ struct EpiProj {
                     const size_t brow = static_cast<size_t>(b * p.H + h) * p.Npad + n;  // padded bias rows
                     p.o.qb[brow] = qb * p.c;
                     p.o.cb[brow] = cb * p.c;
+                    if (p.o.kdq_hi != nullptr) {
+                        uint4* dh = reinterpret_cast<uint4*>(p.o.kdq_hi + base * MC);
+                        uint4* dl = reinterpret_cast<uint4*>(p.o.kdq_lo + base * MC);
+#pragma unroll
+                        for (int i = 0; i < MC / 8; ++i) {
+                            dh[i] = make_uint4(hpk[4 * i], hpk[4 * i + 1], hpk[4 * i + 2], hpk[4 * i + 3]);
+                            dl[i] = make_uint4(lpk[4 * i], lpk[4 * i + 1], lpk[4 * i + 2], lpk[4 * i + 3]);
+                        }
+                    }
                     if (p.o.phi != nullptr) {
                         float4* dp = reinterpret_cast<float4*>(p.o.phi + base * MC);
 #pragma unroll

@@ -12,7 +12,7 @@ import torch
 
 from morphottention_b200.configs import CONFIGS, MorphoConfig
 
-from .helpers import compare, inputs, run_cuda, run_oracle
+from .helpers import compare, gate_tolerance, inputs, run_cuda, run_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -38,7 +38,7 @@ def test_parity_small(cuda, cfg, random_gates):
     g = inp.pop("grad_out", None)
     ours = run_cuda(cfg, inp, grad_out=g)
     ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_out=None if g is None else g.cpu())
-    compare(ours, ref)
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
 
 
 @pytest.mark.parametrize("cfg", [SMALL[0], SMALL[2], SMALL[3]], ids=lambda c: c.name)
