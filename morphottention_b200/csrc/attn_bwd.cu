@@ -16,17 +16,25 @@
 // :436, :442).  Unlike the reference there are no fp16 global atomics: dV and dK are
 // complete per CTA and stored once; only dq is accumulated, in fp32.
 //
-// Warps (448 threads): 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 softmax for
-// queries [0,64) of the tile, 6..9 softmax for queries [64,128), 10..13 dQ epilogue.
+// Warps (512 threads, four warpgroups): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer (warps 2-3 idle), warps 4..7 softmax for queries [0,64) of the tile, 8..11 softmax
+// for queries [64,128), 12..15 dQ epilogue.  setmaxnreg moves registers from the producer
+// and dQ warpgroups to the two softmax warpgroups.
 #include "kernels.h"
 #include "sm100.cuh"
 
 namespace morpho {
 namespace {
 
-constexpr int kBwdThreads = 448;
+constexpr int kBwdThreads = 512;
 constexpr int kTile = 128;
 constexpr int kQStages = 2;
+// Register split (512 threads x 128 at launch = 65536): producer/MMA warpgroup 88, dQ
+// warpgroup 56, the two softmax warpgroups 184 each; 128*88 + 128*56 + 256*184 = 65536.
+constexpr uint32_t kRegsProducer = 88;
+constexpr uint32_t kRegsDq = 56;
+constexpr uint32_t kRegsSoftmax = 184;
+static_assert(128 * kRegsProducer + 128 * kRegsDq + 256 * kRegsSoftmax == 65536, "register split");
 
 template <int MC, int HD>
 struct BwdCfg {
@@ -157,8 +165,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int wgroup = warp >> 2;
 
-    if (warp == 0) {
+    // Each role's code sits inside the branch that adjusts its warpgroup's registers, so
+    // the register allocator budgets it with the post-setmaxnreg count.
+    if (wgroup == 0) {
+      regs_dec<kRegsProducer>();
+      if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     mbar_wait(q_full0 + 8 * (i % kQStages), (i / kQStages) & 1, args.status, K_ATTN_BWD, 2);
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);   // S^T, dP^T
@@ -210,30 +223,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const uint32_t sKL = smem_u32(smem + Cfg::OFF_KL);
             const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
             const uint32_t sDS = smem_u32(smem + Cfg::OFF_DS);
-            bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
-            for (int it = 0; ok && it < n_it; ++it) {
-                const int s = it % kQStages;
-                const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q + s * Cfg::KC_STRIDE);
-                const uint32_t sDO = smem_u32(smem + Cfg::OFF_DO + s * Cfg::V_BYTES);
-                if (!mbar_wait(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 4) || *abort_flag) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                // S^T = Kc . Qc^T
+            auto qbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_Q + (it % kQStages) * Cfg::KC_STRIDE); };
+            auto dobuf = [&](int it) { return smem_u32(smem + Cfg::OFF_DO + (it % kQStages) * Cfg::V_BYTES); };
+            // S^T = Kc . Qc^T
+            auto issue_s = [&](int it) {
+                const uint32_t sQ = qbuf(it);
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks)
                     umma_ss(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
                             id_s, ks > 0 ? 1u : 0u);
                 umma_commit(s_full);
-                // dP^T = V . dO^T
+            };
+            // dP^T = V . dO^T
+            auto issue_dp = [&](int it) {
+                const uint32_t sDO = dobuf(it);
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks)
                     umma_ss(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
                             id_s, ks > 0 ? 1u : 0u);
                 umma_commit(dp_full);
+            };
+            // Issue order per query tile i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}.  tcgen05.mma
+            // from one thread execute in order, so S_{i+1} may overwrite the P_i columns it
+            // follows, and dP_{i+1} the dS_i columns; the softmax warps get S_{i+1} while they
+            // are still busy with dS_i.
+            bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
+            if (ok && n_it > 0) {
+                ok = mbar_wait(q_full0, 0, args.status, K_ATTN_BWD, 4);
+                if (ok) {
+                    tc_fence_after();
+                    issue_s(0);
+                    issue_dp(0);
+                }
+            }
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int s = it % kQStages;
+                const uint32_t sQ = qbuf(it);
+                const uint32_t sDO = dobuf(it);
                 // dV += P^T . dO  (P^T halves live in S columns [0,32) and [64,96))
-                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
+                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5) || *abort_flag) {
                     ok = false;
                     break;
                 }
@@ -243,6 +271,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const uint32_t a = tmem + Cfg::TM_S + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
                     const uint64_t bd = make_sdesc(sDO + ks * 16 * Cfg::V_ROW, kTile * 128, 8 * Cfg::V_ROW, v_sw);
                     umma_ts(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
+                }
+                if (it + 1 < n_it) {
+                    if (!mbar_wait(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1, args.status,
+                                   K_ATTN_BWD, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(it + 1);
                 }
                 // dK += dS^T . Qc ;  dQ = dS . Kc
                 if (!mbar_wait(ds_full, it & 1, args.status, K_ATTN_BWD, 6) ||
@@ -271,6 +308,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 umma_commit(dq_full);
                 umma_commit(ds_smem_free);
                 umma_commit(q_empty0 + 8 * s);
+                if (it + 1 < n_it) issue_dp(it + 1);
             }
             if (ok) {
                 umma_commit(all_done);
@@ -281,9 +319,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 umma_commit(all_done);  // release the epilogue waits
             }
         }
-    } else if (warp < 10) {
-        // ---------------- softmax warps (2..9) ----------------
-        const int wg = (warp - 2) >> 2;   // 0: queries [0,64), 1: queries [64,128)
+      }
+    } else if (wgroup == 1 || wgroup == 2) {
+        regs_inc<kRegsSoftmax>();
+        // ---------------- softmax warps (4..11) ----------------
+        const int wg = wgroup - 1;        // 0: queries [0,64), 1: queries [64,128)
         const int quad = warp & 3;
         const int j = quad * 32 + lane;   // key row within the tile
         const int kv = kv0 + j;
@@ -427,31 +467,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             *abort_flag = 1u;
         }
     } else {
-        // ---------------- dQ warps (10..13) ----------------
+        regs_dec<kRegsDq>();
+        // ---------------- dQ warps (12..15) ----------------
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // query row within the tile
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
         for (int it = 0; it < n_it; ++it) {
             if (!mbar_wait_warp(dq_full, it & 1, args.status, K_ATTN_BWD, 14) || *abort_flag) break;
             tc_fence_after();
-            float v[MC];
+            const int q = (i_begin + it) * kTile + r;
+            float* dst = args.dq + (static_cast<size_t>(bh) * args.N + q) * MC;
 #pragma unroll
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
                 tmem_ld16(lane_base + Cfg::TM_DQ + c, rr);
                 tmem_ld_wait();
+                if (c + 16 == MC) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(dq_free);
+                }
+                if (q < args.N) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[c + i] = u2f(rr[i]) * args.two_scale;
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
-            const int q = (i_begin + it) * kTile + r;
-            if (q < args.N) {
-                float4* dst = reinterpret_cast<float4*>(args.dq + (static_cast<size_t>(bh) * args.N + q) * MC);
-#pragma unroll
-                for (int i = 0; i < MC / 4; ++i)
-                    atomicAdd(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+                    for (int i = 0; i < 16; i += 4)
+                        red_add_v4(dst + c + i, u2f(rr[i]) * args.two_scale, u2f(rr[i + 1]) * args.two_scale,
+                                   u2f(rr[i + 2]) * args.two_scale, u2f(rr[i + 3]) * args.two_scale);
+                }
             }
         }
     }

@@ -17,15 +17,21 @@
 //
 // lse (log2 domain, attention.cu:186) = m + log2(l) - qb', qb' = scale*log2e*qbias.
 //
-// Warps (192 threads): 0 = TMA producer, 1 = TMEM owner + MMA issuer, 2..5 = softmax
-// and epilogue (warp w owns TMEM lanes / query rows 32*(w%4) .. +31).
+// Warps (256 threads, two warpgroups): 0 = TMA producer, 1 = TMEM owner + MMA issuer,
+// 2-3 idle, 4..7 = softmax and epilogue (warp w owns TMEM lanes / query rows
+// 32*(w%4) .. +31).  setmaxnreg moves registers from the first to the second warpgroup.
 #include "kernels.h"
 #include "sm100.cuh"
 
 namespace morpho {
 namespace {
 
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 256;
+// Register split (256 threads x 128 at launch, two CTAs per SM): producer/MMA warpgroup
+// 56, softmax warpgroup 200; 128*56 + 128*200 = 256*128.
+constexpr uint32_t kRegsProducer = 56;
+constexpr uint32_t kRegsSoftmax = 200;
+static_assert(128 * kRegsProducer + 128 * kRegsSoftmax == kFwdThreads * 128, "register split");
 constexpr int kTile = 128;
 constexpr int kKvStages = 3;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -119,7 +125,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp < 4) {
+      regs_dec<kRegsProducer>();
+      if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q);
@@ -157,7 +165,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     mbar_wait(kv_full0 + 8 * (i % kKvStages), (i / kKvStages) & 1, args.status, K_ATTN_FWD, 2);
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
@@ -217,8 +225,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 mbar_wait(drain, 0, args.status, K_ATTN_FWD, 7);
             }
         }
+      }
     } else {
-        // ---------------- softmax + epilogue (warps 2..5) ----------------
+        regs_inc<kRegsSoftmax>();
+        // ---------------- softmax + epilogue (warps 4..7) ----------------
         const int quad = warp & 3;
         const int r = quad * 32 + lane;  // query row within the tile
         const int q = q0 + r;

@@ -253,6 +253,23 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_ma
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Fire-and-forget vector fp32 add to global memory (no return value, so the issuing
+// warp never waits on it).
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+// Per-warpgroup register reallocation (all 128 threads of the warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------------------------
 // small math / packing helpers
 // ------------------------------------------------------------------------------------
