@@ -82,6 +82,21 @@ MORPHO_API int morpho_sm100_backward(const morpho_problem_t* p, const void* grad
                           const float* lse, void* dX, void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V,
                           float* dweights_f32, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Forward that allocates nothing, for callers that cannot allocate device memory where
+ * they run it (a memory-pressure callback, a server whose memory plan is frozen after
+ * start-up, a host language without an allocator binding).  No counterpart in the
+ * reference.  Same arguments and results as morpho_sm100_forward minus the workspace: the
+ * scratch lives in a fixed device array inside this library (size given by
+ * morpho_sm100_forward_noalloc_max_scratch(), 32 MiB), held by every GPU that loads the
+ * library until exit.  Problems whose forward workspace exceeds it are rejected with
+ * MORPHO_ERR_WORKSPACE.  The first call on each device looks the array's address up
+ * (cudaGetSymbolAddress); make it outside any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race; calls ordered on one stream are safe. */
+MORPHO_API int morpho_sm100_forward_noalloc(const morpho_problem_t* p, const void* X, const void* W_phi,
+                                            const void* gate_q, const void* gate_k, const void* W_V, void* out,
+                                            float* lse, void* stream);
+MORPHO_API size_t morpho_sm100_forward_noalloc_max_scratch(void);
+
 /* Projection only (one GEMM with a fused epilogue): the per-head hypercube codes and
  * values the attention kernels consume.  Replaces the per-tile project_phi
  * (packages/morphottention/csrc/cuda/sm120/project.cuh:16-47) and the value projection

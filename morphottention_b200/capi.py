@@ -28,6 +28,8 @@ EXPORTED = (
     "morpho_sm100_forward",
     "morpho_sm100_backward",
     "morpho_sm100_project",
+    "morpho_sm100_forward_noalloc",
+    "morpho_sm100_forward_noalloc_max_scratch",
     "morpho_sm100_weight_grad_elems",
     "morpho_sm100_finalize_weight_grads",
     "morpho_sm100_last_error",
@@ -73,6 +75,10 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_forward.restype = i32
     L.morpho_sm100_backward.argtypes = [P] + [vp] * 14 + [vp, sz, vp]
     L.morpho_sm100_backward.restype = i32
+    L.morpho_sm100_forward_noalloc.argtypes = [P] + [vp] * 7 + [vp]
+    L.morpho_sm100_forward_noalloc.restype = i32
+    L.morpho_sm100_forward_noalloc_max_scratch.argtypes = []
+    L.morpho_sm100_forward_noalloc_max_scratch.restype = sz
     L.morpho_sm100_project.argtypes = [P] + [vp] * 11 + [vp]
     L.morpho_sm100_project.restype = i32
     L.morpho_sm100_finalize_weight_grads.argtypes = [P, vp, ctypes.c_float, vp, vp, vp, vp, vp]
@@ -125,6 +131,17 @@ def forward(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, out, lse, stream=No
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
     _check(L.morpho_sm100_forward(ctypes.byref(p), _ptr(X), _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V),
                                   _ptr(out), _ptr(lse), _ptr(ws), ws_bytes, _stream(stream)))
+
+
+def forward_noalloc(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, out, lse, stream=None) -> None:
+    """Forward without any device allocation: the scratch is the library's built-in array
+    (see ``morpho_sm100_forward_noalloc`` in include/morpho_sm100.h)."""
+    _check(lib().morpho_sm100_forward_noalloc(ctypes.byref(p), _ptr(X), _ptr(W_phi), _ptr(gate_q), _ptr(gate_k),
+                                              _ptr(W_V), _ptr(out), _ptr(lse), _stream(stream)))
+
+
+def forward_noalloc_max_scratch() -> int:
+    return int(lib().morpho_sm100_forward_noalloc_max_scratch())
 
 
 def backward(p: MorphoProblem, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
