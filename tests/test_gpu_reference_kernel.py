@@ -1,0 +1,125 @@
+"""Our kernels against the reference's own CUDA kernels (compiled from its sources into
+oracle/_ref) on identical seeded inputs, at the shapes where the reference launches on
+B200.  Gradients are compared in the reference's gradient semantics (grad_mode
+"reference").  Also prints the measured forward times of both at the long-sequence
+configuration (the reference backward cannot launch there: its shared-memory request
+exceeds the 227 KB limit)."""
+
+import pytest
+import torch
+
+from morphottention_b200.configs import CONFIGS, MorphoConfig, make_inputs
+from oracle import morpho_oracle as O
+
+from . import refkernel
+from .helpers import run_cuda
+
+pytestmark = pytest.mark.gpu
+
+FWD_BWD = [
+    (CONFIGS["c1"], True),
+    (MorphoConfig("narrow_causal_m16", 1, 256, 128, 2, 16, 1.0, True, 21), True),
+    (MorphoConfig("narrow_m32_n197", 1, 197, 128, 2, 32, 0.5, False, 22), True),
+    (MorphoConfig("c3_narrow", 2, 4096, 128, 2, 32, 0.5, False, 2), False),
+]
+FWD_ONLY = [CONFIGS["c2"], CONFIGS["c3"], CONFIGS["c4"]]
+
+
+def _need(cfg):
+    if not refkernel.available(cfg.cube_m, cfg.head_dim, cfg.causal):
+        pytest.skip("reference kernel not built (oracle/_ref); run oracle/build_ref.py")
+
+
+@pytest.mark.parametrize("cfg,gates", FWD_BWD, ids=lambda c: getattr(c, "name", str(c)))
+def test_matches_reference_kernel_fwd_bwd(cuda, cfg, gates):
+    _need(cfg)
+    inp = make_inputs(cfg, device=cuda, random_gates=gates)
+    r_out, r_lse = refkernel.forward(cfg, inp)
+    r_grads = refkernel.backward(cfg, inp, r_out, r_lse, torch.ones_like(r_out))
+    ours = run_cuda(cfg, inp, grad_mode="reference")
+    assert O.rel_l2(ours["out"].float(), r_out.float()) < 1e-3
+    assert O.rel_l2(ours["lse"], r_lse) < 1e-3
+    if cfg.tokens <= 256:
+        # small problems: the reference's fp16 gradient atomics are still accurate
+        for k, tol in (("dX", 1e-2), ("dW_phi", 1e-2), ("d_gate_q", 2e-2), ("d_gate_k", 2e-2), ("dW_V", 1e-2)):
+            e = O.rel_l2(ours[k].float(), r_grads[k].float())
+            print(cfg.name, k, f"{e:.2e}")
+            assert e < tol, (k, e)
+    else:
+        # long sequences: the reference sums thousands of tile partials with fp16 atomics;
+        # judge both against the fp32 oracle in the reference's gradient semantics
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref = O.forward_backward(*(inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")), cfg.H, cfg.cube_m,
+                                 cfg.scale, cfg.causal, grad_mode="reference")
+        for k in ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"):
+            e_ours = O.rel_l2(ours[k].float(), ref[k])
+            e_ref = O.rel_l2(r_grads[k].float(), ref[k])
+            print(cfg.name, k, f"ours {e_ours:.2e} reference-kernel {e_ref:.2e} (vs fp32 oracle)")
+            assert e_ours < 5e-3 and e_ours <= e_ref * 1.05 + 1e-4, (k, e_ours, e_ref)
+
+
+@pytest.mark.parametrize("cfg", FWD_ONLY, ids=lambda c: c.name)
+def test_matches_reference_kernel_forward_and_time(cuda, cfg):
+    _need(cfg)
+    inp = make_inputs(cfg, device=cuda)
+    r_out, r_lse = refkernel.forward(cfg, inp)
+    ours = run_cuda(cfg, inp, backward=False)
+    assert O.rel_l2(ours["out"].float(), r_out.float()) < 1e-3
+    assert O.rel_l2(ours["lse"], r_lse) < 1e-3
+    from morphottention_b200 import capi
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty_like(r_lse)
+
+    def t(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    ref_ms = t(lambda: refkernel.forward(cfg, inp))
+    our_ms = t(lambda: capi.forward(p, inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse))
+    print(f"{cfg.name} forward: reference {ref_ms:.3f} ms ({cfg.tokens / ref_ms * 1e3:.3e} tok/s), "
+          f"ours {our_ms:.3f} ms ({cfg.tokens / our_ms * 1e3:.3e} tok/s), speed-up {ref_ms / our_ms:.1f}x")
+
+
+def test_time_c3_narrow_fwd_bwd(cuda):
+    """fwd+bwd timing at the narrow long-sequence shape where the reference backward
+    launches (B=2... D=128, H=2, m=32, N=4096)."""
+    cfg = FWD_BWD[3][0]
+    _need(cfg)
+    from morphottention_b200 import capi
+    inp = make_inputs(cfg, device=cuda)
+    g = torch.ones_like(inp["x"])
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, capi.MORPHO_GRAD_REFERENCE)
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=cuda)
+    grads = [torch.empty_like(inp[k]) for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+
+    def ours():
+        capi.forward(p, inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse)
+        capi.backward(p, g, inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse, *grads)
+
+    def ref():
+        o, l = refkernel.forward(cfg, inp)
+        refkernel.backward(cfg, inp, o, l, g)
+
+    def t(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    r, o = t(ref), t(ours)
+    print(f"c3_narrow fwd+bwd: reference {r:.3f} ms ({cfg.tokens / r * 1e3:.3e} tok/s), ours {o:.3f} ms "
+          f"({cfg.tokens / o * 1e3:.3e} tok/s), speed-up {r / o:.1f}x")
