@@ -183,7 +183,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import morphottention_b200 as M
-    from morphottention_b200 import capi
+    from morphottention_b200 import capi, dp
     from morphottention_b200.configs import CONFIGS, make_inputs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -215,7 +215,7 @@ def run_ours(args):
         capi.forward(p, x, W_phi, gq, gk, W_V, out, lse)
         if world > 1:
             capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, None, None, None, None, dweights_f32=bucket)
-            dist.all_reduce(bucket)
+            dp.allreduce_bucket(bucket, average=False)
             capi.finalize_weight_grads(p, bucket, 1.0 / world, dW_phi, dgq, dgk, dW_V)
         else:
             capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
@@ -274,14 +274,7 @@ def run_ours(args):
                 q.grad = None
             loss.backward()
             if world > 1:
-                flat = torch.cat([q.grad.float().reshape(-1) for q in params])
-                dist.all_reduce(flat)
-                flat.div_(world)
-                off = 0
-                for q in params:
-                    n = q.numel()
-                    q.grad.copy_(flat[off:off + n].view_as(q.grad))
-                    off += n
+                dp.allreduce_weight_grads(mod)
             return loss.item()
 
         for _ in range(max(2, args.warmup)):
