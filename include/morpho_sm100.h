@@ -102,7 +102,9 @@ MORPHO_API size_t morpho_sm100_forward_noalloc_max_scratch(void);
  * (packages/morphottention/csrc/cuda/sm120/project.cuh:16-47) and the value projection
  * (attention.cu:106-111), which the reference recomputes for every query block.
  * Outputs, with BH = B*H and Npad = N rounded up to a multiple of 128:
- *   qc, kc  fp16 [BH, N, cube_m]   gate_q*phi, gate_k*phi with phi = sigmoid(X @ W_phi_h)
+ *   qc      fp16 [BH, N, cube_m]   gate_q*(phi - 1/2), phi = sigmoid(X @ W_phi_h): centered
+ *                                  query codes, so kc . qc = q.k - cbias/2 (the column bias)
+ *   kc      fp16 [BH, N, cube_m]   gate_k*phi
  *   v       fp16 [BH, N, D/H]      X @ W_V_h
  *   qb, cb  fp32 [BH, Npad]        scale*log2(e) * sum_c gate_k q_c, resp. sum_c gate_q k_c
  *   phi     fp32 [BH, N, cube_m]   optional (may be NULL)

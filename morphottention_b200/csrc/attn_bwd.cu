@@ -3,6 +3,7 @@
 // One CTA = one 128-key tile (kv0 .. kv0+127) of one (batch, head); it loops over the
 // query tiles.  TMEM lane j = key row j.  Per query tile i:
 //   S^T  = Kc . Qc_i^T          (M=128 keys, N=128 queries, K=cube_m)   TMEM [0,128)
+//       (centered query codes: S = k.q - cb_j/2)
 //   dP^T = V . dO_i^T           (K=head_dim)                              TMEM [128,256)
 //   softmax warps: P^T = 2^(2*scale*log2e*S - cb'_j - L_i), L = lse + qb' (recompute
 //       from lse as attention.cu:351-368 does), written back as fp16 into the S columns;
@@ -10,6 +11,7 @@
 //       into a 128B-swizzled shared buffer; dcb_j += sum_i dS (attention.cu:430-437).
 //   dV += P^T . dO_i            (A = P^T from TMEM)                       TMEM [256, +hd)
 //   dK += dS^T . Qc_i           (A = dS^T from TMEM, B = Qc MN-major)      TMEM [.., +m)
+//       (centered codes: this is dk + gate_q * dcb, whose cancelling bias term is exact)
 //   dQ_i = dS . Kc              (A = dS from smem, MN-major)               TMEM [.., +m)
 //   dQ warps: dq[b,h,q,:] += 2*scale * dQ_i  (fp32 atomics into a workspace)
 // Scale factors: dL/dS_raw = 2*scale*dS and dL/dcbias = -scale*sum_i dS (attention.cu:425,
@@ -49,12 +51,14 @@ struct BwdCfg {
     static constexpr int OFF_DO = OFF_Q + kQStages * KC_STRIDE;
     static constexpr int OFF_DS = OFF_DO + kQStages * V_BYTES;  // 2 chunks x 128 rows x 128 B
     static constexpr int DS_BYTES = 2 * kTile * 128;
-    static constexpr int OFF_L = OFF_DS + DS_BYTES;
-    static constexpr int OFF_DELTA = OFF_L + kQStages * kTile * 4;
-    static constexpr int OFF_DCB = OFF_DELTA + kQStages * kTile * 4;
+    static constexpr int AUG_BYTES = kTile * 16 * 2;  // one 16-column bias slice
+    static constexpr int OFF_VAUG = OFF_DS + DS_BYTES;
+    static constexpr int OFF_QAUG = OFF_VAUG + AUG_BYTES;
+    static constexpr int OFF_L = OFF_QAUG + kQStages * AUG_BYTES;
+    static constexpr int OFF_DCB = OFF_L + kQStages * kTile * 4;
     static constexpr int OFF_BAR = OFF_DCB + kTile * 4;
     static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
-    static constexpr int STAGE_TX = KC_BYTES + V_BYTES + 2 * kTile * 4;
+    static constexpr int STAGE_TX = KC_BYTES + V_BYTES + AUG_BYTES + kTile * 4;
     static constexpr uint32_t TM_S = 0;
     static constexpr uint32_t TM_DP = 128;
     static constexpr uint32_t TM_DV = 256;
@@ -64,7 +68,7 @@ struct BwdCfg {
     static constexpr uint32_t KC_ROW = MC * 2;
     static constexpr uint32_t V_ROW = (HD > 64 ? 64 : HD) * 2;
     static_assert(TM_DQ + MC <= TMEM_COLS, "TMEM budget");
-    static_assert(SMEM_BYTES <= 227 * 1024, "smem budget");
+    static_assert(SMEM_BYTES <= 232448, "smem budget");
 };
 
 struct BwdArgs {
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmKH, const __grid_constant__ CUtensorMap tmKL,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmDelta,
+                    const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmQaug,
                     const BwdArgs args) {
     using Cfg = BwdCfg<MC, HD>;
     extern __shared__ uint8_t smem_raw[];
@@ -155,7 +159,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_prefetch_desc(&tmV);
         tma_prefetch_desc(&tmDO);
         tma_prefetch_desc(&tmL);
-        tma_prefetch_desc(&tmDelta);
+        tma_prefetch_desc(&tmQaug);
+    }
+    // Constant value-side slice of the dP MMA: every row [0, 0, 1, 1, 0 ...] (K-major,
+    // 32-byte rows, 32-byte swizzle: the two 16-byte chunks of row r swap when bit 2 of r
+    // is set).  Against the query slice [1, 1, -delta_hi, -delta_lo, ...] it adds -delta.
+    if (threadIdx.x < 2 * kTile) {
+        const int r = threadIdx.x >> 1, c = threadIdx.x & 1;
+        const int phys = c ^ ((r >> 2) & 1);
+        const uint32_t one2 = 0x3C003C00u;  // two fp16 ones
+        *reinterpret_cast<uint4*>(smem + Cfg::OFF_VAUG + r * 32 + phys * 16) =
+            c == 0 ? make_uint4(0u, one2, 0u, 0u) : make_uint4(0u, 0u, 0u, 0u);
+        fence_proxy_async_smem();
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -200,7 +215,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tma_load_3d(sDO, &tmDO, fb, h * HD, q0, b);
                 if (HD > 64) tma_load_3d(sDO + kTile * 128, &tmDO, fb, h * HD + 64, q0, b);
                 tma_load_2d(smem_u32(smem + Cfg::OFF_L + s * kTile * 4), &tmL, fb, q0, bh);
-                tma_load_2d(smem_u32(smem + Cfg::OFF_DELTA + s * kTile * 4), &tmDelta, fb, q0, bh);
+                tma_load_3d(smem_u32(smem + Cfg::OFF_QAUG + s * Cfg::AUG_BYTES), &tmQaug, fb, 0, q0, bh);
                 ++issued;
             }
             mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 2);
@@ -226,6 +241,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             auto qbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_Q + (it % kQStages) * Cfg::KC_STRIDE); };
             auto dobuf = [&](int it) { return smem_u32(smem + Cfg::OFF_DO + (it % kQStages) * Cfg::V_BYTES); };
             // S^T = Kc . Qc^T
+            auto augbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_QAUG + (it % kQStages) * Cfg::AUG_BYTES); };
+            const uint32_t sVaug = smem_u32(smem + Cfg::OFF_VAUG);
+            // S^T = Kc . Qc^T = k.q - cb/2 (centered query codes)
             auto issue_s = [&](int it) {
                 const uint32_t sQ = qbuf(it);
 #pragma unroll
@@ -234,13 +252,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             id_s, ks > 0 ? 1u : 0u);
                 umma_commit(s_full);
             };
-            // dP^T = V . dO^T
+            // dP^T - delta = V . dO^T + [0,0,1,1,..] . [1,1,-delta_hi,-delta_lo,..]^T
             auto issue_dp = [&](int it) {
                 const uint32_t sDO = dobuf(it);
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks)
                     umma_ss(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
                             id_s, ks > 0 ? 1u : 0u);
+                umma_ss(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_s, 1u);
                 umma_commit(dp_full);
             };
             // Issue order per query tile i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}.  tcgen05.mma
@@ -329,7 +348,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int kv = kv0 + j;
         const bool kv_ok = kv < args.N;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-        const float cbj = kv_ok ? args.cb[static_cast<size_t>(bh) * args.Npad + kv] : 0.f;
         const float c2 = args.c2;
         uint8_t* ds_row = smem + Cfg::OFF_DS + wg * (kTile * 128) + j * 128;
         const int sw = j & 7;
@@ -346,21 +364,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             tc_fence_after();
             const float4* Lv = reinterpret_cast<const float4*>(smem + Cfg::OFF_L + s * kTile * 4) + wg * 16;
-            const float4* Dv = reinterpret_cast<const float4*>(smem + Cfg::OFF_DELTA + s * kTile * 4) + wg * 16;
             const bool need_mask = !kv_ok || (qc0 + 64 > args.N) || (CAUSAL && qc0 < kv0 + kTile);
+            // P^T = 2^(c2 * (k.q - cb/2) - L_i): both TMEM loads in flight before one wait
             float p[64];
-#pragma unroll
-            for (int c = 0; c < 64; c += 32) {
-                uint32_t rr[32];
-                tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + c, rr);
+            {
+                uint32_t rr[64];
+                tmem_ld32(lane_base + Cfg::TM_S + wg * 64, rr);
+                tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + 32, rr + 32);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 L = Lv[(c + i) / 4];
-                    p[c + i] = ex2(fmaf(u2f(rr[i]), c2, -cbj) - L.x);
-                    p[c + i + 1] = ex2(fmaf(u2f(rr[i + 1]), c2, -cbj) - L.y);
-                    p[c + i + 2] = ex2(fmaf(u2f(rr[i + 2]), c2, -cbj) - L.z);
-                    p[c + i + 3] = ex2(fmaf(u2f(rr[i + 3]), c2, -cbj) - L.w);
+                for (int i = 0; i < 64; i += 4) {
+                    const float4 L = Lv[i / 4];
+                    p[i] = ex2(fmaf(u2f(rr[i]), c2, -L.x));
+                    p[i + 1] = ex2(fmaf(u2f(rr[i + 1]), c2, -L.y));
+                    p[i + 2] = ex2(fmaf(u2f(rr[i + 2]), c2, -L.z));
+                    p[i + 3] = ex2(fmaf(u2f(rr[i + 3]), c2, -L.w));
                 }
             }
             if (need_mask) {
@@ -389,31 +407,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 break;
             }
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 64; c += 32) {
-                uint32_t rr[32];
-                tmem_ld32(lane_base + Cfg::TM_DP + wg * 64 + c, rr);
+            // dS^T = P^T (dP^T - delta); the MMA already subtracted delta
+            {
+                uint32_t rr[64];
+                tmem_ld32(lane_base + Cfg::TM_DP + wg * 64, rr);
+                tmem_ld32(lane_base + Cfg::TM_DP + wg * 64 + 32, rr + 32);
                 tmem_ld_wait();
-                uint32_t pk[16];
+                uint32_t pk[32];
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 dl = Dv[(c + i) / 4];
-                    const float d0 = p[c + i] * (u2f(rr[i]) - dl.x);
-                    const float d1 = p[c + i + 1] * (u2f(rr[i + 1]) - dl.y);
-                    const float d2 = p[c + i + 2] * (u2f(rr[i + 2]) - dl.z);
-                    const float d3 = p[c + i + 3] * (u2f(rr[i + 3]) - dl.w);
-                    dcb += (d0 + d1) + (d2 + d3);
+                for (int i = 0; i < 64; i += 2) {
+                    const float d0 = p[i] * u2f(rr[i]);
+                    const float d1 = p[i + 1] * u2f(rr[i + 1]);
+                    dcb += d0 + d1;
                     pk[i / 2] = pack_half2(d0, d1);
-                    pk[i / 2 + 1] = pack_half2(d2, d3);
                 }
-                tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + c / 2, pk);
-                // smem copy for the dQ MMA: row j, 16-byte units u = c/8 .. c/8+3, 128B swizzle
+                tmem_st16(lane_base + Cfg::TM_DP + wg * 64, pk);
+                tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + 16, pk + 16);
+                // smem copy for the dQ MMA: row j, 16-byte units u = 0..7, 128-byte swizzle
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int u = c / 8 + k;
+                for (int u = 0; u < 8; ++u)
                     *reinterpret_cast<uint4*>(ds_row + ((u ^ sw) << 4)) =
-                        make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-                }
+                        make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
             }
             tmem_st_wait();
             fence_proxy_async_smem();
@@ -510,9 +524,9 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     using Cfg = BwdCfg<MC, HD>;
     const int BH = s.B * s.H;
     const int Npad = (s.N + kTile - 1) / kTile * kTile;
-    CUtensorMap tQ, tK, tKH, tKL, tV, tDO, tL, tDl;
-    if (p.kdq_hi == nullptr || p.kdq_lo == nullptr)
-        return set_error(MORPHO_ERR_INVALID, "internal: backward needs the centered key codes");
+    CUtensorMap tQ, tK, tKH, tKL, tV, tDO, tL, tQA;
+    if (p.kdq_hi == nullptr || p.kdq_lo == nullptr || io.qaug == nullptr)
+        return set_error(MORPHO_ERR_INVALID, "internal: backward needs the centered key codes and bias slices");
     MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tKH, p.kdq_hi, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
@@ -522,7 +536,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     MORPHO_TRY(make_tmap_3d_f16(&tDO, io.dO, s.D, s.N, s.B, s.D, static_cast<uint64_t>(s.N) * s.D,
                                 HD > 64 ? 64 : HD, kTile));
     MORPHO_TRY(make_tmap_2d_f32(&tL, io.L, BH, Npad, Npad, 1, kTile));
-    MORPHO_TRY(make_tmap_2d_f32(&tDl, io.delta, BH, Npad, Npad, 1, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tQA, io.qaug, 16, s.N, BH, 16, static_cast<uint64_t>(s.N) * 16, 16, kTile));
     BwdArgs a;
     a.N = s.N;
     a.Npad = Npad;
@@ -544,7 +558,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream);
-    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKH, tKL, tV, tDO, tL, tDl, a);
+    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKH, tKL, tV, tDO, tL, tQA, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");
     return MORPHO_OK;
 }

@@ -6,8 +6,9 @@
 //
 // Per KV tile j (128 keys):
 //   MMA warp   : S = Qc . Kc^T   (M=128, N=128, K=cube_m)         -> TMEM cols [0,128)
-//   softmax    : t = 2*scale*log2e * S - cb'_j  (cb' = scale*log2e*cbias, attention.cu:125
-//                with the row-constant query bias moved into lse), masks, row max,
+//                with centered query codes, so S = q.k - cb_j/2 (cb_j = sum_c gate_q k_jc)
+//   softmax    : t = 2*scale*log2e * S = 2*scale*log2e*q.k - cb'_j (attention.cu:125 with
+//                the row-constant query bias moved into lse), masks, row max,
 //                p = 2^(t - m) -> fp16 P                          -> TMEM cols [128,192)
 //   MMA warp   : O += P . V_j    (A = P from TMEM, B = V MN-major) -> TMEM cols [192, ..)
 // The running max is rescaled lazily: O and l are only corrected when the max grows by
@@ -41,13 +42,11 @@ struct FwdCfg {
     static constexpr int Q_BYTES = kTile * MC * 2;
     static constexpr int K_BYTES = kTile * MC * 2;
     static constexpr int V_BYTES = kTile * HD * 2;
-    static constexpr int CB_BYTES = kTile * 4;
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = (Q_BYTES + 1023) / 1024 * 1024;
     static constexpr int K_STRIDE = (K_BYTES + 1023) / 1024 * 1024;
     static constexpr int OFF_V = OFF_K + kKvStages * K_STRIDE;
-    static constexpr int OFF_CB = OFF_V + kKvStages * V_BYTES;
-    static constexpr int OFF_BAR = OFF_CB + kKvStages * CB_BYTES;
+    static constexpr int OFF_BAR = OFF_V + kKvStages * V_BYTES;
     static constexpr int USED = OFF_BAR + 256;
     // hd = 128 needs 512 TMEM columns: keep those CTAs alone on their SM.
     static constexpr int SMEM_BYTES = (HD > 64 && USED + 1024 < 120 * 1024) ? 120 * 1024 : USED + 1024;
@@ -71,8 +70,7 @@ struct FwdArgs {
 template <int MC, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmCB,
-                    const FwdArgs args) {
+                    const __grid_constant__ CUtensorMap tmV, const FwdArgs args) {
     using Cfg = FwdCfg<MC, HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -100,7 +98,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kKvStages; ++s) {
             mbar_init(kv_full0 + 8 * s, 1);
-            mbar_init(kv_empty0 + 8 * s, 1 + 4);  // MMA commit + 4 softmax warps (cb' read)
+            mbar_init(kv_empty0 + 8 * s, 1);  // released by the MMA commit after P.V
         }
         mbar_init(q_full, 1);
         mbar_init(s_full, 1);
@@ -114,7 +112,6 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
-        tma_prefetch_desc(&tmCB);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -146,8 +143,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 const uint32_t fb = kv_full0 + 8 * s;
                 const uint32_t sK = smem_u32(smem + Cfg::OFF_K + s * Cfg::K_STRIDE);
                 const uint32_t sV = smem_u32(smem + Cfg::OFF_V + s * Cfg::V_BYTES);
-                const uint32_t sC = smem_u32(smem + Cfg::OFF_CB + s * Cfg::CB_BYTES);
-                mbar_arrive_expect_tx(fb, Cfg::K_BYTES + Cfg::V_BYTES + Cfg::CB_BYTES);
+                mbar_arrive_expect_tx(fb, Cfg::K_BYTES + Cfg::V_BYTES);
                 tma_load_3d(sK, &tmK, fb, 0, kv0, bh);
                 if (HD > 64) {
                     tma_load_3d(sV, &tmV, fb, 0, kv0, bh);
@@ -155,7 +151,6 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 } else {
                     tma_load_3d(sV, &tmV, fb, 0, kv0, bh);
                 }
-                tma_load_2d(sC, &tmCB, fb, kv0, bh);
                 ++issued;
             }
             // Bounded drain of loads still in flight (abort path, and the Q tile).
@@ -234,6 +229,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         const int q = q0 + r;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
         const float c2 = args.c2;
+        const bool pos = c2 >= 0.f;
         float m_ref = -INFINITY;
         float l = 0.f;
         bool ok = true;
@@ -246,38 +242,32 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 break;
             }
             tc_fence_after();
-            float t[kTile];
+            // S = q.k - cb/2 for the 128 keys of this tile: all four TMEM loads in flight
+            uint32_t sv[kTile];
 #pragma unroll
-            for (int c = 0; c < kTile; c += 32) {
-                uint32_t rr[32];
-                tmem_ld32(lane_base + Cfg::TMEM_S + c, rr);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) t[c + i] = u2f(rr[i]);
-            }
-            const float4* cbv = reinterpret_cast<const float4*>(smem + Cfg::OFF_CB + s * Cfg::CB_BYTES);
-#pragma unroll
-            for (int c = 0; c < kTile; c += 4) {
-                const float4 cb = cbv[c / 4];
-                t[c] = fmaf(t[c], c2, -cb.x);
-                t[c + 1] = fmaf(t[c + 1], c2, -cb.y);
-                t[c + 2] = fmaf(t[c + 2], c2, -cb.z);
-                t[c + 3] = fmaf(t[c + 3], c2, -cb.w);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(kv_empty0 + 8 * s);  // cb' of this stage consumed
+            for (int c = 0; c < kTile; c += 32) tmem_ld32(lane_base + Cfg::TMEM_S + c, sv + c);
+            tmem_ld_wait();
+            // t = c2 * S.  The row max of t is c2 * (max or min of S, by the sign of c2);
+            // masked keys get -inf / +inf so that c2 * S - m is -inf for them.
+            const float masked = pos ? -INFINITY : INFINITY;
             const bool need_mask = (kv0 + kTile > args.N) || (CAUSAL && j == qt);
             if (need_mask) {
 #pragma unroll
                 for (int c = 0; c < kTile; ++c) {
                     const int kv = kv0 + c;
                     const bool drop = kv >= args.N || (CAUSAL && kv > q);
-                    t[c] = drop ? -INFINITY : t[c];
+                    sv[c] = drop ? __float_as_uint(masked) : sv[c];
                 }
             }
-            float mt = t[0];
+            float ms = u2f(sv[0]);
+            if (pos) {
 #pragma unroll
-            for (int c = 1; c < kTile; ++c) mt = fmaxf(mt, t[c]);
+                for (int c = 1; c < kTile; ++c) ms = fmaxf(ms, u2f(sv[c]));
+            } else {
+#pragma unroll
+                for (int c = 1; c < kTile; ++c) ms = fminf(ms, u2f(sv[c]));
+            }
+            const float mt = c2 * ms;
             // Lazy rescale: move the reference max only when the row max grew by > 2^8.
             const bool grow = mt > m_ref + kRescaleThreshold;
             const float m_new = grow ? mt : m_ref;
@@ -306,13 +296,14 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             m_ref = m_new;
             // m_ref is finite here: every row has at least one unmasked key.
             float lsum = 0.f;
+            const float nm = -m_ref;
 #pragma unroll
             for (int c = 0; c < kTile; c += 32) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2(t[c + 2 * i] - m_ref);
-                    const float p1 = ex2(t[c + 2 * i + 1] - m_ref);
+                    const float p0 = ex2(fmaf(u2f(sv[c + 2 * i]), c2, nm));
+                    const float p1 = ex2(fmaf(u2f(sv[c + 2 * i + 1]), c2, nm));
                     lsum += p0 + p1;
                     pk[i] = pack_half2(p0, p1);
                 }
@@ -370,12 +361,11 @@ int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out
     using Cfg = FwdCfg<MC, HD>;
     const int BH = s.B * s.H;
     const int Npad = (s.N + kTile - 1) / kTile * kTile;
-    CUtensorMap tQ, tK, tV, tC;
+    CUtensorMap tQ, tK, tV;
     MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tV, p.v, HD, s.N, BH, HD, static_cast<uint64_t>(s.N) * HD, HD > 64 ? 64 : HD,
                                 kTile));
-    MORPHO_TRY(make_tmap_2d_f32(&tC, p.cb, BH, Npad, Npad, 1, kTile));
     FwdArgs a;
     a.N = s.N;
     a.Npad = Npad;
@@ -391,7 +381,7 @@ int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream);
-    kern<<<grid, kFwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, tC, a);
+    kern<<<grid, kFwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, a);
     MORPHO_LAUNCH_CHECK("attn_fwd");
     return MORPHO_OK;
 }

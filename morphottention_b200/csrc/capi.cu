@@ -83,7 +83,7 @@ void plan_proj(Carve& c, const Shape& s, ProjOut* o) {
 
 struct BwdPlan {
     ProjOut proj;
-    float* delta;
+    __half* qaug;
     float* L;
     float* dq;
     float* dk;
@@ -102,7 +102,7 @@ void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     b->proj.phi = c.take<float>(BH * s.N * s.m);
     b->proj.kdq_hi = c.take<__half>(BH * s.N * s.m);
     b->proj.kdq_lo = c.take<__half>(BH * s.N * s.m);
-    b->delta = c.take<float>(BH * Npad);
+    b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dq = c.take<float>(BH * s.N * s.m);
     b->dk = c.take<float>(BH * s.N * s.m);
@@ -231,12 +231,12 @@ int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const
     const __half* gk = static_cast<const __half*>(gate_k);
     MORPHO_TRY(launch_proj(dev, s, x, wphi, wv, gq, gk, b.proj, st));
     MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse, b.proj.qb,
-                            b.delta, b.L, st));
+                            b.L, b.qaug, st));
     MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
     AttnBwdIO io;
     io.dO = static_cast<const __half*>(grad_out);
     io.L = b.L;
-    io.delta = b.delta;
+    io.qaug = b.qaug;
     io.dcat = b.dcat;
     io.dk = b.dk;
     io.dcb = b.dcb;

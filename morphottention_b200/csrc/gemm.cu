@@ -2,6 +2,7 @@
 // TMA-fed multi-stage shared-memory ring, fp32 accumulator in TMEM) with three
 // epilogues:
 //   * EpiProj  : X @ [W_phi | W_V]   -> sigmoid, gating, bias sums, fp16 codes and V
+//                (query codes centered: gate_q * (phi - 1/2), see ProjOut)
 //                (replaces the per-tile re-projection of project.cuh:16-47 and
 //                attention.cu:102-111, which the reference repeats for every Q block)
 //   * EpiHalf  : dcat @ [W_phi | W_V]^T -> dX fp16  (replaces the fp16 atomics of
@@ -101,7 +102,7 @@ struct EpiProj {
                     const float k0 = gk.x * p0, k1 = gk.y * p1;
                     qb = fmaf(gk.x, q0, fmaf(gk.y, q1, qb));
                     cb = fmaf(gq.x, k0, fmaf(gq.y, k1, cb));
-                    qpk[c / 2] = pack_half2(q0, q1);
+                    qpk[c / 2] = pack_half2(q0 - 0.5f * gq.x, q1 - 0.5f * gq.y);  // centered query code
                     kpk[c / 2] = pack_half2(k0, k1);
                     const float c0 = k0 - 0.5f * gk.x, c1 = k1 - 0.5f * gk.y;  // centered key code
                     const __half2 hi = __floats2half2_rn(c0, c1);

@@ -28,7 +28,10 @@ struct Shape {
 // attention tile is one contiguous box: codes [B*H, N, m], V [B*H, N, hd], biases
 // [B*H, N] pre-multiplied by scale*log2(e).
 struct ProjOut {
-    __half* qc = nullptr;   // gate_q * phi
+    // Centered query codes gate_q * (phi - 1/2).  Since cb_j = sum_c gate_q,c k_jc, the
+    // plain dot product k_j . qc_i equals k_j . q_i - cb_j / 2: the score MMA yields the
+    // column-biased score directly, and dK = dS^T . qc needs no cancelling bias term.
+    __half* qc = nullptr;
     __half* kc = nullptr;   // gate_k * phi
     __half* v = nullptr;    // x @ W_V head slice
     float* qb = nullptr;    // scale*log2e * sum_c gate_k q_c
@@ -59,15 +62,16 @@ int dw_splits(const DeviceInfo& dev, const Shape& s);
 int launch_attn_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* lse,
                     cudaStream_t stream);
 
-// Attention backward (KV-stationary).  Inputs: codes/V/biases, dO, L = lse + qb
-// (log2 domain, without the query bias), delta = rowsum(dO * O).  Outputs: dV into
-// dcat[:, Hp + h*hd + e] (fp16), dk (fp32 [B*H, N, m], = 2*scale * dS^T q),
+// Attention backward (KV-stationary).  Inputs: codes/V/bias slices, dO, L = lse + qb
+// (log2 domain, without the query bias), the query slice qaug.  Outputs: dV into
+// dcat[:, Hp + h*hd + e] (fp16), dk (fp32 [B*H, N, m], = 2*scale * dS^T qc with the
+// centered query codes),
 // dcb (fp32 [B*H, N], = -scale * sum_i dS_ij), and dq (fp32 [B*H, N, m], accumulated
 // with atomics, = 2*scale * dS k; must be zeroed first).
 struct AttnBwdIO {
     const __half* dO;
     const float* L;
-    const float* delta;
+    const __half* qaug;
     __half* dcat;
     float* dk;
     float* dcb;
@@ -76,9 +80,11 @@ struct AttnBwdIO {
 int launch_attn_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnBwdIO& io,
                     cudaStream_t stream);
 
-// delta[bh, n] = sum_e dO * O over the head slice; L[bh, n] = lse + qb.
-int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* delta,
-                 float* L, cudaStream_t stream);
+// Per query row (padded [B*H, Npad] fp32) L = lse + qb, and the query slice of the
+// augmented backward MMAs, fp16 [B*H, N, 16]: [1, 1, -delta (hi), -delta (lo), 0 ...] with
+// delta = sum_e dO * O over the head slice (attention.cu:294-311).
+int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* L,
+                 __half* qaug, cudaStream_t stream);
 
 // dZ = dL/dphi * phi (1 - phi) into dcat[:, h*m + c] and per-block gate partials.
 int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,

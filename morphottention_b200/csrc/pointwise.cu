@@ -1,6 +1,7 @@
 // pointwise.cu -- the memory-bound helpers of the backward:
-//   * delta_kernel  : delta = rowsum(dO * O) per head (attention.cu:294-311) and
-//                     L = lse + qb' (the query bias the forward folded into lse)
+//   * delta_kernel  : delta = rowsum(dO * O) per head (attention.cu:294-311), written as
+//                     the -delta slice of the augmented dP MMA, and L = lse + qb' (the
+//                     query bias the forward folded into lse)
 //   * dz_kernel     : dZ = dL/dphi * phi (1 - phi) for the shared q/k projection and the
 //                     per-block gate-gradient partials (project.cuh:70-85, applied to
 //                     both the key and -- in full mode -- the query side)
@@ -23,7 +24,7 @@ inline int npad_of(int N) { return (N + kTile - 1) / kTile * kTile; }
 // a head spans hd/8 lanes.
 __global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ dO, const __half* __restrict__ O,
                                                     const float* __restrict__ lse, const float* __restrict__ qb,
-                                                    float* __restrict__ delta, float* __restrict__ L, int T, int N,
+                                                    float* __restrict__ L, __half* __restrict__ qaug, int T, int N,
                                                     int Npad, int D, int H, int hd) {
     const int lane = threadIdx.x & 31;
     const int warps_total = gridDim.x * (blockDim.x >> 5);
@@ -52,8 +53,14 @@ __global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ d
             if (chunk < D / 8 && (chunk % lanes_per_head) == 0) {
                 const int h = chunk / lanes_per_head;
                 const size_t bh = static_cast<size_t>(b) * H + h;
-                delta[bh * Npad + n] = acc;
                 L[bh * Npad + n] = lse[bh * N + n] + qb[bh * Npad + n];
+                const __half one = __float2half_rn(1.0f);
+                const __half hi = __float2half_rn(-acc);
+                const __half lo = __float2half_rn(-acc - __half2float(hi));
+                __half2 ones = __halves2half2(one, one), dl = __halves2half2(hi, lo);
+                uint4* qa = reinterpret_cast<uint4*>(qaug + (bh * N + n) * 16);
+                qa[0] = make_uint4(*reinterpret_cast<uint32_t*>(&ones), *reinterpret_cast<uint32_t*>(&dl), 0u, 0u);
+                qa[1] = make_uint4(0u, 0u, 0u, 0u);
             }
         }
     }
@@ -64,7 +71,6 @@ __global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ d
         for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
             const int bh = i / pad;
             const int n = N + (i - bh * pad);
-            delta[static_cast<size_t>(bh) * Npad + n] = 0.f;
             L[static_cast<size_t>(bh) * Npad + n] = 0.f;
         }
     }
@@ -113,15 +119,18 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
                 float dz[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    // dL/dphi = dq*gq + dk*gk + dcb*gq*gk  (query-bias term is identically 0)
-                    float dphi = fmaf(kv[i], g_k[i], db * g_q[i] * g_k[i]);
+                    // dk_c = dk + gate_q*dcb (centered query codes), so
+                    //   dL/dphi = dq*gq + dk*gk + dcb*gq*gk = dq*gq + dk_c*gk
+                    //   d gate_k += dk*phi + dcb*gq*phi = dk_c*phi
+                    //   d gate_q += dq*phi + dcb*gk*phi
+                    // (the query-bias terms are identically 0)
+                    float dphi = kv[i] * g_k[i];
                     if (FULL) dphi = fmaf(qv[i], g_q[i], dphi);
                     dz[i] = dphi * fv[i] * (1.0f - fv[i]);
-                    // d gate_q += dq*phi + dcb*gk*phi ; d gate_k += dk*phi + dcb*gq*phi
                     float gqi = db * g_k[i] * fv[i];
                     if (FULL) gqi = fmaf(qv[i], fv[i], gqi);
                     aq[i] += gqi;
-                    ak[i] += fmaf(kv[i], fv[i], db * g_q[i] * fv[i]);
+                    ak[i] += kv[i] * fv[i];
                 }
                 out = make_uint2(pack_half2(dz[0], dz[1]), pack_half2(dz[2], dz[3]));
             }
@@ -213,12 +222,12 @@ int grid_for(long long work, int per_block, int cap) {
 
 }  // namespace
 
-int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* delta,
-                 float* L, cudaStream_t stream) {
+int launch_delta(const Shape& s, const __half* dO, const __half* O, const float* lse, const float* qb, float* L,
+                 __half* qaug, cudaStream_t stream) {
     const int T = static_cast<int>(s.tokens());
     const int grid = grid_for(T, 8, 148 * 16);
     prof_begin(stream);
-    delta_kernel<<<grid, 256, 0, stream>>>(dO, O, lse, qb, delta, L, T, s.N, npad_of(s.N), s.D, s.H, s.hd);
+    delta_kernel<<<grid, 256, 0, stream>>>(dO, O, lse, qb, L, qaug, T, s.N, npad_of(s.N), s.D, s.H, s.hd);
     MORPHO_LAUNCH_CHECK("delta");
     return MORPHO_OK;
 }

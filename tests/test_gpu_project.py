@@ -32,7 +32,9 @@ def test_project(cuda, cfg):
     BH, N = cfg.B * cfg.H, cfg.N
     cl = cfg.scale * O.LOG2E
     assert O.rel_l2(o["phi"].cpu(), phi.reshape(BH, N, -1)) < 1e-5
-    assert O.rel_l2(o["qc"].cpu().float(), q.reshape(BH, N, -1)) < 1e-3
+    gq = c["gate_q"].view(1, cfg.H, 1, cfg.cube_m)
+    qc = (q - 0.5 * gq).reshape(BH, N, -1)  # centered query codes
+    assert O.rel_l2(o["qc"].cpu().float(), qc) < 2e-3
     assert O.rel_l2(o["kc"].cpu().float(), k.reshape(BH, N, -1)) < 1e-3
     assert O.rel_l2(o["v"].cpu().float(), v.reshape(BH, N, -1)) < 1e-3
     assert O.rel_l2(o["qb"][:, :N].cpu(), cl * qb.reshape(BH, N)) < 1e-5
