@@ -30,7 +30,6 @@ namespace {
 
 constexpr int kBwdThreads = 512;
 constexpr int kTile = 128;
-constexpr int kQStages = 2;
 // Register split (512 threads x 128 at launch = 65536): producer/MMA warpgroup 88, dQ
 // warpgroup 56, the two softmax warpgroups 184 each; 128*88 + 128*56 + 256*184 = 65536.
 constexpr uint32_t kRegsProducer = 88;
@@ -39,14 +38,32 @@ constexpr uint32_t kRegsSoftmax = 184;
 static_assert(128 * kRegsProducer + 128 * kRegsDq + 256 * kRegsSoftmax == 65536, "register split");
 
 template <int MC, int HD>
+struct BwdStages {
+    // Fixed buffers, then as many query-tile stages (Q, dO, bias slice, L) as fit in the
+    // 232448-byte opt-in shared memory, up to 4: the next tiles' loads must be issued well
+    // ahead of the MMA that needs them.
+    static constexpr int KC = kTile * MC * 2;
+    static constexpr int KCS = (KC + 1023) / 1024 * 1024;
+    static constexpr int VB = kTile * HD * 2;
+    static constexpr int FIXED = 3 * KCS + VB + 2 * kTile * 128 + kTile * 32 + kTile * 4 + 256 + 1024;
+    static constexpr int STAGE = KCS + VB + kTile * 32 + kTile * 4;
+    static constexpr int value = FIXED + 4 * STAGE <= 232448 ? 4 : (FIXED + 3 * STAGE <= 232448 ? 3 : 2);
+};
+
+template <int MC, int HD>
 struct BwdCfg {
+    static constexpr int kQStages = BwdStages<MC, HD>::value;
     static constexpr int KC_BYTES = kTile * MC * 2;  // one code tile (K or Q)
     static constexpr int V_BYTES = kTile * HD * 2;   // one V or dO tile
     static constexpr int KC_STRIDE = (KC_BYTES + 1023) / 1024 * 1024;
+    // dQ = dS . [hi | lo]: one MMA with N = 2m when its TMEM columns fit (m <= 32), else
+    // two accumulating N = m passes.
+    static constexpr bool DQ_MERGED = MC <= 32;
+    static constexpr int DQ_COLS = DQ_MERGED ? 2 * MC : MC;
+    static constexpr uint32_t KD_ROW = DQ_MERGED ? 4 * MC : 128;  // bytes per row of one kdq chunk
     static constexpr int OFF_K = 0;
-    static constexpr int OFF_KH = OFF_K + KC_STRIDE;   // centered key codes, hi part (dQ MMA)
-    static constexpr int OFF_KL = OFF_KH + KC_STRIDE;  // centered key codes, lo part
-    static constexpr int OFF_V = OFF_KL + KC_STRIDE;
+    static constexpr int OFF_KD = OFF_K + KC_STRIDE;  // centered key codes [hi | lo] (dQ MMA)
+    static constexpr int OFF_V = OFF_KD + 2 * KC_STRIDE;
     static constexpr int OFF_Q = OFF_V + V_BYTES;
     static constexpr int OFF_DO = OFF_Q + kQStages * KC_STRIDE;
     static constexpr int OFF_DS = OFF_DO + kQStages * V_BYTES;  // 2 chunks x 128 rows x 128 B
@@ -65,9 +82,10 @@ struct BwdCfg {
     static constexpr uint32_t TM_DK = 256 + HD;
     static constexpr uint32_t TM_DQ = 256 + HD + MC;
     static constexpr uint32_t TMEM_COLS = 512;
+    static_assert(TM_DQ + DQ_COLS <= TMEM_COLS, "TMEM budget (dQ)");
     static constexpr uint32_t KC_ROW = MC * 2;
     static constexpr uint32_t V_ROW = (HD > 64 ? 64 : HD) * 2;
-    static_assert(TM_DQ + MC <= TMEM_COLS, "TMEM budget");
+
     static_assert(SMEM_BYTES <= 232448, "smem budget");
 };
 
@@ -97,17 +115,20 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks) {
 template <int MC, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmKH, const __grid_constant__ CUtensorMap tmKL,
+                    const __grid_constant__ CUtensorMap tmKD,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmQaug,
                     const BwdArgs args) {
     using Cfg = BwdCfg<MC, HD>;
+    constexpr int kQStages = Cfg::kQStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,2) q_full, [2,4) q_empty, 4 kv_full, 5 s_full, 6 dp_full, 7 p_full, 8 ds_full,
-    //       9 dq_full, 10 dq_free, 11 ds_smem_free, 12 all_done, 13 drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    // bars: [0,S) q_full, [S,2S) q_empty, then kv_full, s_full, dp_full, p_full, ds_full,
+    //       dq_full, dq_free, ds_smem_free, all_done, drain; TMEM slot after them (256 B total)
+    constexpr int NB = 2 * kQStages + 10;
+    static_assert(NB * 8 + 8 <= 256, "barrier block");
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NB);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int warp = warp_id();
@@ -121,17 +142,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int n_it = args.n_qtiles - i_begin;
 
     const uint32_t q_full0 = smem_u32(bars);
-    const uint32_t q_empty0 = smem_u32(bars + 2);
-    const uint32_t kv_full = smem_u32(bars + 4);
-    const uint32_t s_full = smem_u32(bars + 5);
-    const uint32_t dp_full = smem_u32(bars + 6);
-    const uint32_t p_full = smem_u32(bars + 7);
-    const uint32_t ds_full = smem_u32(bars + 8);
-    const uint32_t dq_full = smem_u32(bars + 9);
-    const uint32_t dq_free = smem_u32(bars + 10);
-    const uint32_t ds_smem_free = smem_u32(bars + 11);
-    const uint32_t all_done = smem_u32(bars + 12);
-    const uint32_t drain = smem_u32(bars + 13);
+    const uint32_t q_empty0 = smem_u32(bars + kQStages);
+    const uint32_t kv_full = smem_u32(bars + 2 * kQStages);
+    const uint32_t s_full = kv_full + 8;
+    const uint32_t dp_full = kv_full + 16;
+    const uint32_t p_full = kv_full + 24;
+    const uint32_t ds_full = kv_full + 32;
+    const uint32_t dq_full = kv_full + 40;
+    const uint32_t dq_free = kv_full + 48;
+    const uint32_t ds_smem_free = kv_full + 56;
+    const uint32_t all_done = kv_full + 64;
+    const uint32_t drain = kv_full + 72;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kQStages; ++s) {
@@ -154,8 +175,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmKH);
-        tma_prefetch_desc(&tmKL);
+        tma_prefetch_desc(&tmKD);
         tma_prefetch_desc(&tmV);
         tma_prefetch_desc(&tmDO);
         tma_prefetch_desc(&tmL);
@@ -193,8 +213,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
             mbar_arrive_expect_tx(kv_full, 3 * Cfg::KC_BYTES + Cfg::V_BYTES);
             tma_load_3d(sK, &tmK, kv_full, 0, kv0, bh);
-            tma_load_3d(smem_u32(smem + Cfg::OFF_KH), &tmKH, kv_full, 0, kv0, bh);
-            tma_load_3d(smem_u32(smem + Cfg::OFF_KL), &tmKL, kv_full, 0, kv0, bh);
+            if (Cfg::DQ_MERGED) {
+                tma_load_3d(smem_u32(smem + Cfg::OFF_KD), &tmKD, kv_full, 0, kv0, bh);
+            } else {  // two 64-column chunks: hi, lo
+                tma_load_3d(smem_u32(smem + Cfg::OFF_KD), &tmKD, kv_full, 0, kv0, bh);
+                tma_load_3d(smem_u32(smem + Cfg::OFF_KD + Cfg::KC_STRIDE), &tmKD, kv_full, MC, kv0, bh);
+            }
             tma_load_3d(sV, &tmV, kv_full, 0, kv0, bh);
             if (HD > 64) tma_load_3d(sV + kTile * 128, &tmV, kv_full, 64, kv0, bh);
             int issued = 0;
@@ -230,12 +254,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);   // S^T, dP^T
             constexpr uint32_t id_dv = make_idesc_f16(128, HD, false, true);    // dV
             constexpr uint32_t id_mc = make_idesc_f16(128, MC, false, true);    // dK (A in TMEM)
-            constexpr uint32_t id_dq = make_idesc_f16(128, MC, true, true);     // dQ (A MN-major smem)
+            constexpr uint32_t id_dq = make_idesc_f16(128, Cfg::DQ_COLS, true, true);  // dQ (A MN-major smem)
+            constexpr uint32_t kd_sw = swizzle_code_for_row_bytes(Cfg::KD_ROW);
             constexpr uint32_t kc_sw = swizzle_code_for_row_bytes(Cfg::KC_ROW);
             constexpr uint32_t v_sw = swizzle_code_for_row_bytes(Cfg::V_ROW);
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K);
-            const uint32_t sKH = smem_u32(smem + Cfg::OFF_KH);
-            const uint32_t sKL = smem_u32(smem + Cfg::OFF_KL);
+            const uint32_t sKD = smem_u32(smem + Cfg::OFF_KD);
             const uint32_t sV = smem_u32(smem + Cfg::OFF_V);
             const uint32_t sDS = smem_u32(smem + Cfg::OFF_DS);
             auto qbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_Q + (it % kQStages) * Cfg::KC_STRIDE); };
@@ -313,14 +337,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const uint64_t bd = make_sdesc(sQ + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
                     umma_ts(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
                 }
-                // dQ = dS . (k - gate_k/2) as hi + lo fp16 parts, both accumulated in TMEM
+                // dQ = dS . (k - gate_k/2) with the fp16 hi + lo parts: one N = 2m MMA whose
+                // column halves the dQ warps add, or two accumulating N = m passes
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const uint32_t sKd = part == 0 ? sKH : sKL;
+                for (int part = 0; part < (Cfg::DQ_MERGED ? 1 : 2); ++part) {
+                    const uint32_t sKd = sKD + part * Cfg::KC_STRIDE;
 #pragma unroll
                     for (int ks = 0; ks < kTile / 16; ++ks) {
                         const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
-                        const uint64_t bd = make_sdesc(sKd + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
+                        const uint64_t bd = make_sdesc(sKd + ks * 16 * Cfg::KD_ROW, 16, 8 * Cfg::KD_ROW, kd_sw);
                         umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
                     }
                 }
@@ -495,7 +520,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
                 tmem_ld16(lane_base + Cfg::TM_DQ + c, rr);
-                tmem_ld_wait();
+                if (Cfg::DQ_MERGED) {  // add the lo half
+                    uint32_t lo[16];
+                    tmem_ld16(lane_base + Cfg::TM_DQ + MC + c, lo);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(u2f(rr[i]) + u2f(lo[i]));
+                } else {
+                    tmem_ld_wait();
+                }
                 if (c + 16 == MC) {
                     tc_fence_before();
                     __syncwarp();
@@ -524,13 +557,13 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     using Cfg = BwdCfg<MC, HD>;
     const int BH = s.B * s.H;
     const int Npad = (s.N + kTile - 1) / kTile * kTile;
-    CUtensorMap tQ, tK, tKH, tKL, tV, tDO, tL, tQA;
-    if (p.kdq_hi == nullptr || p.kdq_lo == nullptr || io.qaug == nullptr)
+    CUtensorMap tQ, tK, tKD, tV, tDO, tL, tQA;
+    if (p.kdq == nullptr || io.qaug == nullptr)
         return set_error(MORPHO_ERR_INVALID, "internal: backward needs the centered key codes and bias slices");
     MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tK, p.kc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
-    MORPHO_TRY(make_tmap_3d_f16(&tKH, p.kdq_hi, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
-    MORPHO_TRY(make_tmap_3d_f16(&tKL, p.kdq_lo, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
+    MORPHO_TRY(make_tmap_3d_f16(&tKD, p.kdq, 2 * MC, s.N, BH, 2 * MC, static_cast<uint64_t>(s.N) * 2 * MC,
+                                Cfg::DQ_MERGED ? 2 * MC : MC, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tV, p.v, HD, s.N, BH, HD, static_cast<uint64_t>(s.N) * HD, HD > 64 ? 64 : HD,
                                 kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tDO, io.dO, s.D, s.N, s.B, s.D, static_cast<uint64_t>(s.N) * s.D,
@@ -558,7 +591,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream);
-    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKH, tKL, tV, tDO, tL, tQA, a);
+    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKD, tV, tDO, tL, tQA, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");
     return MORPHO_OK;
 }

@@ -100,8 +100,7 @@ void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
     plan_proj(c, s, &b->proj);
     b->proj.phi = c.take<float>(BH * s.N * s.m);
-    b->proj.kdq_hi = c.take<__half>(BH * s.N * s.m);
-    b->proj.kdq_lo = c.take<__half>(BH * s.N * s.m);
+    b->proj.kdq = c.take<__half>(BH * s.N * 2 * s.m);
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dq = c.take<float>(BH * s.N * s.m);

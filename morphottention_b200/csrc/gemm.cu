@@ -122,9 +122,9 @@ struct EpiProj {
                     const size_t brow = static_cast<size_t>(b * p.H + h) * p.Npad + n;  // padded bias rows
                     p.o.qb[brow] = qb * p.c;
                     p.o.cb[brow] = cb * p.c;
-                    if (p.o.kdq_hi != nullptr) {
-                        uint4* dh = reinterpret_cast<uint4*>(p.o.kdq_hi + base * MC);
-                        uint4* dl = reinterpret_cast<uint4*>(p.o.kdq_lo + base * MC);
+                    if (p.o.kdq != nullptr) {
+                        uint4* dh = reinterpret_cast<uint4*>(p.o.kdq + base * (2 * MC));
+                        uint4* dl = dh + MC / 8;
 #pragma unroll
                         for (int i = 0; i < MC / 8; ++i) {
                             dh[i] = make_uint4(hpk[4 * i], hpk[4 * i + 1], hpk[4 * i + 2], hpk[4 * i + 3]);

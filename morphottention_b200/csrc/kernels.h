@@ -38,11 +38,10 @@ struct ProjOut {
     float* cb = nullptr;    // scale*log2e * sum_c gate_q k_c
     float* phi = nullptr;   // optional fp32 phi [B*H, N, m] (backward recompute)
     // Optional (backward): centered key codes k - gate_k/2 split into fp16 hi + lo parts,
-    // [B*H, N, m] each.  dq = dS . k is computed as dS . hi + dS . lo: every row of dS sums
-    // to zero, so the centering term drops out exactly while the fp16 rounding of the large
-    // mean of k no longer leaks into dq.
-    __half* kdq_hi = nullptr;
-    __half* kdq_lo = nullptr;
+    // interleaved per row as [hi (m) | lo (m)], [B*H, N, 2m].  dq = dS . k is computed as
+    // dS . hi + dS . lo: every row of dS sums to zero, so the centering term drops out
+    // exactly while the fp16 rounding of the large mean of k no longer leaks into dq.
+    __half* kdq = nullptr;
 };
 
 // X [T, D] @ [W_phi | W_V] with the sigmoid / gating / bias epilogue.

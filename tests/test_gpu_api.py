@@ -15,6 +15,14 @@ from .helpers import TOL_GRAD, TOL_OUT
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _device_status_clean(cuda):
+    """Every kernel's bounded waits must have finished in time."""
+    yield
+    torch.cuda.synchronize()
+    assert capi.device_status(reset=True) == 0
+
+
 def _module(cfg, inp, dev):
     m = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=dev)
     with torch.no_grad():
