@@ -167,6 +167,20 @@ def _config_dict(cfg, world, per_step_note=None):
     return d
 
 
+def _traffic(kernel, config_name, cfg):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (profiles/traffic.json),
+    scaled from the captured batch to this run's batch; None when not captured."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f).get(kernel)
+        if t is None or t.get("config") != config_name:
+            return None
+        from morphottention_b200.configs import CONFIGS
+        return t["dram_bytes_per_launch"] * cfg.B / CONFIGS[config_name].B
+    except Exception:
+        return None
+
+
 def algorithmic_flops(cfg):
     """Dense-contraction FLOPs per launch of each kernel (recompute included per launch)."""
     m, hd, T = cfg.cube_m, cfg.head_dim, cfg.tokens
@@ -196,6 +210,8 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     cfg = CONFIGS[args.config]
+    if args.batch is not None:
+        cfg = cfg.with_(B=args.batch)
     w = make_inputs(cfg, device="cpu")  # weights: identical on every rank
     if world > 1:
         g = torch.Generator().manual_seed(cfg.seed * 1000 + rank)
@@ -312,7 +328,7 @@ def run_ours(args):
         achieved = flops.get(dom, 0.0) / per_launch_s / 1e12
         peak = peaks["bf16_tflops_sustained"]
         roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None,
+                "frac": achieved / peak, "traffic": _traffic(dom, args.config, cfg),
                 "peak_note": f"{peaks['source']} dense bf16 (sustained, kernel timed inside a step); fp16 rate equal",
                 "flops_per_launch": flops.get(dom, 0.0)}
         if dom in ("attn_bwd", "attn_fwd"):
@@ -347,6 +363,8 @@ def main():
     ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the per-GPU batch (small cases for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
