@@ -129,6 +129,12 @@ MORPHO_API const char* morpho_sm100_last_error(void);
  * the stream.  reset != 0 clears the word after reading it. */
 MORPHO_API int morpho_sm100_device_status(void* stream, int reset, uint32_t* status_out);
 
+/* Failure-path self test (no reference counterpart): launches one kernel whose bounded wait
+ * on a barrier that nothing arrives at gives up after limit_us microseconds (<= 1 s),
+ * records its code (kernel 15, site 1, bit 31) in the device status word and returns.  Read
+ * the word with morpho_sm100_device_status. */
+MORPHO_API int morpho_sm100_selftest_wait_timeout(uint32_t limit_us, void* stream);
+
 /* Number of kernels the last forward / backward call on this thread launched. */
 MORPHO_API int morpho_sm100_last_launch_count(void);
 

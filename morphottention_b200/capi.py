@@ -35,6 +35,7 @@ EXPORTED = (
     "morpho_sm100_last_error",
     "morpho_sm100_device_status",
     "morpho_sm100_last_launch_count",
+    "morpho_sm100_selftest_wait_timeout",
     "morpho_sm100_profile_enable",
     "morpho_sm100_profile_collect",
 )
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_device_status.restype = i32
     L.morpho_sm100_last_launch_count.argtypes = []
     L.morpho_sm100_last_launch_count.restype = i32
+    L.morpho_sm100_selftest_wait_timeout.argtypes = [ctypes.c_uint32, vp]
+    L.morpho_sm100_selftest_wait_timeout.restype = i32
     L.morpho_sm100_profile_enable.argtypes = [i32]
     L.morpho_sm100_profile_enable.restype = None
     L.morpho_sm100_profile_collect.argtypes = [ctypes.c_char_p, i32, ctypes.POINTER(ctypes.c_float),
@@ -216,3 +219,8 @@ def profile_collect(max_kernels: int = 32) -> dict:
         nm = names.raw[i * name_len:(i + 1) * name_len].split(b"\0", 1)[0].decode()
         out[nm] = (float(ms[i]), int(cnt[i]))
     return out
+
+
+def selftest_wait_timeout(limit_us: int = 20000, stream=None) -> None:
+    """Launch the failure-path self test (a bounded wait that is made to run out)."""
+    _check(lib().morpho_sm100_selftest_wait_timeout(int(limit_us), _stream(stream)))

@@ -17,7 +17,7 @@ namespace morpho {
 // ------------------------------------------------------------------------------------
 // Layout of the 32-bit device status word: bits 0-7 kernel id, bits 8-15 wait site,
 // bit 31 "timeout".  The first failing wait wins (atomicCAS from 0).
-enum KernelId : uint32_t { K_GEMM = 1, K_ATTN_FWD = 2, K_ATTN_BWD = 3 };
+enum KernelId : uint32_t { K_GEMM = 1, K_ATTN_FWD = 2, K_ATTN_BWD = 3, K_SELFTEST = 15 };
 constexpr uint32_t STATUS_TIMEOUT = 0x80000000u;
 constexpr uint64_t WAIT_LIMIT_NS = 1000ull * 1000ull * 1000ull;  // 1 s per wait
 
@@ -68,18 +68,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false (and
-// records kernel/site in *status) when WAIT_LIMIT_NS passes first.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* status, uint32_t kernel,
-                                          uint32_t site) {
+// records kernel/site in *status) when limit_ns passes first.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint64_t limit_ns, uint32_t* status,
+                                              uint32_t kernel, uint32_t site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+        if (global_timer_ns() - t0 > limit_ns) {
             report_timeout(status, kernel, site);
             return false;
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* status, uint32_t kernel,
+                                          uint32_t site) {
+    return mbar_wait_for(bar, parity, WAIT_LIMIT_NS, status, kernel, site);
 }
 
 // Warp-uniform variant: every lane waits and the warp agrees on the outcome, so a
