@@ -21,7 +21,7 @@ def _load_c_extension() -> None:
     if not os.path.exists(SHIM_PATH) or not os.path.exists(LIBRARY_PATH):
         raise ImportError(
             f"Could not find the compiled morphottention_b200 extension in {_PKG_DIR} "
-            "(_C.so and libmorpho_sm100.so). Build it with `python -m morphottention_b200.build`.")
+            "(_C.so and libmorpho_sm100.so). Build it with `python morphottention_b200/build.py`.")
     if not hasattr(torch.ops, _NAMESPACE) or not hasattr(getattr(torch.ops, _NAMESPACE), "forward"):
         torch.ops.load_library(SHIM_PATH)
 

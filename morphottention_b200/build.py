@@ -7,7 +7,7 @@ Produces, next to this file:
 * ``_C.so`` -- the torch op shim registering ``torch.ops.morphottention.*``; links
   ``libmorpho_sm100.so`` through an ``$ORIGIN`` rpath.
 
-Run ``python -m morphottention_b200.build`` (or call :func:`build`).  Objects go to
+Run ``python morphottention_b200/build.py`` (or call :func:`build`).  Objects go to
 ``<repo>/_build``; a source is recompiled when it or any header is newer than its object.
 """
 

@@ -62,7 +62,7 @@ def lib() -> ctypes.CDLL:
     if _lib is not None:
         return _lib
     if not os.path.exists(LIBRARY_PATH):
-        raise ImportError(f"{LIBRARY_PATH} is missing; build it with `python -m morphottention_b200.build`")
+        raise ImportError(f"{LIBRARY_PATH} is missing; build it with `python morphottention_b200/build.py`")
     L = ctypes.CDLL(LIBRARY_PATH)
     P = ctypes.POINTER(MorphoProblem)
     vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int

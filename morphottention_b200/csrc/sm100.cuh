@@ -20,6 +20,7 @@ namespace morpho {
 enum KernelId : uint32_t { K_GEMM = 1, K_ATTN_FWD = 2, K_ATTN_BWD = 3, K_SELFTEST = 15 };
 constexpr uint32_t STATUS_TIMEOUT = 0x80000000u;
 constexpr uint64_t WAIT_LIMIT_NS = 1000ull * 1000ull * 1000ull;  // 1 s per wait
+constexpr uint32_t WAIT_PARK_NS = 100u * 1000u;                      // re-check the clock every 0.1 ms
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
@@ -67,6 +68,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but lets the hardware park the thread for up to hint_ns while the
+// phase is incomplete (it resumes as soon as the phase completes), so a waiting warp does
+// not spin and take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_parked(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns false (and
 // records kernel/site in *status) when limit_ns passes first.
 __device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint64_t limit_ns, uint32_t* status,
@@ -74,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uin
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_parked(bar, parity, WAIT_PARK_NS)) return true;
         if (global_timer_ns() - t0 > limit_ns) {
             report_timeout(status, kernel, site);
             return false;
