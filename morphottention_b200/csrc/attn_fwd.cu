@@ -75,8 +75,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, 2S+1 s_full, 2S+2 p_full, 2S+3 o_done, 2S+4 drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kKvStages + 5);
+    // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, 2S+1 s_full, 2S+2 p_full, 2S+3 o_done, 2S+4 drain,
+    //       2S+5 s_free
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kKvStages + 6);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int warp = warp_id();
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     const uint32_t p_full = q_full + 16;
     const uint32_t o_done = q_full + 24;
     const uint32_t drain = q_full + 32;
+    const uint32_t s_free = q_full + 40;  // the softmax warps hold S_j in registers
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kKvStages; ++s) {
@@ -105,6 +107,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         mbar_init(p_full, 4);
         mbar_init(o_done, 1);
         mbar_init(drain, 1);
+        mbar_init(s_free, 4);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -190,20 +193,24 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             }
             for (int j = 0; ok && j < n_kv; ++j) {
                 const int s = j % kKvStages;
-                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5) || *abort_flag) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                // S_{j+1} as soon as the softmax warps have read S_j (its columns are free),
+                // so the next scores are ready when they finish P_j
                 if (j + 1 < n_kv) {
                     const int s1 = (j + 1) % kKvStages;
-                    if (!mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
+                    if (!mbar_wait(s_free, j & 1, args.status, K_ATTN_FWD, 12) ||
+                        !mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6) ||
+                        *abort_flag) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_s(j + 1);
                 }
+                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5) || *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 const uint32_t sV = smem_u32(smem + Cfg::OFF_V + s * Cfg::V_BYTES);
 #pragma unroll
                 for (int ks = 0; ks < kTile / 16; ++ks) {
@@ -247,6 +254,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 #pragma unroll
             for (int c = 0; c < kTile; c += 32) tmem_ld32(lane_base + Cfg::TMEM_S + c, sv + c);
             tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
             // t = c2 * S.  The row max of t is c2 * (max or min of S, by the sign of c2);
             // masked keys get -inf / +inf so that c2 * S - m is -inf for them.
             const float masked = pos ? -INFINITY : INFINITY;
