@@ -227,14 +227,19 @@ def run_ours(args):
     dgq, dgk = torch.empty_like(gq), torch.empty_like(gk)
     bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev) if world > 1 else None
 
+    # the training pair: the forward keeps its projection for the backward (as the
+    # module's autograd Function does)
+    saved = torch.empty(capi.saved_bytes(p), dtype=torch.uint8, device=dev)
+
     def step():
-        capi.forward(p, x, W_phi, gq, gk, W_V, out, lse)
+        capi.forward_save(p, x, W_phi, gq, gk, W_V, out, lse, saved=saved)
         if world > 1:
-            capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, None, None, None, None, dweights_f32=bucket)
+            capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, None, None, None, None,
+                                dweights_f32=bucket)
             dp.allreduce_bucket(bucket, average=False)
             capi.finalize_weight_grads(p, bucket, 1.0 / world, dW_phi, dgq, dgk, dW_V)
         else:
-            capi.backward(p, grad, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
+            capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
 
     def barrier():
         if world > 1:

@@ -82,6 +82,28 @@ MORPHO_API int morpho_sm100_backward(const morpho_problem_t* p, const void* grad
                           const float* lse, void* dX, void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V,
                           float* dweights_f32, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Training pair that keeps the projection between the two passes (no reference
+ * counterpart: the reference recomputes it in the backward, attention.cu:524-576 calling
+ * the same projection as the forward).  morpho_sm100_forward_save is morpho_sm100_forward
+ * that leaves every projection output the backward needs -- codes, values, biases, phi and
+ * the centered hi/lo key codes -- in the caller's `saved` buffer of
+ * morpho_sm100_saved_bytes(p) bytes (no other workspace).  morpho_sm100_backward_saved is
+ * morpho_sm100_backward that reads them from `saved` instead of running the projection
+ * again; its workspace is morpho_sm100_backward_saved_workspace_size(p) bytes.  `saved`
+ * must come from a forward_save call with the same problem, inputs and weights, and stay
+ * untouched in between.  Results are bit-identical to forward + backward. */
+MORPHO_API size_t morpho_sm100_saved_bytes(const morpho_problem_t* p);
+MORPHO_API size_t morpho_sm100_backward_saved_workspace_size(const morpho_problem_t* p);
+MORPHO_API int morpho_sm100_forward_save(const morpho_problem_t* p, const void* X, const void* W_phi,
+                                         const void* gate_q, const void* gate_k, const void* W_V, void* out,
+                                         float* lse, void* saved, size_t saved_bytes, void* stream);
+MORPHO_API int morpho_sm100_backward_saved(const morpho_problem_t* p, const void* grad_out, const void* saved,
+                                           size_t saved_bytes, const void* X, const void* W_phi,
+                                           const void* gate_q, const void* gate_k, const void* W_V,
+                                           const void* out, const float* lse, void* dX, void* dW_phi,
+                                           void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* Forward that allocates nothing, for callers that cannot allocate device memory where
  * they run it (a memory-pressure callback, a server whose memory plan is frozen after
  * start-up, a host language without an allocator binding).  No counterpart in the

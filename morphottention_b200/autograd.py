@@ -4,7 +4,11 @@ Drop-in for the reference's ``torch-ext/morphottention/autograd.py``: the same
 ``MorphoAttention`` constructor (``:101-135``), the same ``MorphoAttentionFunction``
 (``:34-88``) and ``morpho_attention`` (``:143-162``), calling the same
 ``torch.ops.morphottention.forward/backward`` schemas.  Additions: a fake (meta)
-implementation for ``backward`` and :func:`set_grad_mode`.
+implementation for ``backward``, :func:`set_grad_mode`, and -- when a gradient is needed --
+the ``forward_save`` / ``backward_saved`` op pair, which keeps the forward's projection
+(codes, values, biases, phi) for the backward instead of recomputing it.  Gradients are
+bit-identical either way; the kept buffer costs ``morpho_sm100_saved_bytes`` of memory per
+call until the backward runs.
 """
 
 from __future__ import annotations
@@ -30,6 +34,22 @@ def _morpho_forward_fake(X, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, sca
 @torch.library.register_fake(add_op_namespace_prefix("backward"))
 def _morpho_backward_fake(grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, H: int, cube_m: int, scale: float,
                           causal: bool):
+    return [torch.empty_like(X), torch.empty_like(W_phi), torch.empty_like(gate_q), torch.empty_like(gate_k),
+            torch.empty_like(W_V)]
+
+
+@torch.library.register_fake(add_op_namespace_prefix("forward_save"))
+def _morpho_forward_save_fake(X, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool):
+    from . import capi
+    B, N, D = X.shape
+    nbytes = capi.saved_bytes(capi.problem(B, N, D, H, cube_m, scale, causal))
+    return [torch.empty_like(X), X.new_empty((B * H, N), dtype=torch.float32),
+            X.new_empty((nbytes,), dtype=torch.uint8)]
+
+
+@torch.library.register_fake(add_op_namespace_prefix("backward_saved"))
+def _morpho_backward_saved_fake(grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H: int, cube_m: int,
+                                scale: float, causal: bool):
     return [torch.empty_like(X), torch.empty_like(W_phi), torch.empty_like(gate_q), torch.empty_like(gate_k),
             torch.empty_like(W_V)]
 
@@ -69,8 +89,11 @@ class MorphoAttentionFunction(torch.autograd.Function):
         if not x.is_cuda:
             raise ValueError("MorphoAttention expects a CUDA tensor")
         x = x.contiguous()
-        out, lse = ops.forward(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
-        ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse)
+        if any(ctx.needs_input_grad[:5]):
+            out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
+            ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
+        else:
+            out, lse = ops.forward(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
         ctx.H = H
         ctx.cube_m = cube_m
         ctx.scale = scale
@@ -79,10 +102,10 @@ class MorphoAttentionFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, W_phi, gate_q, gate_k, W_V, out, lse = ctx.saved_tensors
+        x, W_phi, gate_q, gate_k, W_V, out, lse, saved = ctx.saved_tensors
         grad_out = grad_out.contiguous()
-        dX, dW_phi, d_gate_q, d_gate_k, dW_V = ops.backward(
-            grad_out, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal)
+        dX, dW_phi, d_gate_q, d_gate_k, dW_V = ops.backward_saved(
+            grad_out, saved, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal)
         return dX, dW_phi, d_gate_q, d_gate_k, dW_V, None, None, None, None
 
 

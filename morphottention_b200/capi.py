@@ -27,6 +27,10 @@ EXPORTED = (
     "morpho_sm100_backward_workspace_size",
     "morpho_sm100_forward",
     "morpho_sm100_backward",
+    "morpho_sm100_saved_bytes",
+    "morpho_sm100_backward_saved_workspace_size",
+    "morpho_sm100_forward_save",
+    "morpho_sm100_backward_saved",
     "morpho_sm100_project",
     "morpho_sm100_forward_noalloc",
     "morpho_sm100_forward_noalloc_max_scratch",
@@ -76,6 +80,14 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_forward.restype = i32
     L.morpho_sm100_backward.argtypes = [P] + [vp] * 14 + [vp, sz, vp]
     L.morpho_sm100_backward.restype = i32
+    L.morpho_sm100_saved_bytes.argtypes = [P]
+    L.morpho_sm100_saved_bytes.restype = sz
+    L.morpho_sm100_backward_saved_workspace_size.argtypes = [P]
+    L.morpho_sm100_backward_saved_workspace_size.restype = sz
+    L.morpho_sm100_forward_save.argtypes = [P] + [vp] * 7 + [vp, sz, vp]
+    L.morpho_sm100_forward_save.restype = i32
+    L.morpho_sm100_backward_saved.argtypes = [P, vp, vp, sz] + [vp] * 13 + [vp, sz, vp]
+    L.morpho_sm100_backward_saved.restype = i32
     L.morpho_sm100_forward_noalloc.argtypes = [P] + [vp] * 7 + [vp]
     L.morpho_sm100_forward_noalloc.restype = i32
     L.morpho_sm100_forward_noalloc_max_scratch.argtypes = []
@@ -160,6 +172,41 @@ def backward(p: MorphoProblem, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse
                                    _ptr(gate_k), _ptr(W_V), _ptr(out), _ptr(lse), _ptr(dX), _ptr(dW_phi),
                                    _ptr(d_gate_q), _ptr(d_gate_k), _ptr(dW_V), _ptr(dweights_f32), _ptr(ws),
                                    ws_bytes, _stream(stream)))
+
+
+def saved_bytes(p: MorphoProblem) -> int:
+    n = int(lib().morpho_sm100_saved_bytes(ctypes.byref(p)))
+    if n == 0:
+        raise MorphoError(MORPHO_ERR_INVALID, last_error())
+    return n
+
+
+def forward_save(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, out, lse, saved=None, stream=None):
+    """Forward that keeps the projection outputs for ``backward_saved``; returns the
+    ``saved`` uint8 CUDA tensor (allocated here when not given)."""
+    import torch
+    n = saved_bytes(p)
+    if saved is None:
+        saved = torch.empty(n, dtype=torch.uint8, device=X.device)
+    _check(lib().morpho_sm100_forward_save(ctypes.byref(p), _ptr(X), _ptr(W_phi), _ptr(gate_q), _ptr(gate_k),
+                                           _ptr(W_V), _ptr(out), _ptr(lse), _ptr(saved), saved.numel(),
+                                           _stream(stream)))
+    return saved
+
+
+def backward_saved(p: MorphoProblem, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi,
+                   d_gate_q, d_gate_k, dW_V, dweights_f32=None, stream=None) -> None:
+    """Backward reading the projection ``forward_save`` kept (no projection recompute)."""
+    import torch
+    L = lib()
+    ws_bytes = L.morpho_sm100_backward_saved_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        raise MorphoError(MORPHO_ERR_INVALID, last_error())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
+    _check(L.morpho_sm100_backward_saved(ctypes.byref(p), _ptr(grad_out), _ptr(saved), saved.numel(), _ptr(X),
+                                         _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V), _ptr(out), _ptr(lse),
+                                         _ptr(dX), _ptr(dW_phi), _ptr(d_gate_q), _ptr(d_gate_k), _ptr(dW_V),
+                                         _ptr(dweights_f32), _ptr(ws), ws_bytes, _stream(stream)))
 
 
 def project(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, stream=None, with_phi=True) -> dict:

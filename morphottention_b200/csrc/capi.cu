@@ -95,12 +95,18 @@ struct BwdPlan {
     int gate_blocks;
 };
 
-void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
+// Every projection output the backward reads (what forward_save keeps).
+void plan_saved(Carve& c, const Shape& s, ProjOut* o) {
+    const size_t BH = static_cast<size_t>(s.B) * s.H;
+    plan_proj(c, s, o);
+    o->phi = c.take<float>(BH * s.N * s.m);
+    o->kdq = c.take<__half>(BH * s.N * 2 * s.m);
+}
+
+// The backward's own buffers, after the projection outputs.
+void plan_bwd_rest(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     const size_t BH = static_cast<size_t>(s.B) * s.H;
     const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
-    plan_proj(c, s, &b->proj);
-    b->proj.phi = c.take<float>(BH * s.N * s.m);
-    b->proj.kdq = c.take<__half>(BH * s.N * 2 * s.m);
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dq = c.take<float>(BH * s.N * s.m);
@@ -113,6 +119,68 @@ void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     b->dw_part = c.take<float>(static_cast<size_t>(b->splits) * s.D * s.Cp());
     b->gate_blocks = dz_gate_blocks(s);
     b->gate_part = c.take<float>(static_cast<size_t>(b->gate_blocks) * 2 * s.Hm());
+}
+
+void plan_bwd(Carve& c, const Shape& s, int sms, BwdPlan* b) {
+    plan_saved(c, s, &b->proj);
+    plan_bwd_rest(c, s, sms, b);
+}
+
+// Argument checks shared by both backward entry points.
+int check_bwd_args(const void* grad_out, const void* X, const void* W_phi, const void* gate_q, const void* gate_k,
+                   const void* W_V, const void* out, const float* lse, void* dX, void* dW_phi, void* d_gate_q,
+                   void* d_gate_k, void* dW_V, float* dweights_f32, void* workspace) {
+    MORPHO_TRY(check_ptr(grad_out, "grad_out"));
+    MORPHO_TRY(check_ptr(X, "X"));
+    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
+    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
+    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
+    MORPHO_TRY(check_ptr(W_V, "W_V"));
+    MORPHO_TRY(check_ptr(out, "out"));
+    MORPHO_TRY(check_ptr(lse, "lse"));
+    MORPHO_TRY(check_ptr(dX, "dX"));
+    if (dweights_f32 != nullptr) {
+        MORPHO_TRY(check_ptr(dweights_f32, "dweights_f32"));
+    } else {
+        MORPHO_TRY(check_ptr(dW_phi, "dW_phi"));
+        MORPHO_TRY(check_ptr(d_gate_q, "d_gate_q"));
+        MORPHO_TRY(check_ptr(d_gate_k, "d_gate_k"));
+        MORPHO_TRY(check_ptr(dW_V, "dW_V"));
+    }
+    MORPHO_TRY(check_ptr(workspace, "workspace"));
+    return MORPHO_OK;
+}
+
+// Everything of the backward after the projection: delta, attention backward, the
+// sigmoid/gate chain rule, dX and dW GEMMs and the weight-gradient reduction.
+int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan& b, const void* grad_out,
+                            const void* X, const void* W_phi, const void* gate_q, const void* gate_k,
+                            const void* W_V, const void* out, const float* lse, void* dX, void* dW_phi,
+                            void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32, cudaStream_t st) {
+    const __half* x = static_cast<const __half*>(X);
+    const __half* wphi = static_cast<const __half*>(W_phi);
+    const __half* wv = static_cast<const __half*>(W_V);
+    const __half* gq = static_cast<const __half*>(gate_q);
+    const __half* gk = static_cast<const __half*>(gate_k);
+    MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse, b.proj.qb,
+                            b.L, b.qaug, st));
+    MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
+    AttnBwdIO io;
+    io.dO = static_cast<const __half*>(grad_out);
+    io.L = b.L;
+    io.qaug = b.qaug;
+    io.dcat = b.dcat;
+    io.dk = b.dk;
+    io.dcb = b.dcb;
+    io.dq = b.dq;
+    MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
+    MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
+    MORPHO_TRY(launch_dx(dev, s, b.dcat, wphi, wv, static_cast<__half*>(dX), st));
+    MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
+    MORPHO_TRY(launch_reduce_weights(s, b.dw_part, b.splits, b.gate_part, b.gate_blocks, dweights_f32,
+                                     static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
+                                     static_cast<__half*>(d_gate_q), static_cast<__half*>(d_gate_k), st));
+    return MORPHO_OK;
 }
 
 // The workspace size depends on the SM count (split-K factor); query the current
@@ -193,24 +261,8 @@ int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const
     reset_launch_count();
     Shape s;
     MORPHO_TRY(validate(p, &s));
-    MORPHO_TRY(check_ptr(grad_out, "grad_out"));
-    MORPHO_TRY(check_ptr(X, "X"));
-    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
-    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
-    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
-    MORPHO_TRY(check_ptr(W_V, "W_V"));
-    MORPHO_TRY(check_ptr(out, "out"));
-    MORPHO_TRY(check_ptr(lse, "lse"));
-    MORPHO_TRY(check_ptr(dX, "dX"));
-    if (dweights_f32 != nullptr) {
-        MORPHO_TRY(check_ptr(dweights_f32, "dweights_f32"));
-    } else {
-        MORPHO_TRY(check_ptr(dW_phi, "dW_phi"));
-        MORPHO_TRY(check_ptr(d_gate_q, "d_gate_q"));
-        MORPHO_TRY(check_ptr(d_gate_k, "d_gate_k"));
-        MORPHO_TRY(check_ptr(dW_V, "dW_V"));
-    }
-    MORPHO_TRY(check_ptr(workspace, "workspace"));
+    MORPHO_TRY(check_bwd_args(grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
+                              dW_V, dweights_f32, workspace));
     DeviceInfo dev;
     MORPHO_TRY(current_device_info(&dev));
     Carve need_c(nullptr);
@@ -223,31 +275,92 @@ int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const
     Carve c(workspace);
     BwdPlan b;
     plan_bwd(c, s, dev.sms, &b);
-    const __half* x = static_cast<const __half*>(X);
-    const __half* wphi = static_cast<const __half*>(W_phi);
-    const __half* wv = static_cast<const __half*>(W_V);
-    const __half* gq = static_cast<const __half*>(gate_q);
-    const __half* gk = static_cast<const __half*>(gate_k);
-    MORPHO_TRY(launch_proj(dev, s, x, wphi, wv, gq, gk, b.proj, st));
-    MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse, b.proj.qb,
-                            b.L, b.qaug, st));
-    MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
-    AttnBwdIO io;
-    io.dO = static_cast<const __half*>(grad_out);
-    io.L = b.L;
-    io.qaug = b.qaug;
-    io.dcat = b.dcat;
-    io.dk = b.dk;
-    io.dcb = b.dcb;
-    io.dq = b.dq;
-    MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
-    MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
-    MORPHO_TRY(launch_dx(dev, s, b.dcat, wphi, wv, static_cast<__half*>(dX), st));
-    MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
-    MORPHO_TRY(launch_reduce_weights(s, b.dw_part, b.splits, b.gate_part, b.gate_blocks, dweights_f32,
-                                     static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
-                                     static_cast<__half*>(d_gate_q), static_cast<__half*>(d_gate_k), st));
+    MORPHO_TRY(launch_proj(dev, s, static_cast<const __half*>(X), static_cast<const __half*>(W_phi),
+                           static_cast<const __half*>(W_V), static_cast<const __half*>(gate_q),
+                           static_cast<const __half*>(gate_k), b.proj, st));
+    return run_backward_after_proj(dev, s, b, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q,
+                                   d_gate_k, dW_V, dweights_f32, st);
+}
+
+size_t morpho_sm100_saved_bytes(const morpho_problem_t* p) {
+    Shape s;
+    if (validate(p, &s) != MORPHO_OK) return 0;
+    Carve c(nullptr);
+    ProjOut o;
+    plan_saved(c, s, &o);
+    return c.off + 256;
+}
+
+size_t morpho_sm100_backward_saved_workspace_size(const morpho_problem_t* p) {
+    Shape s;
+    if (validate(p, &s) != MORPHO_OK) return 0;
+    Carve c(nullptr);
+    BwdPlan b;
+    plan_bwd_rest(c, s, sms_for_sizing(), &b);
+    return c.off + 256;
+}
+
+int morpho_sm100_forward_save(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,
+                              const void* gate_k, const void* W_V, void* out, float* lse, void* saved,
+                              size_t saved_bytes, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(X, "X"));
+    MORPHO_TRY(check_ptr(W_phi, "W_phi"));
+    MORPHO_TRY(check_ptr(gate_q, "gate_q"));
+    MORPHO_TRY(check_ptr(gate_k, "gate_k"));
+    MORPHO_TRY(check_ptr(W_V, "W_V"));
+    MORPHO_TRY(check_ptr(out, "out"));
+    MORPHO_TRY(check_ptr(lse, "lse"));
+    MORPHO_TRY(check_ptr(saved, "saved"));
+    const size_t need = morpho_sm100_saved_bytes(p);
+    if (saved_bytes < need)
+        return set_error(MORPHO_ERR_WORKSPACE, "saved buffer too small: %zu < %zu bytes", saved_bytes, need);
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    Carve c(saved);
+    ProjOut o;
+    plan_saved(c, s, &o);
+    MORPHO_TRY(launch_proj(dev, s, static_cast<const __half*>(X), static_cast<const __half*>(W_phi),
+                           static_cast<const __half*>(W_V), static_cast<const __half*>(gate_q),
+                           static_cast<const __half*>(gate_k), o, st));
+    MORPHO_TRY(launch_attn_fwd(dev, s, o, static_cast<__half*>(out), lse, st));
     return MORPHO_OK;
+}
+
+int morpho_sm100_backward_saved(const morpho_problem_t* p, const void* grad_out, const void* saved,
+                                size_t saved_bytes, const void* X, const void* W_phi, const void* gate_q,
+                                const void* gate_k, const void* W_V, const void* out, const float* lse, void* dX,
+                                void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    reset_launch_count();
+    Shape s;
+    MORPHO_TRY(validate(p, &s));
+    MORPHO_TRY(check_ptr(saved, "saved"));
+    MORPHO_TRY(check_bwd_args(grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
+                              dW_V, dweights_f32, workspace));
+    if (saved_bytes < morpho_sm100_saved_bytes(p))
+        return set_error(MORPHO_ERR_WORKSPACE, "saved buffer too small: %zu < %zu bytes", saved_bytes,
+                         morpho_sm100_saved_bytes(p));
+    DeviceInfo dev;
+    MORPHO_TRY(current_device_info(&dev));
+    Carve need_c(nullptr);
+    BwdPlan need_plan;
+    plan_bwd_rest(need_c, s, dev.sms, &need_plan);
+    if (workspace_bytes < need_c.off + 256)
+        return set_error(MORPHO_ERR_WORKSPACE, "backward workspace too small: %zu < %zu bytes", workspace_bytes,
+                         need_c.off + 256);
+    Carve cs(const_cast<void*>(saved));
+    BwdPlan b;
+    plan_saved(cs, s, &b.proj);
+    Carve c(workspace);
+    plan_bwd_rest(c, s, dev.sms, &b);
+    return run_backward_after_proj(dev, s, b, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q,
+                                   d_gate_k, dW_V, dweights_f32, static_cast<cudaStream_t>(stream));
 }
 
 int morpho_sm100_project(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,

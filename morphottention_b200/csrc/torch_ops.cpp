@@ -5,9 +5,10 @@
 // (packages/morphottention/csrc/cuda/binder.cpp:6-15, csrc/cuda/dispatch.cpp:3-15,
 // csrc/cuda/attention/attention.cpp:9-118).  Differences: a device guard (the reference
 // has none), workspace from the torch caching allocator on the current stream, no
-// zero-fill of the gradient outputs (the kernels overwrite them), and two extra ops:
+// zero-fill of the gradient outputs (the kernels overwrite them), and extra ops:
 // set_grad_mode / get_grad_mode select full gradients (default) or the reference
-// kernel's gradient semantics.
+// kernel's gradient semantics; forward_save / backward_saved keep the projection of the
+// forward for the backward instead of recomputing it (the autograd Function uses them).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -53,9 +54,9 @@ void check_shapes(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor
     TORCH_CHECK(gate_k.dim() == 2 && gate_k.size(0) == H && gate_k.size(1) == cube_m, "gate_k must be [H, cube_m]");
 }
 
-std::vector<at::Tensor> morpho_forward(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
-                                       const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
-                                       double scale, bool causal) {
+std::vector<at::Tensor> forward_impl(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
+                                     const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
+                                     double scale, bool causal, bool save) {
     check(X, "X");
     check(W_phi, "W_phi");
     check(gate_q, "gate_q");
@@ -67,21 +68,40 @@ std::vector<at::Tensor> morpho_forward(const at::Tensor& X, const at::Tensor& W_
     auto out = at::empty_like(X);
     auto lse = at::empty({B * H, N}, X.options().dtype(at::kFloat));
     morpho_problem_t p = problem(X, H, cube_m, scale, causal);
-    const size_t ws_bytes = morpho_sm100_forward_workspace_size(&p);
+    const size_t ws_bytes = save ? morpho_sm100_saved_bytes(&p) : morpho_sm100_forward_workspace_size(&p);
     TORCH_CHECK(ws_bytes > 0, "morphottention forward: unsupported problem: ", morpho_sm100_last_error());
     auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
     auto stream = at::cuda::getCurrentCUDAStream(X.device().index());
-    const int rc = morpho_sm100_forward(&p, X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(),
-                                        W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(), ws.data_ptr(),
-                                        ws_bytes, static_cast<void*>(stream.stream()));
+    const int rc =
+        save ? morpho_sm100_forward_save(&p, X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(),
+                                         W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(), ws.data_ptr(),
+                                         ws_bytes, static_cast<void*>(stream.stream()))
+             : morpho_sm100_forward(&p, X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(),
+                                    W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(), ws.data_ptr(), ws_bytes,
+                                    static_cast<void*>(stream.stream()));
     TORCH_CHECK(rc == MORPHO_OK, "morphottention forward failed (", rc, "): ", morpho_sm100_last_error());
+    if (save) return {out, lse, ws};
     return {out, lse};
 }
 
-std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Tensor& X, const at::Tensor& W_phi,
-                                        const at::Tensor& gate_q, const at::Tensor& gate_k, const at::Tensor& W_V,
-                                        const at::Tensor& out, const at::Tensor& lse, int64_t H, int64_t cube_m,
-                                        double scale, bool causal) {
+std::vector<at::Tensor> morpho_forward(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
+                                       const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
+                                       double scale, bool causal) {
+    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, false);
+}
+
+// As forward, plus a third output: the uint8 buffer of projection outputs that
+// backward_saved reads.
+std::vector<at::Tensor> morpho_forward_save(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
+                                            const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H,
+                                            int64_t cube_m, double scale, bool causal) {
+    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, true);
+}
+
+std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tensor* saved, const at::Tensor& X,
+                                      const at::Tensor& W_phi, const at::Tensor& gate_q, const at::Tensor& gate_k,
+                                      const at::Tensor& W_V, const at::Tensor& out, const at::Tensor& lse, int64_t H,
+                                      int64_t cube_m, double scale, bool causal) {
     TORCH_CHECK(grad_out.is_cuda() && X.is_cuda(), "Gradient output and X must be a CUDA tensors");
     check(grad_out, "grad_out");
     check(X, "X");
@@ -107,17 +127,46 @@ std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Te
     auto d_gate_k = at::empty_like(gate_k);
     auto dW_V = at::empty_like(W_V);
     morpho_problem_t p = problem(X, H, cube_m, scale, causal);
-    const size_t ws_bytes = morpho_sm100_backward_workspace_size(&p);
+    if (saved != nullptr) {
+        TORCH_CHECK(saved->is_cuda() && saved->scalar_type() == at::kByte && saved->is_contiguous(),
+                    "saved must be the contiguous uint8 CUDA tensor forward_save returned");
+        TORCH_CHECK(static_cast<size_t>(saved->numel()) >= morpho_sm100_saved_bytes(&p),
+                    "saved does not match this problem");
+    }
+    const size_t ws_bytes = saved != nullptr ? morpho_sm100_backward_saved_workspace_size(&p)
+                                             : morpho_sm100_backward_workspace_size(&p);
     TORCH_CHECK(ws_bytes > 0, "morphottention backward: unsupported problem: ", morpho_sm100_last_error());
     auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
     auto stream = at::cuda::getCurrentCUDAStream(X.device().index());
-    const int rc = morpho_sm100_backward(&p, grad_out.data_ptr(), X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(),
-                                         gate_k.data_ptr(), W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(),
-                                         dX.data_ptr(), dW_phi.data_ptr(), d_gate_q.data_ptr(), d_gate_k.data_ptr(),
-                                         dW_V.data_ptr(), nullptr, ws.data_ptr(), ws_bytes,
-                                         static_cast<void*>(stream.stream()));
+    const int rc =
+        saved != nullptr
+            ? morpho_sm100_backward_saved(&p, grad_out.data_ptr(), saved->data_ptr(), saved->numel(), X.data_ptr(),
+                                          W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(), W_V.data_ptr(),
+                                          out.data_ptr(), lse.data_ptr<float>(), dX.data_ptr(), dW_phi.data_ptr(),
+                                          d_gate_q.data_ptr(), d_gate_k.data_ptr(), dW_V.data_ptr(), nullptr,
+                                          ws.data_ptr(), ws_bytes, static_cast<void*>(stream.stream()))
+            : morpho_sm100_backward(&p, grad_out.data_ptr(), X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(),
+                                    gate_k.data_ptr(), W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(),
+                                    dX.data_ptr(), dW_phi.data_ptr(), d_gate_q.data_ptr(), d_gate_k.data_ptr(),
+                                    dW_V.data_ptr(), nullptr, ws.data_ptr(), ws_bytes,
+                                    static_cast<void*>(stream.stream()));
     TORCH_CHECK(rc == MORPHO_OK, "morphottention backward failed (", rc, "): ", morpho_sm100_last_error());
     return {dX, dW_phi, d_gate_q, d_gate_k, dW_V};
+}
+
+std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Tensor& X, const at::Tensor& W_phi,
+                                        const at::Tensor& gate_q, const at::Tensor& gate_k, const at::Tensor& W_V,
+                                        const at::Tensor& out, const at::Tensor& lse, int64_t H, int64_t cube_m,
+                                        double scale, bool causal) {
+    return backward_impl(grad_out, nullptr, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal);
+}
+
+std::vector<at::Tensor> morpho_backward_saved(const at::Tensor& grad_out, const at::Tensor& saved, const at::Tensor& X,
+                                              const at::Tensor& W_phi, const at::Tensor& gate_q,
+                                              const at::Tensor& gate_k, const at::Tensor& W_V, const at::Tensor& out,
+                                              const at::Tensor& lse, int64_t H, int64_t cube_m, double scale,
+                                              bool causal) {
+    return backward_impl(grad_out, &saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal);
 }
 
 int64_t set_grad_mode(int64_t mode) {
@@ -136,6 +185,12 @@ TORCH_LIBRARY(morphottention, m) {
     m.def(
         "backward(Tensor grad_out, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
         "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
+    m.def(
+        "forward_save(Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, Tensor W_V, "
+        "int H, int cube_m, float scale, bool causal) -> Tensor[]");
+    m.def(
+        "backward_saved(Tensor grad_out, Tensor saved, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
+        "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
     m.def("set_grad_mode(int mode) -> int", &set_grad_mode);
     m.def("get_grad_mode() -> int", &get_grad_mode);
 }
@@ -143,4 +198,6 @@ TORCH_LIBRARY(morphottention, m) {
 TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {
     m.impl("forward", &morpho_forward);
     m.impl("backward", &morpho_backward);
+    m.impl("forward_save", &morpho_forward_save);
+    m.impl("backward_saved", &morpho_backward_saved);
 }

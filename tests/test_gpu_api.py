@@ -157,3 +157,50 @@ def test_native_library_is_loaded(cuda):
     torch.ops.morphottention.forward(*_args(cfg, inp))
     maps = open("/proc/self/maps").read()
     assert "libmorpho_sm100.so" in maps and "morphottention_b200/_C.so" in maps
+
+
+@pytest.mark.parametrize("cfg", [CONFIGS["c1"], MorphoConfig("saved_causal", 2, 300, 256, 4, 32, 0.7, True, 5),
+                                 MorphoConfig("saved_m64", 1, 256, 512, 4, 64, 1.0, False, 6)],
+                         ids=lambda c: c.name)
+def test_saved_pair_matches_recompute(cuda, cfg):
+    """forward_save + backward_saved (projection kept) give bit-identical results to
+    forward + backward (projection recomputed), through the C ABI and the torch ops."""
+    inp = make_inputs(cfg, device=cuda, random_gates=True, with_grad_out=True)
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+
+    def run(saved_path):
+        out = torch.empty_like(inp["x"])
+        lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=cuda)
+        grads = [torch.empty_like(t) for t in args]
+        if saved_path:
+            saved = capi.forward_save(p, *args, out, lse)
+            assert saved.numel() == capi.saved_bytes(p)
+            capi.backward_saved(p, inp["grad_out"], saved, *args, out, lse, *grads)
+        else:
+            capi.forward(p, *args, out, lse)
+            capi.backward(p, inp["grad_out"], *args, out, lse, *grads)
+        torch.cuda.synchronize()
+        return [out, lse] + grads
+
+    a, b = run(False), run(True)
+    for name, u, v in zip(("out", "lse", "dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), a, b):
+        assert torch.equal(u, v), name
+    o, l, s = torch.ops.morphottention.forward_save(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    assert torch.equal(o, a[0]) and s.dtype == torch.uint8
+    g = torch.ops.morphottention.backward_saved(inp["grad_out"], s, *args, o, l, cfg.H, cfg.cube_m, cfg.scale,
+                                                cfg.causal)
+    for name, u, v in zip(("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), a[2:], g):
+        assert torch.equal(u, v), name
+
+
+def test_saved_buffer_size_is_checked(cuda):
+    cfg = CONFIGS["c1"]
+    inp = make_inputs(cfg, device=cuda, with_grad_out=True)
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=cuda)
+    small = torch.empty(capi.saved_bytes(p) - 4096, dtype=torch.uint8, device=cuda)
+    with pytest.raises(capi.MorphoError, match="saved buffer too small"):
+        capi.forward_save(p, *args, out, lse, saved=small)
