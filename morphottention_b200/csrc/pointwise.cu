@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
                 g_k[i] = __half2float(gk[col0 + i]);
             }
         }
+#pragma unroll 4
         for (int t = t0; t < t1; ++t) {
             uint2 out = make_uint2(0u, 0u);
             if (live) {
@@ -149,19 +150,24 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
 }
 
 // Sum split partials.  Output index space: [dW_phi D*Hm | dW_V D*D | gq Hm | gk Hm].
+// Blocks [0, main_blocks) sum the dW split-K partials, four consecutive outputs per thread
+// (rows of Hm or D are multiples of 16 elements); the remaining blocks give each gate
+// output one warp, whose lanes take every 32nd dz block and combine by a fixed shuffle
+// tree (deterministic).
 __global__ void __launch_bounds__(256) reduce_weights_kernel(const float* __restrict__ part, int splits,
                                                              const float* __restrict__ gate_part, int gate_blocks,
                                                              float* __restrict__ bucket, __half* __restrict__ dW_phi,
                                                              __half* __restrict__ dW_V, __half* __restrict__ dgq,
-                                                             __half* __restrict__ dgk, int D, int Hm, int Hp, int Cp) {
+                                                             __half* __restrict__ dgk, int D, int Hm, int Hp, int Cp,
+                                                             int main_blocks) {
     const long long n_phi = static_cast<long long>(D) * Hm;
     const long long n_v = static_cast<long long>(D) * D;
-    const long long total = n_phi + n_v + 2LL * Hm;
     const long long plane = static_cast<long long>(D) * Cp;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        float acc = 0.f;
-        if (i < n_phi + n_v) {
+    if (static_cast<int>(blockIdx.x) < main_blocks) {
+        const long long quads = (n_phi + n_v) / 4;
+        for (long long qd = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; qd < quads;
+             qd += static_cast<long long>(main_blocks) * blockDim.x) {
+            const long long i = qd * 4;
             long long src;
             if (i < n_phi) {
                 const long long d = i / Hm;
@@ -171,23 +177,41 @@ __global__ void __launch_bounds__(256) reduce_weights_kernel(const float* __rest
                 const long long d = k / D;
                 src = d * Cp + Hp + (k - d * D);
             }
-            for (int z = 0; z < splits; ++z) acc += part[z * plane + src];
-        } else {
-            const long long k = i - n_phi - n_v;
-            const int g = k < Hm ? 0 : 1;
-            const long long col = k - g * Hm;
-            for (int blk = 0; blk < gate_blocks; ++blk) acc += gate_part[(static_cast<long long>(blk) * 2 + g) * Hm + col];
+            float4 acc = *reinterpret_cast<const float4*>(part + src);
+            for (int z = 1; z < splits; ++z) {
+                const float4 v = *reinterpret_cast<const float4*>(part + z * plane + src);
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            if (bucket != nullptr) {
+                *reinterpret_cast<float4*>(bucket + i) = acc;
+            } else {
+                __half* dst = i < n_phi ? dW_phi + i : dW_V + (i - n_phi);
+                *reinterpret_cast<uint2*>(dst) = make_uint2(pack_half2(acc.x, acc.y), pack_half2(acc.z, acc.w));
+            }
         }
-        if (bucket != nullptr) {
-            bucket[i] = acc;
-        } else if (i < n_phi) {
-            dW_phi[i] = __float2half_rn(acc);
-        } else if (i < n_phi + n_v) {
-            dW_V[i - n_phi] = __float2half_rn(acc);
-        } else if (i < n_phi + n_v + Hm) {
-            dgq[i - n_phi - n_v] = __float2half_rn(acc);
-        } else {
-            dgk[i - n_phi - n_v - Hm] = __float2half_rn(acc);
+        return;
+    }
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x - main_blocks) * (blockDim.x >> 5);
+    for (int k = (blockIdx.x - main_blocks) * (blockDim.x >> 5) + (threadIdx.x >> 5); k < 2 * Hm; k += warps) {
+        const int g = k < Hm ? 0 : 1;
+        const int col = k - g * Hm;
+        float acc = 0.f;
+        for (int blk = lane; blk < gate_blocks; blk += 32)
+            acc += gate_part[(static_cast<long long>(blk) * 2 + g) * Hm + col];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) {
+            const long long i = n_phi + n_v + k;
+            if (bucket != nullptr)
+                bucket[i] = acc;
+            else if (g == 0)
+                dgq[col] = __float2half_rn(acc);
+            else
+                dgk[col] = __float2half_rn(acc);
         }
     }
 }
@@ -234,9 +258,13 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
 
 int dz_gate_blocks(const Shape& s) {
     const long long T = s.tokens();
-    // ~64 tokens per block keeps the partial buffer small and the grid several waves deep
-    return grid_for(T, 64, 4096);
+    // ~16 tokens per block: enough blocks (and loads in flight) to cover HBM latency; the
+    // gate partials stay small (blocks x 2 x H*m floats)
+    return grid_for(T, 16, 8192);
 }
+
+// Threads per dz block: one per 4 columns of [0, Hp), a multiple of 32, at most 256.
+int dz_threads(const Shape& s) { return min(256, (s.Hp() / 4 + 31) / 32 * 32); }
 
 int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,
               const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part, int gate_blocks,
@@ -245,10 +273,10 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
     const int tpb = (T + gate_blocks - 1) / gate_blocks;
     prof_begin(stream);
     if (s.grad_mode == MORPHO_GRAD_FULL)
-        dz_kernel<true><<<gate_blocks, 256, 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+        dz_kernel<true><<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
                                                          npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     else
-        dz_kernel<false><<<gate_blocks, 256, 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+        dz_kernel<false><<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
                                                           npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     MORPHO_LAUNCH_CHECK("dz");
     return MORPHO_OK;
@@ -257,11 +285,13 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
 int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, const float* gate_part, int gate_blocks,
                           float* bucket, __half* dW_phi, __half* dW_V, __half* d_gate_q, __half* d_gate_k,
                           cudaStream_t stream) {
-    const long long total = static_cast<long long>(s.D) * (s.Hm() + s.D) + 2LL * s.Hm();
+    const long long quads = static_cast<long long>(s.D) * (s.Hm() + s.D) / 4;
+    const int main_blocks = grid_for(quads, 256, 148 * 8);
+    const int gate_warp_blocks = (2 * s.Hm() + 7) / 8;  // one warp per gate output, 8 warps per block
     prof_begin(stream);
-    reduce_weights_kernel<<<grid_for(total, 256, 148 * 8), 256, 0, stream>>>(
+    reduce_weights_kernel<<<main_blocks + gate_warp_blocks, 256, 0, stream>>>(
         dw_part, splits, gate_part, gate_blocks, bucket, dW_phi, dW_V, d_gate_q, d_gate_k, s.D, s.Hm(), s.Hp(),
-        s.Cp());
+        s.Cp(), main_blocks);
     MORPHO_LAUNCH_CHECK("reduce_weights");
     return MORPHO_OK;
 }
