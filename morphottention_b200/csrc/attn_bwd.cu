@@ -76,11 +76,19 @@ struct BwdCfg {
     static constexpr int OFF_BAR = OFF_DCB + kTile * 4;
     static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
     static constexpr int STAGE_TX = KC_BYTES + V_BYTES + AUG_BYTES + kTile * 4;
+    // TMEM columns: S 128 | [P 64] | dP 128 | dV hd | dK m | dQ.  When the 64 columns fit,
+    // P (fp16) has its own columns, so S_{i+1} can be issued as soon as the softmax warps
+    // have read S_i; otherwise P overwrites the first half of each S half and S_{i+1} waits
+    // for dV_i.
+    static constexpr bool P_SEP = 256 + 64 + HD + MC + DQ_COLS <= 512;
     static constexpr uint32_t TM_S = 0;
-    static constexpr uint32_t TM_DP = 128;
-    static constexpr uint32_t TM_DV = 256;
-    static constexpr uint32_t TM_DK = 256 + HD;
-    static constexpr uint32_t TM_DQ = 256 + HD + MC;
+    static constexpr uint32_t TM_P = 128;  // used when P_SEP
+    static constexpr uint32_t TM_DP = P_SEP ? 192 : 128;
+    static constexpr uint32_t TM_DV = TM_DP + 128;
+    static constexpr uint32_t TM_DK = TM_DV + HD;
+    static constexpr uint32_t TM_DQ = TM_DK + MC;
+    // first TMEM column of query half w's P (64 queries as 32 fp16 pairs)
+    static constexpr uint32_t p_col(int w) { return P_SEP ? TM_P + 32 * w : TM_S + 64 * w; }
     static constexpr uint32_t TMEM_COLS = 512;
     static_assert(TM_DQ + DQ_COLS <= TMEM_COLS, "TMEM budget (dQ)");
     static constexpr uint32_t KC_ROW = MC * 2;
@@ -125,8 +133,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     // bars: [0,S) q_full, [S,2S) q_empty, then kv_full, s_full, dp_full, p_full, ds_full,
-    //       dq_full, dq_free, ds_smem_free, all_done, drain; TMEM slot after them (256 B total)
-    constexpr int NB = 2 * kQStages + 10;
+    //       dq_full, dq_free, ds_smem_free, all_done, drain, s_free, dv_done; TMEM slot after
+    //       them (256 B total)
+    constexpr int NB = 2 * kQStages + 12;
     static_assert(NB * 8 + 8 <= 256, "barrier block");
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NB);
     volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -153,6 +162,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t ds_smem_free = kv_full + 56;
     const uint32_t all_done = kv_full + 64;
     const uint32_t drain = kv_full + 72;
+    const uint32_t s_free = kv_full + 80;   // the softmax warps hold S_i in registers
+    const uint32_t dv_done = kv_full + 88;  // dV_i has read P_i
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kQStages; ++s) {
@@ -169,6 +180,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_init(ds_smem_free, 1);
         mbar_init(all_done, 1);
         mbar_init(drain, 1);
+        mbar_init(s_free, 8);
+        mbar_init(dv_done, 1);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -286,10 +299,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 umma_ss(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_s, 1u);
                 umma_commit(dp_full);
             };
-            // Issue order per query tile i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}.  tcgen05.mma
-            // from one thread execute in order, so S_{i+1} may overwrite the P_i columns it
-            // follows, and dP_{i+1} the dS_i columns; the softmax warps get S_{i+1} while they
-            // are still busy with dS_i.
+            // Issue order per query tile i: S_{i+1} (once the softmax warps hold S_i, when P has
+            // its own columns), dV_i, [S_{i+1} here instead when P overwrites S], dK_i, dQ_i,
+            // dP_{i+1}.  tcgen05.mma from one thread execute in order, so S_{i+1} may overwrite
+            // the P_i columns it follows, and dP_{i+1} the dS_i columns.
             bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
             if (ok && n_it > 0) {
                 ok = mbar_wait(q_full0, 0, args.status, K_ATTN_BWD, 4);
@@ -303,7 +316,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const int s = it % kQStages;
                 const uint32_t sQ = qbuf(it);
                 const uint32_t sDO = dobuf(it);
-                // dV += P^T . dO  (P^T halves live in S columns [0,32) and [64,96))
+                if (Cfg::P_SEP && it + 1 < n_it) {
+                    // S_{i+1} as soon as the softmax warps have read S_i
+                    if (!mbar_wait(s_free, it & 1, args.status, K_ATTN_BWD, 15) ||
+                        !mbar_wait(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1, args.status,
+                                   K_ATTN_BWD, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(it + 1);
+                }
+                // dV += P^T . dO  (P^T of query half w in columns p_col(w) .. +32)
                 if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5) || *abort_flag) {
                     ok = false;
                     break;
@@ -311,11 +335,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kTile / 16; ++ks) {
-                    const uint32_t a = tmem + Cfg::TM_S + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
+                    const uint32_t a = tmem + (ks < 4 ? Cfg::p_col(0) + ks * 8 : Cfg::p_col(1) + (ks - 4) * 8);
                     const uint64_t bd = make_sdesc(sDO + ks * 16 * Cfg::V_ROW, kTile * 128, 8 * Cfg::V_ROW, v_sw);
                     umma_ts(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
                 }
-                if (it + 1 < n_it) {
+                umma_commit(dv_done);
+                if (!Cfg::P_SEP && it + 1 < n_it) {
                     if (!mbar_wait(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1, args.status,
                                    K_ATTN_BWD, 4)) {
                         ok = false;
@@ -397,6 +422,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64, rr);
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + 32, rr + 32);
                 tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free);  // S_{i+1} may overwrite the S columns
 #pragma unroll
                 for (int i = 0; i < 64; i += 4) {
                     const float4 L = Lv[i / 4];
@@ -414,12 +442,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     p[c] = keep ? p[c] : 0.f;
                 }
             }
+            if (Cfg::P_SEP && it > 0) {  // the P columns hold P_{i-1} until dV_{i-1} has read it
+                if (!mbar_wait_warp(dv_done, (it - 1) & 1, args.status, K_ATTN_BWD, 16)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
             {
                 uint32_t pk[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) pk[i] = pack_half2(p[2 * i], p[2 * i + 1]);
-                tmem_st16(lane_base + Cfg::TM_S + wg * 64, pk);
-                tmem_st16(lane_base + Cfg::TM_S + wg * 64 + 16, pk + 16);
+                tmem_st16(lane_base + Cfg::p_col(wg), pk);
+                tmem_st16(lane_base + Cfg::p_col(wg) + 16, pk + 16);
             }
             tmem_st_wait();
             tc_fence_before();
