@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     // bars: [0,S) q_full, [S,2S) q_empty, then kv_full, s_full, dp_full, p_full, ds_full,
-    //       dq_full, dq_free, ds_smem_free, all_done, drain, s_free, dv_done; TMEM slot after
+    //       dq_full, dq_free, (unused), all_done, drain, s_free, dv_done; TMEM slot after
     //       them (256 B total)
     constexpr int NB = 2 * kQStages + 12;
     static_assert(NB * 8 + 8 <= 256, "barrier block");
@@ -159,7 +159,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t ds_full = kv_full + 32;
     const uint32_t dq_full = kv_full + 40;
     const uint32_t dq_free = kv_full + 48;
-    const uint32_t ds_smem_free = kv_full + 56;
     const uint32_t all_done = kv_full + 64;
     const uint32_t drain = kv_full + 72;
     const uint32_t s_free = kv_full + 80;   // the softmax warps hold S_i in registers
@@ -177,7 +176,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_init(ds_full, 8);
         mbar_init(dq_full, 1);
         mbar_init(dq_free, 4);
-        mbar_init(ds_smem_free, 1);
         mbar_init(all_done, 1);
         mbar_init(drain, 1);
         mbar_init(s_free, 8);
@@ -316,11 +314,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const int s = it % kQStages;
                 const uint32_t sQ = qbuf(it);
                 const uint32_t sDO = dobuf(it);
+                // The MMA thread waits on as few barriers as possible: each probe of shared memory
+                // it makes while MMAs are in flight stalls it for about an MMA latency.  The
+                // softmax warps fold the other conditions into their arrivals: s_free(i) also
+                // means "stage i+1 has landed", ds_full(i) also "dQ_{i-1} has been read".
                 if (Cfg::P_SEP && it + 1 < n_it) {
                     // S_{i+1} as soon as the softmax warps have read S_i
-                    if (!mbar_wait(s_free, it & 1, args.status, K_ATTN_BWD, 15) ||
-                        !mbar_wait(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1, args.status,
-                                   K_ATTN_BWD, 4)) {
+                    if (!mbar_wait(s_free, it & 1, args.status, K_ATTN_BWD, 15)) {
                         ok = false;
                         break;
                     }
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     issue_s(it + 1);
                 }
                 // dV += P^T . dO  (P^T of query half w in columns p_col(w) .. +32)
-                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5) || *abort_flag) {
+                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
                     ok = false;
                     break;
                 }
@@ -340,18 +340,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     umma_ts(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(dv_done);
-                if (!Cfg::P_SEP && it + 1 < n_it) {
-                    if (!mbar_wait(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1, args.status,
-                                   K_ATTN_BWD, 4)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    issue_s(it + 1);
-                }
+                if (!Cfg::P_SEP && it + 1 < n_it) issue_s(it + 1);  // stage i+1 landed (see s_free)
                 // dK += dS^T . Qc ;  dQ = dS . Kc
-                if (!mbar_wait(ds_full, it & 1, args.status, K_ATTN_BWD, 6) ||
-                    (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7))) {
+                if (!mbar_wait(ds_full, it & 1, args.status, K_ATTN_BWD, 6)) {
                     ok = false;
                     break;
                 }
@@ -374,8 +365,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                         umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
                     }
                 }
-                umma_commit(dq_full);
-                umma_commit(ds_smem_free);
+                umma_commit(dq_full);  // also: the shared dS tile is free again
                 umma_commit(q_empty0 + 8 * s);
                 if (it + 1 < n_it) issue_dp(it + 1);
             }
@@ -422,9 +412,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64, rr);
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + 32, rr + 32);
                 tmem_ld_wait();
+                // s_free(i) tells the MMA thread both that S_{i+1} may overwrite the S columns
+                // and that the next stage has landed
+                if (it + 1 < n_it && !mbar_wait_warp(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1,
+                                                     args.status, K_ATTN_BWD, 17)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(s_free);  // S_{i+1} may overwrite the S columns
+                if (lane == 0) mbar_arrive(s_free);
 #pragma unroll
                 for (int i = 0; i < 64; i += 4) {
                     const float4 L = Lv[i / 4];
@@ -461,8 +458,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
 
-            if (!mbar_wait_warp(dp_full, it & 1, args.status, K_ATTN_BWD, 11) ||
-                (it > 0 && !mbar_wait_warp(ds_smem_free, (it - 1) & 1, args.status, K_ATTN_BWD, 12))) {
+            if (!mbar_wait_warp(dp_full, it & 1, args.status, K_ATTN_BWD, 11)) {
                 ok = false;
                 break;
             }
@@ -483,7 +479,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64, pk);
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + 16, pk + 16);
-                // smem copy for the dQ MMA: row j, 16-byte units u = 0..7, 128-byte swizzle
+                // smem copy for the dQ MMA: row j, 16-byte units u = 0..7, 128-byte swizzle, once
+                // dQ_{i-1} is done with the tile (dq_full(i-1)) and the dQ warps have read dQ_{i-1}
+                // (dq_free(i-1), which ds_full(i) then tells the MMA thread)
+                if (it > 0 && (!mbar_wait_warp(dq_full, (it - 1) & 1, args.status, K_ATTN_BWD, 12) ||
+                               !mbar_wait_warp(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7))) {
+                    ok = false;
+                    break;
+                }
 #pragma unroll
                 for (int u = 0; u < 8; ++u)
                     *reinterpret_cast<uint4*>(ds_row + ((u ^ sw) << 4)) =
