@@ -10,11 +10,18 @@
 //   * EpiF32   : X^T @ dcat -> fp32 split-K partials of [dW_phi | dW_V]  (replaces the
 //                fp16 atomics of attention.cu:382-390 and project.cuh:89-96)
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
-// warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, one output row per
-// thread).  Operands are fp16 with 128-byte swizzle; A and B may each be K-major or
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2-9 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, one output row per
+// thread; warps 2-5 and 6-9 take the two column halves of a tile when BN >= 128).  Operands are fp16 with 128-byte swizzle; A and B may each be K-major or
 // MN-major, which the instruction descriptor's transpose bits express, so no operand
 // is ever transposed in memory.
+//
+// Persistent: one CTA per SM walks the work items (tile, K split) with a stride of the
+// grid size; the fp32 accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of one tile overlaps the main loop of the next.  Items are numbered with the
+// N tile fastest, so CTAs running at the same time share an A row block in L2.  BN = 256
+// where the shape allows: each MMA then does twice the work of an N = 128 one for the
+// same per-instruction and per-barrier-probe costs of the issuing thread.
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -23,26 +30,28 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // producer, MMA, 8 epilogue warps
 
 enum BMode : int { B_SINGLE = 0, B_SPLIT_N = 1, B_SPLIT_K = 2 };
 
 template <int BN>
 struct GemmCfg {
-    static constexpr int STAGES = BN == 128 ? 3 : 4;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);  // <= 192 KB of ring
     static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024;  // barriers + 1 KB alignment slack
-    static constexpr uint32_t TMEM_COLS = BN;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;                 // double-buffered accumulator
+    static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
 struct GemmArgs {
     int M, N;
     int k_blocks;      // ceil(K / BK)
-    int kb_per_split;  // K blocks handled by one blockIdx.z
+    int kb_per_split;  // K blocks handled by one split
     int b_split;       // B_SPLIT_N: first column of B1; B_SPLIT_K: first K index of B1
+    int tiles_m, tiles_n, splits;
     uint32_t* status;
 };
 
@@ -84,59 +93,67 @@ struct EpiProj {
             for (int hc = 0; hc < BN / MC; ++hc) {
                 const int h = n0 / MC + hc;
                 if (h >= p.H) break;  // pad columns of the last phi tile
-                float zr[MC];
-                tmem_load_cols<MC>(tacc + hc * MC, zr);
+                // the head's MC columns in chunks of CW (bias sums carry over), so that a 64-wide
+                // head does not hold all its columns in registers at once
+                constexpr int CW = MC < 32 ? MC : 32;
                 const __half2* gq2 = reinterpret_cast<const __half2*>(p.gq + h * MC);
                 const __half2* gk2 = reinterpret_cast<const __half2*>(p.gk + h * MC);
+                const size_t base = static_cast<size_t>(b * p.H + h) * p.N + n;
                 float qb = 0.f, cb = 0.f;
-                uint32_t qpk[MC / 2], kpk[MC / 2], hpk[MC / 2], lpk[MC / 2];
 #pragma unroll
-                for (int c = 0; c < MC; c += 2) {
-                    const float2 gq = __half22float2(gq2[c / 2]);
-                    const float2 gk = __half22float2(gk2[c / 2]);
-                    const float p0 = 1.0f / (1.0f + __expf(-zr[c]));
-                    const float p1 = 1.0f / (1.0f + __expf(-zr[c + 1]));
-                    zr[c] = p0;
-                    zr[c + 1] = p1;
-                    const float q0 = gq.x * p0, q1 = gq.y * p1;
-                    const float k0 = gk.x * p0, k1 = gk.y * p1;
-                    qb = fmaf(gk.x, q0, fmaf(gk.y, q1, qb));
-                    cb = fmaf(gq.x, k0, fmaf(gq.y, k1, cb));
-                    qpk[c / 2] = pack_half2(q0 - 0.5f * gq.x, q1 - 0.5f * gq.y);  // centered query code
-                    kpk[c / 2] = pack_half2(k0, k1);
-                    const float c0 = k0 - 0.5f * gk.x, c1 = k1 - 0.5f * gk.y;  // centered key code
-                    const __half2 hi = __floats2half2_rn(c0, c1);
-                    const float2 hf = __half22float2(hi);
-                    hpk[c / 2] = *reinterpret_cast<const uint32_t*>(&hi);
-                    lpk[c / 2] = pack_half2(c0 - hf.x, c1 - hf.y);
+                for (int q = 0; q < MC / CW; ++q) {
+                    float zr[CW];
+                    tmem_load_cols<CW>(tacc + hc * MC + q * CW, zr);
+                    uint32_t qpk[CW / 2], kpk[CW / 2], hpk[CW / 2], lpk[CW / 2];
+#pragma unroll
+                    for (int c = 0; c < CW; c += 2) {
+                        const float2 gq = __half22float2(gq2[(q * CW + c) / 2]);
+                        const float2 gk = __half22float2(gk2[(q * CW + c) / 2]);
+                        const float p0 = 1.0f / (1.0f + __expf(-zr[c]));
+                        const float p1 = 1.0f / (1.0f + __expf(-zr[c + 1]));
+                        zr[c] = p0;
+                        zr[c + 1] = p1;
+                        const float q0 = gq.x * p0, q1 = gq.y * p1;
+                        const float k0 = gk.x * p0, k1 = gk.y * p1;
+                        qb = fmaf(gk.x, q0, fmaf(gk.y, q1, qb));
+                        cb = fmaf(gq.x, k0, fmaf(gq.y, k1, cb));
+                        qpk[c / 2] = pack_half2(q0 - 0.5f * gq.x, q1 - 0.5f * gq.y);  // centered query code
+                        kpk[c / 2] = pack_half2(k0, k1);
+                        const float c0 = k0 - 0.5f * gk.x, c1 = k1 - 0.5f * gk.y;  // centered key code
+                        const __half2 hi = __floats2half2_rn(c0, c1);
+                        const float2 hf = __half22float2(hi);
+                        hpk[c / 2] = *reinterpret_cast<const uint32_t*>(&hi);
+                        lpk[c / 2] = pack_half2(c0 - hf.x, c1 - hf.y);
+                    }
+                    if (live) {
+                        uint4* dq = reinterpret_cast<uint4*>(p.o.qc + base * MC + q * CW);
+                        uint4* dk = reinterpret_cast<uint4*>(p.o.kc + base * MC + q * CW);
+#pragma unroll
+                        for (int i = 0; i < CW / 8; ++i) {
+                            dq[i] = make_uint4(qpk[4 * i], qpk[4 * i + 1], qpk[4 * i + 2], qpk[4 * i + 3]);
+                            dk[i] = make_uint4(kpk[4 * i], kpk[4 * i + 1], kpk[4 * i + 2], kpk[4 * i + 3]);
+                        }
+                        if (p.o.kdq != nullptr) {
+                            uint4* dh = reinterpret_cast<uint4*>(p.o.kdq + base * (2 * MC) + q * CW);
+                            uint4* dl = reinterpret_cast<uint4*>(p.o.kdq + base * (2 * MC) + MC + q * CW);
+#pragma unroll
+                            for (int i = 0; i < CW / 8; ++i) {
+                                dh[i] = make_uint4(hpk[4 * i], hpk[4 * i + 1], hpk[4 * i + 2], hpk[4 * i + 3]);
+                                dl[i] = make_uint4(lpk[4 * i], lpk[4 * i + 1], lpk[4 * i + 2], lpk[4 * i + 3]);
+                            }
+                        }
+                        if (p.o.phi != nullptr) {
+                            float4* dp = reinterpret_cast<float4*>(p.o.phi + base * MC + q * CW);
+#pragma unroll
+                            for (int i = 0; i < CW / 4; ++i)
+                                dp[i] = make_float4(zr[4 * i], zr[4 * i + 1], zr[4 * i + 2], zr[4 * i + 3]);
+                        }
+                    }
                 }
                 if (live) {
-                    const size_t base = static_cast<size_t>(b * p.H + h) * p.N + n;
-                    uint4* dq = reinterpret_cast<uint4*>(p.o.qc + base * MC);
-                    uint4* dk = reinterpret_cast<uint4*>(p.o.kc + base * MC);
-#pragma unroll
-                    for (int i = 0; i < MC / 8; ++i) {
-                        dq[i] = make_uint4(qpk[4 * i], qpk[4 * i + 1], qpk[4 * i + 2], qpk[4 * i + 3]);
-                        dk[i] = make_uint4(kpk[4 * i], kpk[4 * i + 1], kpk[4 * i + 2], kpk[4 * i + 3]);
-                    }
                     const size_t brow = static_cast<size_t>(b * p.H + h) * p.Npad + n;  // padded bias rows
                     p.o.qb[brow] = qb * p.c;
                     p.o.cb[brow] = cb * p.c;
-                    if (p.o.kdq != nullptr) {
-                        uint4* dh = reinterpret_cast<uint4*>(p.o.kdq + base * (2 * MC));
-                        uint4* dl = dh + MC / 8;
-#pragma unroll
-                        for (int i = 0; i < MC / 8; ++i) {
-                            dh[i] = make_uint4(hpk[4 * i], hpk[4 * i + 1], hpk[4 * i + 2], hpk[4 * i + 3]);
-                            dl[i] = make_uint4(lpk[4 * i], lpk[4 * i + 1], lpk[4 * i + 2], lpk[4 * i + 3]);
-                        }
-                    }
-                    if (p.o.phi != nullptr) {
-                        float4* dp = reinterpret_cast<float4*>(p.o.phi + base * MC);
-#pragma unroll
-                        for (int i = 0; i < MC / 4; ++i)
-                            dp[i] = make_float4(zr[4 * i], zr[4 * i + 1], zr[4 * i + 2], zr[4 * i + 3]);
-                    }
                 }
             }
         } else {
@@ -223,37 +240,53 @@ struct EpiF32 {
 // A is M x K, B is K x N (logical).  A_MN: A stored [K, M] (M contiguous), else [M, K].
 // B_MN: B stored [K, N] (N contiguous), else [N, K].
 template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 2)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                 const __grid_constant__ CUtensorMap tmB1, const GemmArgs args, const typename Epi::Params ep) {
     using Cfg = GemmCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
+    // epilogue warps 2..9; with BN >= 128 each of the two warpgroups takes half the columns,
+    // with BN = 64 only warps 2..5 work
+    constexpr int kEpiGroups = BN >= 128 ? 2 : 1;
+    constexpr int kEpiWarps = 4 * kEpiGroups;
+    constexpr int kEpiCols = BN / kEpiGroups;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFFSET);
-    // bars[0..S) full, bars[S..2S) empty, bars[2S] accumulator ready, bars[2S+1] drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+    // bars[0..S) full, bars[S..2S) empty, then acc_full[2], acc_empty[2], drain
+    constexpr int NB = 2 * STAGES + 5;
+    static_assert(NB * 8 + 8 <= 256, "barrier block");
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NB);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM;
-    const int n0 = blockIdx.y * BN;
-    const int kb0 = blockIdx.z * args.kb_per_split;
-    const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
-    const int nkb = kb1 - kb0;
+    const int n_items = args.tiles_m * args.tiles_n * args.splits;
+    const int mn_tiles = args.tiles_m * args.tiles_n;
+    // work item -> (m0, n0, split): N tile fastest, then M tile, then split
+    auto decode = [&](int w, int& m0, int& n0, int& z) {
+        z = w / mn_tiles;
+        const int r = w - z * mn_tiles;
+        const int mt = r / args.tiles_n;
+        m0 = mt * BM;
+        n0 = (r - mt * args.tiles_n) * BN;
+    };
 
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
-    const uint32_t acc_bar = smem_u32(bars + 2 * STAGES);
-    const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 1);
+    const uint32_t acc_full0 = smem_u32(bars + 2 * STAGES);      // + 8 * buffer
+    const uint32_t acc_empty0 = smem_u32(bars + 2 * STAGES + 2);  // + 8 * buffer
+    const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(acc_bar, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(acc_full0 + 8 * a, 1);
+            mbar_init(acc_empty0 + 8 * a, kEpiWarps);
+        }
         mbar_init(drain_bar, 1);
         *abort_flag = 0u;
         fence_barrier_init();
@@ -275,48 +308,50 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % STAGES;
-                if (i >= STAGES) {
-                    if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) & 1) ^ 1, args.status, K_GEMM, 1)) {
+            int g = 0;  // K blocks loaded so far, over all items: ring slot and phase
+            for (int w = blockIdx.x; w < n_items && !*abort_flag; w += gridDim.x) {
+                int m0, n0, z;
+                decode(w, m0, n0, z);
+                const int kb0 = z * args.kb_per_split;
+                const int kb1 = min(args.k_blocks, kb0 + args.kb_per_split);
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (g >= STAGES && !mbar_wait(empty0 + 8 * s, ((g / STAGES) & 1) ^ 1, args.status, K_GEMM, 1)) {
                         *abort_flag = 1u;
                         break;
                     }
-                }
-                if (*abort_flag) break;
-                const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
-                const uint32_t sB = sA + Cfg::A_BYTES;
-                const uint32_t fb = full0 + 8 * s;
-                const int k0 = (kb0 + i) * BK;
-                mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-                if (A_MN) {
-                    tma_load_2d(sA, &tmA, fb, m0, k0);
-                    tma_load_2d(sA + 64 * 128, &tmA, fb, m0 + 64, k0);
-                } else {
-                    tma_load_2d(sA, &tmA, fb, k0, m0);
-                }
-                const CUtensorMap* tb = &tmB0;
-                int bn = n0, bk = k0;
-                if (BMODE == B_SPLIT_N && n0 >= args.b_split) {
-                    tb = &tmB1;
-                    bn = n0 - args.b_split;
-                }
-                if (BMODE == B_SPLIT_K && k0 >= args.b_split) {
-                    tb = &tmB1;
-                    bk = k0 - args.b_split;
-                }
-                if (B_MN) {
+                    const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                    const uint32_t sB = sA + Cfg::A_BYTES;
+                    const uint32_t fb = full0 + 8 * s;
+                    const int k0 = kb * BK;
+                    mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+                    if (A_MN) {
+                        tma_load_2d(sA, &tmA, fb, m0, k0);
+                        tma_load_2d(sA + 64 * 128, &tmA, fb, m0 + 64, k0);
+                    } else {
+                        tma_load_2d(sA, &tmA, fb, k0, m0);
+                    }
+                    const CUtensorMap* tb = &tmB0;
+                    int bn = n0, bk = k0;
+                    if (BMODE == B_SPLIT_N && n0 >= args.b_split) {
+                        tb = &tmB1;
+                        bn = n0 - args.b_split;
+                    }
+                    if (BMODE == B_SPLIT_K && k0 >= args.b_split) {
+                        tb = &tmB1;
+                        bk = k0 - args.b_split;
+                    }
+                    if (B_MN) {
 #pragma unroll
-                    for (int c = 0; c < BN / 64; ++c) tma_load_2d(sB + c * 64 * 128, tb, fb, bn + 64 * c, bk);
-                } else {
-                    tma_load_2d(sB, tb, fb, bk, bn);
+                        for (int c = 0; c < BN / 64; ++c) tma_load_2d(sB + c * 64 * 128, tb, fb, bn + 64 * c, bk);
+                    } else {
+                        tma_load_2d(sB, tb, fb, bk, bn);
+                    }
                 }
-                ++issued;
             }
             // Drain: wait (bounded) for this thread's loads still in flight.
             if (*abort_flag) {
-                for (int i = max(0, issued - STAGES); i < issued; ++i)
+                for (int i = max(0, g - STAGES); i < g; ++i)
                     mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, args.status, K_GEMM, 2);
             }
         }
@@ -325,43 +360,71 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         if (lane == 0) {
             constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN);
             bool ok = true;
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % STAGES;
-                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, args.status, K_GEMM, 3) || *abort_flag) {
-                    *abort_flag = 1u;
+            int g = 0;  // K blocks consumed so far
+            int j = 0;  // items of this CTA so far: accumulator buffer j & 1
+            for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++j) {
+                int m0, n0, z;
+                decode(w, m0, n0, z);
+                const int kb0 = z * args.kb_per_split;
+                const int nkb = min(args.k_blocks, kb0 + args.kb_per_split) - kb0;
+                const int a = j & 1;
+                // the epilogue warps have drained this buffer (its previous use, item j - 2)
+                if (j >= 2 && !mbar_wait(acc_empty0 + 8 * a, ((j >> 1) & 1) ^ 1, args.status, K_GEMM, 6)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
-                const uint32_t sB = sA + Cfg::A_BYTES;
+                const uint32_t dacc = tmem + a * BN;
+                for (int i = 0; i < nkb; ++i, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(full0 + 8 * s, (g / STAGES) & 1, args.status, K_GEMM, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sA = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                    const uint32_t sB = sA + Cfg::A_BYTES;
 #pragma unroll
-                for (int ks = 0; ks < BK / 16; ++ks) {
-                    const uint64_t ad = A_MN ? make_sdesc(sA + ks * 2048, 64 * 128, 1024, SW_128)
-                                             : make_sdesc(sA + ks * 32, 16, 1024, SW_128);
-                    const uint64_t bd = B_MN ? make_sdesc(sB + ks * 2048, 64 * 128, 1024, SW_128)
-                                             : make_sdesc(sB + ks * 32, 16, 1024, SW_128);
-                    umma_ss(tmem, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+                    for (int ks = 0; ks < BK / 16; ++ks) {
+                        const uint64_t ad = A_MN ? make_sdesc(sA + ks * 2048, 64 * 128, 1024, SW_128)
+                                                 : make_sdesc(sA + ks * 32, 16, 1024, SW_128);
+                        const uint64_t bd = B_MN ? make_sdesc(sB + ks * 2048, 64 * 128, 1024, SW_128)
+                                                 : make_sdesc(sB + ks * 32, 16, 1024, SW_128);
+                        umma_ss(dacc, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    umma_commit(empty0 + 8 * s);
                 }
-                umma_commit(empty0 + 8 * s);
+                if (ok) umma_commit(acc_full0 + 8 * a);
             }
-            if (ok) {
-                umma_commit(acc_bar);
-            } else {
+            if (!ok) {
+                *abort_flag = 1u;
                 umma_commit(drain_bar);
                 mbar_wait(drain_bar, 0, args.status, K_GEMM, 4);
+                // release the epilogue warps' next wait on either buffer
+                umma_commit(acc_full0);
+                umma_commit(acc_full0 + 8);
             }
         }
-    } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+    } else if (warp - 2 < kEpiWarps) {
+        // ---------------- epilogue (warps 2..9) ----------------
         const int quad = warp & 3;
-        const int row = m0 + quad * 32 + lane;
-        const bool ok = mbar_wait_warp(acc_bar, 0, args.status, K_GEMM, 5);
-        if (ok && nkb > 0) {
+        const int half = (warp - 2) >> 2;  // column half of the tile
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        int j = 0;
+        for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++j) {
+            int m0, n0, z;
+            decode(w, m0, n0, z);
+            const int a = j & 1;
+            if (!mbar_wait_warp(acc_full0 + 8 * a, (j >> 1) & 1, args.status, K_GEMM, 5) || *abort_flag) {
+                *abort_flag = 1u;
+                break;
+            }
             tc_fence_after();
-            Epi::template run<BN>(ep, tmem + (static_cast<uint32_t>(quad * 32) << 16), row, n0, blockIdx.z);
-        } else if (!ok) {
-            *abort_flag = 1u;
+            Epi::template run<kEpiCols>(ep, tmem + a * BN + half * kEpiCols + lane_off, m0 + quad * 32 + lane,
+                                        n0 + half * kEpiCols, z);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty0 + 8 * a);
         }
     }
 
@@ -375,13 +438,18 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 
 template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
 int run_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1, const GemmArgs& args,
-             const typename Epi::Params& ep, int splits, cudaStream_t stream, const char* name) {
+             const typename Epi::Params& ep, int splits, int sms, cudaStream_t stream, const char* name) {
     auto kern = gemm_kernel<BN, A_MN, B_MN, BMODE, Epi>;
     constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid((args.M + BM - 1) / BM, (args.N + BN - 1) / BN, splits);
+    GemmArgs a = args;
+    a.tiles_m = (args.M + BM - 1) / BM;
+    a.tiles_n = (args.N + BN - 1) / BN;
+    a.splits = splits;
+    const int items = a.tiles_m * a.tiles_n * splits;
+    const int grid = items < sms ? items : sms;  // persistent: at most one CTA per SM
     prof_begin(stream);
-    kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB0, tmB1, args, ep);
+    kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB0, tmB1, a, ep);
     MORPHO_LAUNCH_CHECK(name);
     return MORPHO_OK;
 }
@@ -394,7 +462,8 @@ int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __
                 const __half* gate_q, const __half* gate_k, const ProjOut& o, cudaStream_t stream) {
     const long long T = s.tokens();
     const int Hp = s.Hp();
-    const int BN = (Hp % 128 == 0 && s.D % 128 == 0) ? 128 : 64;
+    // tiles never straddle the phi / V column boundary Hp
+    const int BN = (Hp % 256 == 0 && s.D % 256 == 0) ? 256 : (Hp % 128 == 0 && s.D % 128 == 0) ? 128 : 64;
     CUtensorMap tA, tB0, tB1;
     MORPHO_TRY(make_tmap_2d_f16(&tA, X, T, s.D, s.D, BM, BK));
     MORPHO_TRY(make_tmap_2d_f16(&tB0, W_phi, s.D, s.Hm(), s.Hm(), BK, 64));
@@ -420,14 +489,17 @@ int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __
     p.o = o;
     switch (s.m) {
         case 16:
-            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, stream, "proj")
-                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+            return BN == 256   ? run_gemm<256, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                   : BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                               : run_gemm<64, false, true, B_SPLIT_N, EpiProj<16>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj");
         case 32:
-            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, stream, "proj")
-                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+            return BN == 256   ? run_gemm<256, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                   : BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                               : run_gemm<64, false, true, B_SPLIT_N, EpiProj<32>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj");
         case 64:
-            return BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, stream, "proj")
-                             : run_gemm<64, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, stream, "proj");
+            return BN == 256   ? run_gemm<256, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                   : BN == 128 ? run_gemm<128, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj")
+                               : run_gemm<64, false, true, B_SPLIT_N, EpiProj<64>>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "proj");
         default:
             return set_error(MORPHO_ERR_INVALID, "cube_m %d not supported (16, 32 or 64)", s.m);
     }
@@ -436,7 +508,7 @@ int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __
 int launch_dx(const DeviceInfo& dev, const Shape& s, const __half* dcat, const __half* W_phi, const __half* W_V,
               __half* dX, cudaStream_t stream) {
     const long long T = s.tokens();
-    constexpr int BN = 128;
+    const int BN = s.D % 256 == 0 ? 256 : 128;
     CUtensorMap tA, tB0, tB1;
     MORPHO_TRY(make_tmap_2d_f16(&tA, dcat, T, s.Cp(), s.Cp(), BM, BK));
     // B^T = [W_phi | W_V] viewed as K-major [D rows, K cols]
@@ -454,22 +526,32 @@ int launch_dx(const DeviceInfo& dev, const Shape& s, const __half* dcat, const _
     p.N = s.D;
     p.ld = s.D;
     p.out = dX;
-    return run_gemm<BN, false, false, B_SPLIT_K, EpiHalf>(tA, tB0, tB1, a, p, 1, stream, "dx_gemm");
+    return BN == 256 ? run_gemm<256, false, false, B_SPLIT_K, EpiHalf>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "dx_gemm")
+                     : run_gemm<128, false, false, B_SPLIT_K, EpiHalf>(tA, tB0, tB1, a, p, 1, dev.sms, stream, "dx_gemm");
 }
 
+// N tile of the dW GEMM (its output columns are [0, Cp)).
+int dw_bn(const Shape& s) { return s.Cp() % 256 == 0 ? 256 : 128; }
+
 int dw_splits(const DeviceInfo& dev, const Shape& s) {
-    const int tiles = ((s.D + BM - 1) / BM) * ((s.Cp() + 127) / 128);
+    const int BN = dw_bn(s);
+    const int tiles = ((s.D + BM - 1) / BM) * ((s.Cp() + BN - 1) / BN);
     const int kblocks = static_cast<int>((s.tokens() + BK - 1) / BK);
-    // Aim for about two co-resident CTAs per SM, at least 8 K blocks per split.
-    int splits = (2 * dev.sms + tiles - 1) / tiles;
-    splits = max(1, min(splits, kblocks / 8));
+    // About one work item per SM (persistent CTAs), at least 8 K blocks per split; the
+    // split count is then reduced until no split is empty.
+    int splits = max(1, min(dev.sms / tiles, kblocks / 8));
+    while (splits > 1) {
+        const int per = (kblocks + splits - 1) / splits;
+        if ((kblocks + per - 1) / per == splits) break;
+        --splits;
+    }
     return splits;
 }
 
 int launch_dw(const DeviceInfo& dev, const Shape& s, const __half* X, const __half* dcat, float* part, int splits,
               cudaStream_t stream) {
     const long long T = s.tokens();
-    constexpr int BN = 128;
+    const int BN = dw_bn(s);
     CUtensorMap tA, tB0;
     // A = X^T: stored [T (K), D (M)] -> MN-major boxes of 64 x 64.
     MORPHO_TRY(make_tmap_2d_f16(&tA, X, T, s.D, s.D, BK, 64));
@@ -491,7 +573,8 @@ int launch_dw(const DeviceInfo& dev, const Shape& s, const __half* X, const __ha
     p.N = s.Cp();
     p.ld = s.Cp();
     p.out = part;
-    return run_gemm<BN, true, true, B_SINGLE, EpiF32>(tA, tB0, tB0, a, p, splits, stream, "dw_gemm");
+    return BN == 256 ? run_gemm<256, true, true, B_SINGLE, EpiF32>(tA, tB0, tB0, a, p, splits, dev.sms, stream, "dw_gemm")
+                     : run_gemm<128, true, true, B_SINGLE, EpiF32>(tA, tB0, tB0, a, p, splits, dev.sms, stream, "dw_gemm");
 }
 
 }  // namespace morpho
