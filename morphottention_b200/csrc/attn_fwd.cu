@@ -197,16 +197,17 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 // so the next scores are ready when they finish P_j
                 if (j + 1 < n_kv) {
                     const int s1 = (j + 1) % kKvStages;
+                    // (no abort-flag read here: every shared-memory probe of the MMA thread stalls
+                    // it while MMAs are in flight; a failure elsewhere ends its bounded waits)
                     if (!mbar_wait(s_free, j & 1, args.status, K_ATTN_FWD, 12) ||
-                        !mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6) ||
-                        *abort_flag) {
+                        !mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5) || *abort_flag) {
+                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5)) {
                     ok = false;
                     break;
                 }
