@@ -397,8 +397,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const int s = it % kQStages;
             const int q0 = (i_begin + it) * kTile;
             const int qc0 = q0 + wg * 64;  // first query of this warp group's half
+            // stage i has landed: waited for as "stage i+1" in the previous iteration
             if (!mbar_wait_warp(s_full, it & 1, args.status, K_ATTN_BWD, 9) ||
-                !mbar_wait_warp(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 10)) {
+                (it == 0 && !mbar_wait_warp(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 10))) {
                 ok = false;
                 break;
             }
@@ -480,10 +481,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64, pk);
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + 16, pk + 16);
                 // smem copy for the dQ MMA: row j, 16-byte units u = 0..7, 128-byte swizzle, once
-                // dQ_{i-1} is done with the tile (dq_full(i-1)) and the dQ warps have read dQ_{i-1}
-                // (dq_free(i-1), which ds_full(i) then tells the MMA thread)
-                if (it > 0 && (!mbar_wait_warp(dq_full, (it - 1) & 1, args.status, K_ATTN_BWD, 12) ||
-                               !mbar_wait_warp(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7))) {
+                // the dQ warps have read dQ_{i-1} (dq_free(i-1), which ds_full(i) then tells the
+                // MMA thread).  They arrive only after dq_full(i-1), so dQ_{i-1} is also done
+                // with the tile.
+                if (it > 0 && !mbar_wait_warp(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7)) {
                     ok = false;
                     break;
                 }
