@@ -233,11 +233,9 @@ def run_ours(args):
 
     def step():
         capi.forward_save(p, x, W_phi, gq, gk, W_V, out, lse, saved=saved)
-        if world > 1:
-            capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, None, None, None, None,
-                                dweights_f32=bucket)
-            dp.allreduce_bucket(bucket, average=False)
-            capi.finalize_weight_grads(p, bucket, 1.0 / world, dW_phi, dgq, dgk, dW_V)
+        if world > 1:  # weight-gradient all-reduce overlapped with the dX GEMM
+            dp.backward_allreduce(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V,
+                                  bucket)
         else:
             capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
 
@@ -284,6 +282,9 @@ def run_ours(args):
             mod.W_V.copy_(W_V)
             mod.gate_q.copy_(gq)
             mod.gate_k.copy_(gk)
+        # data parallel: gradients averaged over the ranks inside backward, the all-reduce
+        # overlapped with the dX GEMM
+        model = dp.DataParallelAttention(mod) if world > 1 else mod
         x_host = x.cpu().pin_memory()
         params = list(mod.parameters())
         # Overlapped form, as a prefetching training loop runs: step k+1's host->device input
@@ -315,13 +316,11 @@ def run_ours(args):
                 xd = x_dev[k % 2]
             else:
                 xd = x_host.to(dev, non_blocking=True)
-            o = mod(xd)
+            o = model(xd)
             loss = o.sum(dtype=torch.float32)
             for q in params:
                 q.grad = None
             loss.backward()
-            if world > 1:
-                dp.allreduce_weight_grads(mod)
             if not overlap:
                 return loss.item()
             released[k % 2].record()

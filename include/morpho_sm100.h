@@ -104,6 +104,19 @@ MORPHO_API int morpho_sm100_backward_saved(const morpho_problem_t* p, const void
                                            void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32,
                                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Data-parallel form of morpho_sm100_backward_saved (no reference counterpart: the reference
+ * has no multi-GPU code): the weight gradients go to the fp32 bucket dweights_f32 (required),
+ * which is complete before dX is computed; if bucket_ready (a cudaEvent_t) is non-NULL it is
+ * recorded on the stream at that point, so the caller can all-reduce the bucket on another
+ * stream while the dX GEMM runs, then call morpho_sm100_finalize_weight_grads.  Results are
+ * bit-identical to morpho_sm100_backward_saved with the same bucket. */
+MORPHO_API int morpho_sm100_backward_saved_dp(const morpho_problem_t* p, const void* grad_out, const void* saved,
+                                              size_t saved_bytes, const void* X, const void* W_phi,
+                                              const void* gate_q, const void* gate_k, const void* W_V,
+                                              const void* out, const float* lse, void* dX, float* dweights_f32,
+                                              void* bucket_ready, void* workspace, size_t workspace_bytes,
+                                              void* stream);
+
 /* Forward that allocates nothing, for callers that cannot allocate device memory where
  * they run it (a memory-pressure callback, a server whose memory plan is frozen after
  * start-up, a host language without an allocator binding).  No counterpart in the

@@ -31,6 +31,7 @@ EXPORTED = (
     "morpho_sm100_backward_saved_workspace_size",
     "morpho_sm100_forward_save",
     "morpho_sm100_backward_saved",
+    "morpho_sm100_backward_saved_dp",
     "morpho_sm100_project",
     "morpho_sm100_forward_noalloc",
     "morpho_sm100_forward_noalloc_max_scratch",
@@ -88,6 +89,8 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_forward_save.restype = i32
     L.morpho_sm100_backward_saved.argtypes = [P, vp, vp, sz] + [vp] * 13 + [vp, sz, vp]
     L.morpho_sm100_backward_saved.restype = i32
+    L.morpho_sm100_backward_saved_dp.argtypes = [P, vp, vp, sz] + [vp] * 10 + [vp, sz, vp]
+    L.morpho_sm100_backward_saved_dp.restype = i32
     L.morpho_sm100_forward_noalloc.argtypes = [P] + [vp] * 7 + [vp]
     L.morpho_sm100_forward_noalloc.restype = i32
     L.morpho_sm100_forward_noalloc_max_scratch.argtypes = []
@@ -207,6 +210,27 @@ def backward_saved(p: MorphoProblem, grad_out, saved, X, W_phi, gate_q, gate_k, 
                                          _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V), _ptr(out), _ptr(lse),
                                          _ptr(dX), _ptr(dW_phi), _ptr(d_gate_q), _ptr(d_gate_k), _ptr(dW_V),
                                          _ptr(dweights_f32), _ptr(ws), ws_bytes, _stream(stream)))
+
+
+def backward_saved_dp(p: MorphoProblem, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, dX,
+                      dweights_f32, bucket_ready=None, stream=None) -> None:
+    """Data-parallel ``backward_saved``: the weight gradients go to the fp32 bucket, which is
+    complete before dX; ``bucket_ready`` (a ``torch.cuda.Event``) is recorded at that point."""
+    import torch
+    L = lib()
+    ws_bytes = L.morpho_sm100_backward_saved_workspace_size(ctypes.byref(p))
+    if ws_bytes == 0:
+        raise MorphoError(MORPHO_ERR_INVALID, last_error())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=X.device)
+    ev = None
+    if bucket_ready is not None:
+        if not bucket_ready.cuda_event:  # torch creates the CUDA event on its first record
+            bucket_ready.record()
+        ev = bucket_ready.cuda_event
+    _check(L.morpho_sm100_backward_saved_dp(ctypes.byref(p), _ptr(grad_out), _ptr(saved), saved.numel(), _ptr(X),
+                                            _ptr(W_phi), _ptr(gate_q), _ptr(gate_k), _ptr(W_V), _ptr(out),
+                                            _ptr(lse), _ptr(dX), _ptr(dweights_f32), ev, _ptr(ws), ws_bytes,
+                                            _stream(stream)))
 
 
 def project(p: MorphoProblem, X, W_phi, gate_q, gate_k, W_V, stream=None, with_phi=True) -> dict:

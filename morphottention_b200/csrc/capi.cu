@@ -152,11 +152,14 @@ int check_bwd_args(const void* grad_out, const void* X, const void* W_phi, const
 }
 
 // Everything of the backward after the projection: delta, attention backward, the
-// sigmoid/gate chain rule, dX and dW GEMMs and the weight-gradient reduction.
+// sigmoid/gate chain rule, the weight-gradient chain (dW GEMM, reduction) and then the dX
+// GEMM, so that a data-parallel caller can start the all-reduce of the weight gradients
+// (bucket_ready, recorded in between) while dX runs.
 int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan& b, const void* grad_out,
                             const void* X, const void* W_phi, const void* gate_q, const void* gate_k,
                             const void* W_V, const void* out, const float* lse, void* dX, void* dW_phi,
-                            void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32, cudaStream_t st) {
+                            void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32, cudaStream_t st,
+                            cudaEvent_t bucket_ready = nullptr) {
     const __half* x = static_cast<const __half*>(X);
     const __half* wphi = static_cast<const __half*>(W_phi);
     const __half* wv = static_cast<const __half*>(W_V);
@@ -175,11 +178,12 @@ int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan
     io.dq = b.dq;
     MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
     MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
-    MORPHO_TRY(launch_dx(dev, s, b.dcat, wphi, wv, static_cast<__half*>(dX), st));
     MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
     MORPHO_TRY(launch_reduce_weights(s, b.dw_part, b.splits, b.gate_part, b.gate_blocks, dweights_f32,
                                      static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
                                      static_cast<__half*>(d_gate_q), static_cast<__half*>(d_gate_k), st));
+    if (bucket_ready != nullptr) MORPHO_CUDA_TRY(cudaEventRecord(bucket_ready, st));
+    MORPHO_TRY(launch_dx(dev, s, b.dcat, wphi, wv, static_cast<__half*>(dX), st));
     return MORPHO_OK;
 }
 
@@ -331,11 +335,12 @@ int morpho_sm100_forward_save(const morpho_problem_t* p, const void* X, const vo
     return MORPHO_OK;
 }
 
-int morpho_sm100_backward_saved(const morpho_problem_t* p, const void* grad_out, const void* saved,
-                                size_t saved_bytes, const void* X, const void* W_phi, const void* gate_q,
-                                const void* gate_k, const void* W_V, const void* out, const float* lse, void* dX,
-                                void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+int backward_saved_impl(const morpho_problem_t* p, const void* grad_out, const void* saved, size_t saved_bytes,
+                        const void* X, const void* W_phi, const void* gate_q, const void* gate_k, const void* W_V,
+                        const void* out, const float* lse, void* dX, void* dW_phi, void* d_gate_q, void* d_gate_k,
+                        void* dW_V, float* dweights_f32, void* bucket_ready, void* workspace, size_t workspace_bytes,
+                        void* stream) {
     clear_error();
     reset_launch_count();
     Shape s;
@@ -360,7 +365,32 @@ int morpho_sm100_backward_saved(const morpho_problem_t* p, const void* grad_out,
     Carve c(workspace);
     plan_bwd_rest(c, s, dev.sms, &b);
     return run_backward_after_proj(dev, s, b, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q,
-                                   d_gate_k, dW_V, dweights_f32, static_cast<cudaStream_t>(stream));
+                                   d_gate_k, dW_V, dweights_f32, static_cast<cudaStream_t>(stream),
+                                   static_cast<cudaEvent_t>(bucket_ready));
+}
+}  // namespace
+
+int morpho_sm100_backward_saved(const morpho_problem_t* p, const void* grad_out, const void* saved,
+                                size_t saved_bytes, const void* X, const void* W_phi, const void* gate_q,
+                                const void* gate_k, const void* W_V, const void* out, const float* lse, void* dX,
+                                void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    return backward_saved_impl(p, grad_out, saved, saved_bytes, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi,
+                               d_gate_q, d_gate_k, dW_V, dweights_f32, nullptr, workspace, workspace_bytes, stream);
+}
+
+int morpho_sm100_backward_saved_dp(const morpho_problem_t* p, const void* grad_out, const void* saved,
+                                   size_t saved_bytes, const void* X, const void* W_phi, const void* gate_q,
+                                   const void* gate_k, const void* W_V, const void* out, const float* lse, void* dX,
+                                   float* dweights_f32, void* bucket_ready, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    if (dweights_f32 == nullptr) {
+        clear_error();
+        return set_error(MORPHO_ERR_INVALID, "dweights_f32 is NULL");
+    }
+    return backward_saved_impl(p, grad_out, saved, saved_bytes, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, nullptr,
+                               nullptr, nullptr, nullptr, dweights_f32, bucket_ready, workspace, workspace_bytes,
+                               stream);
 }
 
 int morpho_sm100_project(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,

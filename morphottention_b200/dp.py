@@ -41,3 +41,84 @@ def allreduce_weight_grads(module, group=None, average: bool = True) -> None:
         else:
             p.grad.copy_(g)
         off += n
+
+
+_COMM_STREAMS: dict = {}
+
+
+def _comm_stream(device) -> torch.cuda.Stream:
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    if idx not in _COMM_STREAMS:
+        _COMM_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return _COMM_STREAMS[idx]
+
+
+def backward_allreduce(p, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
+                       dW_V, bucket, group=None, average: bool = True) -> None:
+    """``capi.backward_saved`` for a data-parallel rank, with the weight-gradient all-reduce
+    overlapped with the dX GEMM: the library fills the fp32 ``bucket`` first and records an
+    event; a communication stream waits for it and all-reduces the bucket while dX runs on
+    the current stream, which then waits for the collective and writes the fp16 weight
+    gradients (divided by the world size when ``average``)."""
+    from . import capi
+    cur = torch.cuda.current_stream(X.device)
+    comm = _comm_stream(X.device)
+    ready = torch.cuda.Event()
+    capi.backward_saved_dp(p, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, bucket,
+                           bucket_ready=ready)
+    with torch.cuda.stream(comm):
+        comm.wait_event(ready)
+        dist.all_reduce(bucket, op=dist.ReduceOp.SUM, group=group)
+    cur.wait_stream(comm)
+    bucket.record_stream(comm)
+    alpha = 1.0 / dist.get_world_size(group) if average else 1.0
+    capi.finalize_weight_grads(p, bucket, alpha, dW_phi, d_gate_q, d_gate_k, dW_V)
+
+
+class _DataParallelFunction(torch.autograd.Function):
+    """MorphoAttention whose backward all-reduces the weight gradients, overlapped with dX."""
+
+    @staticmethod
+    def forward(ctx, x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool, group):
+        from ._ops import ops
+        if not x.is_cuda:
+            raise ValueError("MorphoAttention expects a CUDA tensor")
+        x = x.contiguous()
+        out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
+        ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
+        ctx.H, ctx.cube_m, ctx.scale, ctx.causal, ctx.group = H, cube_m, scale, causal, group
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from . import capi
+        from .autograd import GRAD_MODES, get_grad_mode
+        x, W_phi, gate_q, gate_k, W_V, out, lse, saved = ctx.saved_tensors
+        grad_out = grad_out.contiguous()
+        B, N, D = x.shape
+        p = capi.problem(B, N, D, ctx.H, ctx.cube_m, ctx.scale, ctx.causal, grad_mode=GRAD_MODES[get_grad_mode()])
+        dX = torch.empty_like(x)
+        grads = [torch.empty_like(t) for t in (W_phi, gate_q, gate_k, W_V)]
+        bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=x.device)
+        backward_allreduce(p, grad_out, saved, x, W_phi, gate_q, gate_k, W_V, out, lse, dX, *grads, bucket,
+                           group=ctx.group)
+        return (dX, *grads, None, None, None, None, None)
+
+
+class DataParallelAttention(torch.nn.Module):
+    """Wraps a ``MorphoAttention`` for batch-sharded data parallelism: its parameter
+    gradients come out of ``backward`` already averaged over ``group`` (one fp32 bucket per
+    step, all-reduced while the dX GEMM runs), as ``DistributedDataParallel`` would give
+    them.  Every rank must hold the same weights."""
+
+    def __init__(self, module, group=None) -> None:
+        super().__init__()
+        self.module = module
+        self.group = group
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        m = self.module
+        return _DataParallelFunction.apply(x, m.W_phi, m.gate_q, m.gate_k, m.W_V, m.num_heads, m.cube_m, m.scale,
+                                           m.causal, self.group)
