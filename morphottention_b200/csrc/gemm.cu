@@ -60,14 +60,12 @@ struct GemmArgs {
 template <int NC>
 __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
     static_assert(NC % 16 == 0, "columns in multiples of 16");
+    uint32_t r[NC];
 #pragma unroll
-    for (int c = 0; c < NC; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c, r);
-        tmem_ld_wait();
+    for (int c = 0; c < NC; c += 16) tmem_ld16(taddr + c, r + c);
+    tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) out[c + i] = u2f(r[i]);
-    }
+    for (int i = 0; i < NC; ++i) out[i] = u2f(r[i]);
 }
 
 struct ProjParams {
@@ -109,8 +107,8 @@ struct EpiProj {
                     for (int c = 0; c < CW; c += 2) {
                         const float2 gq = __half22float2(gq2[(q * CW + c) / 2]);
                         const float2 gk = __half22float2(gk2[(q * CW + c) / 2]);
-                        const float p0 = 1.0f / (1.0f + __expf(-zr[c]));
-                        const float p1 = 1.0f / (1.0f + __expf(-zr[c + 1]));
+                        const float p0 = __fdividef(1.0f, 1.0f + __expf(-zr[c]));
+                        const float p1 = __fdividef(1.0f, 1.0f + __expf(-zr[c + 1]));
                         zr[c] = p0;
                         zr[c + 1] = p1;
                         const float q0 = gq.x * p0, q1 = gq.y * p1;
@@ -157,13 +155,16 @@ struct EpiProj {
                 }
             }
         } else {
-#pragma unroll 1
+            // the next 32-column chunk's TMEM load is in flight while this one is stored
+            uint32_t rb[2][32];
+            tmem_ld32(tacc, rb[0]);
+            tmem_ld_wait();
+#pragma unroll
             for (int cc = 0; cc < BN / 32; ++cc) {
                 const int g = n0 - p.Hp + cc * 32;  // V column
                 if (g >= p.D) break;
-                uint32_t r[32];
-                tmem_ld32(tacc + cc * 32, r);
-                tmem_ld_wait();
+                const uint32_t* r = rb[cc & 1];
+                if (cc + 1 < BN / 32 && g + 32 < p.D) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
                 if (live) {
                     const int h = g / p.hd;
                     const int e = g - h * p.hd;
@@ -175,6 +176,7 @@ struct EpiProj {
                                            pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
                                            pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
                 }
+                tmem_ld_wait();
             }
         }
     }
@@ -189,13 +191,16 @@ struct EpiHalf {
     using Params = HalfParams;
     template <int BN>
     __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/) {
-#pragma unroll 1
+        // the next 32-column chunk's TMEM load is in flight while this one is stored
+        uint32_t rb[2][32];
+        tmem_ld32(tacc, rb[0]);
+        tmem_ld_wait();
+#pragma unroll
         for (int cc = 0; cc < BN / 32; ++cc) {
             const int col = n0 + cc * 32;
             if (col >= p.N) break;
-            uint32_t r[32];
-            tmem_ld32(tacc + cc * 32, r);
-            tmem_ld_wait();
+            const uint32_t* r = rb[cc & 1];
+            if (cc + 1 < BN / 32 && col + 32 < p.N) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
             if (row < p.M) {
                 uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ld + col);
 #pragma unroll
@@ -205,6 +210,7 @@ struct EpiHalf {
                                         pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
                                         pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
             }
+            tmem_ld_wait();
         }
     }
 };
@@ -218,19 +224,23 @@ struct EpiF32 {
     using Params = F32Params;
     template <int BN>
     __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int z) {
-#pragma unroll 1
+        // the next 32-column chunk's TMEM load is in flight while this one is stored
+        uint32_t rb[2][32];
+        tmem_ld32(tacc, rb[0]);
+        tmem_ld_wait();
+#pragma unroll
         for (int cc = 0; cc < BN / 32; ++cc) {
             const int col = n0 + cc * 32;
             if (col >= p.N) break;
-            uint32_t r[32];
-            tmem_ld32(tacc + cc * 32, r);
-            tmem_ld_wait();
+            const uint32_t* r = rb[cc & 1];
+            if (cc + 1 < BN / 32 && col + 32 < p.N) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
             if (row < p.M) {
                 float4* dst = reinterpret_cast<float4*>(p.out + (static_cast<size_t>(z) * p.M + row) * p.ld + col);
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                     dst[i] = make_float4(u2f(r[4 * i]), u2f(r[4 * i + 1]), u2f(r[4 * i + 2]), u2f(r[4 * i + 3]));
             }
+            tmem_ld_wait();
         }
     }
 };
