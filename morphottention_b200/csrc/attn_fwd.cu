@@ -270,13 +270,29 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     sv[c] = drop ? __float_as_uint(masked) : sv[c];
                 }
             }
-            float ms = u2f(sv[0]);
-            if (pos) {
+            // row max (min) with the three-input max.f32 / min.f32 of sm_100: four chains of 16
+            float ms;
+            {
+                float a0 = u2f(sv[0]), a1 = u2f(sv[1]), a2 = u2f(sv[2]), a3 = u2f(sv[3]);
+                if (pos) {
 #pragma unroll
-                for (int c = 1; c < kTile; ++c) ms = fmaxf(ms, u2f(sv[c]));
-            } else {
+                    for (int c = 4; c < kTile; c += 8) {
+                        a0 = fmax3(a0, u2f(sv[c]), u2f(sv[c + 1]));
+                        a1 = fmax3(a1, u2f(sv[c + 2]), u2f(sv[c + 3]));
+                        if (c + 4 < kTile) a2 = fmax3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
+                        if (c + 6 < kTile) a3 = fmax3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
+                    }
+                    ms = fmax3(a0, a1, fmaxf(a2, a3));
+                } else {
 #pragma unroll
-                for (int c = 1; c < kTile; ++c) ms = fminf(ms, u2f(sv[c]));
+                    for (int c = 4; c < kTile; c += 8) {
+                        a0 = fmin3(a0, u2f(sv[c]), u2f(sv[c + 1]));
+                        a1 = fmin3(a1, u2f(sv[c + 2]), u2f(sv[c + 3]));
+                        if (c + 4 < kTile) a2 = fmin3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
+                        if (c + 6 < kTile) a3 = fmin3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
+                    }
+                    ms = fmin3(a0, a1, fminf(a2, a3));
+                }
             }
             const float mt = c2 * ms;
             // Lazy rescale: move the reference max only when the row max grew by > 2^8.

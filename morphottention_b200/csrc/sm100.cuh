@@ -294,6 +294,18 @@ __device__ __forceinline__ void regs_inc() {
 // ------------------------------------------------------------------------------------
 // small math / packing helpers
 // ------------------------------------------------------------------------------------
+// Three-input max / min (max.f32 / min.f32 with three sources, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
