@@ -44,6 +44,12 @@ extern "C" {
 #define MORPHO_ERR_DEVICE 4    /* current device is not sm_100 */
 #define MORPHO_ERR_TIMEOUT 5   /* a kernel's bounded wait expired (see morpho_sm100_device_status) */
 
+/* Hypercube projection phi = proj(z), z = X @ W_phi (reference morfology/cube.cuh:10-45, a
+ * compile-time choice there, a run-time field here). */
+#define MORPHO_PROJ_SIGMOID 0     /* 1 / (1 + e^-z)   (the reference default) */
+#define MORPHO_PROJ_HARDTANH01 1  /* min(1, max(0, (z + 1) / 2)), gradient 1/2 on -1 < z < 1 */
+#define MORPHO_PROJ_IDENTITY 2    /* z */
+
 /* Gradient semantics of the backward. */
 #define MORPHO_GRAD_FULL 0      /* true gradient of the forward (default) */
 #define MORPHO_GRAD_REFERENCE 1 /* reference kernel semantics: query-code and query-bias
@@ -58,6 +64,10 @@ typedef struct morpho_problem {
     float scale;    /* softmax temperature */
     int32_t causal; /* 0 or 1 */
     int32_t grad_mode; /* MORPHO_GRAD_FULL or MORPHO_GRAD_REFERENCE (backward only) */
+    int32_t projection; /* MORPHO_PROJ_* (0 = sigmoid) */
+    int32_t mask_diag;  /* 1: also drop key j == query i (reference MORPHO_MASK_DIAG,
+                           utils/declarations.cuh:79-82, attention.cu:131, :363); a query row
+                           left with no key gives out = 0, lse = -FLT_MAX and no gradient */
 } morpho_problem_t;
 
 /* Bytes of device workspace the forward / backward need for problem p (0 on invalid p). */

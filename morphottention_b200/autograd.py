@@ -72,6 +72,50 @@ def get_grad_mode() -> str:
     return {v: k for k, v in GRAD_MODES.items()}[int(ops.get_grad_mode())]
 
 
+CUBE_PROJECTIONS = {"sigmoid": 0, "hardtanh01": 1, "identity": 2}
+
+
+def set_cube_projection(proj: str) -> str:
+    """Select the hypercube projection phi = proj(x @ W_phi) for subsequent calls:
+    ``"sigmoid"`` (default), ``"hardtanh01"`` (``min(1, max(0, (z + 1) / 2))``) or
+    ``"identity"``.  The reference picks one at compile time
+    (``csrc/cuda/morfology/cube.cuh:10-45``).  Process-wide; returns the previous one."""
+    if proj not in CUBE_PROJECTIONS:
+        raise ValueError(f"cube projection must be one of {tuple(CUBE_PROJECTIONS)}")
+    prev = int(ops.set_cube_projection(CUBE_PROJECTIONS[proj]))
+    return {v: k for k, v in CUBE_PROJECTIONS.items()}[prev]
+
+
+def get_cube_projection() -> str:
+    return {v: k for k, v in CUBE_PROJECTIONS.items()}[int(ops.get_cube_projection())]
+
+
+def set_mask_diag(on: bool) -> bool:
+    """Also mask key j == query i (the reference's compile-time ``MORPHO_MASK_DIAG``,
+    ``csrc/cuda/utils/declarations.cuh:79-82``) in subsequent calls.  A query row left
+    without any key gets ``out = 0``, ``lse = -FLT_MAX`` and no gradient.  Process-wide;
+    returns the previous setting."""
+    return bool(ops.set_mask_diag(1 if on else 0))
+
+
+def get_mask_diag() -> bool:
+    return bool(ops.get_mask_diag())
+
+
+@contextlib.contextmanager
+def attention_options(projection: str | None = None, mask_diag: bool | None = None):
+    """Scoped :func:`set_cube_projection` / :func:`set_mask_diag`."""
+    prev_p = set_cube_projection(projection) if projection is not None else None
+    prev_m = set_mask_diag(mask_diag) if mask_diag is not None else None
+    try:
+        yield
+    finally:
+        if prev_p is not None:
+            set_cube_projection(prev_p)
+        if prev_m is not None:
+            set_mask_diag(prev_m)
+
+
 @contextlib.contextmanager
 def grad_mode(mode: str):
     prev = set_grad_mode(mode)

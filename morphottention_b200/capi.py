@@ -21,6 +21,11 @@ MORPHO_ERR_DEVICE = 4
 MORPHO_ERR_TIMEOUT = 5
 MORPHO_GRAD_FULL = 0
 MORPHO_GRAD_REFERENCE = 1
+MORPHO_PROJ_SIGMOID = 0
+MORPHO_PROJ_HARDTANH01 = 1
+MORPHO_PROJ_IDENTITY = 2
+PROJECTIONS = {"sigmoid": MORPHO_PROJ_SIGMOID, "hardtanh01": MORPHO_PROJ_HARDTANH01,
+               "identity": MORPHO_PROJ_IDENTITY}
 
 EXPORTED = (
     "morpho_sm100_forward_workspace_size",
@@ -49,7 +54,7 @@ EXPORTED = (
 class MorphoProblem(ctypes.Structure):
     _fields_ = [("B", ctypes.c_int32), ("N", ctypes.c_int32), ("D", ctypes.c_int32), ("H", ctypes.c_int32),
                 ("cube_m", ctypes.c_int32), ("scale", ctypes.c_float), ("causal", ctypes.c_int32),
-                ("grad_mode", ctypes.c_int32)]
+                ("grad_mode", ctypes.c_int32), ("projection", ctypes.c_int32), ("mask_diag", ctypes.c_int32)]
 
 
 class MorphoError(RuntimeError):
@@ -116,8 +121,12 @@ def lib() -> ctypes.CDLL:
     return L
 
 
-def problem(B, N, D, H, cube_m, scale=1.0, causal=False, grad_mode=MORPHO_GRAD_FULL) -> MorphoProblem:
-    return MorphoProblem(B, N, D, H, cube_m, float(scale), 1 if causal else 0, int(grad_mode))
+def problem(B, N, D, H, cube_m, scale=1.0, causal=False, grad_mode=MORPHO_GRAD_FULL, projection=MORPHO_PROJ_SIGMOID,
+            mask_diag=False) -> MorphoProblem:
+    if isinstance(projection, str):
+        projection = PROJECTIONS[projection]
+    return MorphoProblem(B, N, D, H, cube_m, float(scale), 1 if causal else 0, int(grad_mode), int(projection),
+                         1 if mask_diag else 0)
 
 
 def last_error() -> str:

@@ -99,6 +99,7 @@ struct BwdCfg {
 
 struct BwdArgs {
     int N, Npad, H, D, Hp, Cp, n_qtiles;
+    int mask_diag;  // also drop key j == query i
     float c2;     // 2 * scale * log2(e)
     float two_scale;
     float neg_scale;
@@ -405,7 +406,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             tc_fence_after();
             const float4* Lv = reinterpret_cast<const float4*>(smem + Cfg::OFF_L + s * kTile * 4) + wg * 16;
-            const bool need_mask = !kv_ok || (qc0 + 64 > args.N) || (CAUSAL && qc0 < kv0 + kTile);
+            const bool need_mask =
+                !kv_ok || (qc0 + 64 > args.N) || (CAUSAL && qc0 < kv0 + kTile) || (args.mask_diag && q0 == kv0);
             // P^T = 2^(c2 * (k.q - cb/2) - L_i): both TMEM loads in flight before one wait
             float p[64];
             {
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 64; ++c) {
                     const int qi = qc0 + c;
-                    const bool keep = kv_ok && qi < args.N && (!CAUSAL || kv <= qi);
+                    const bool keep = kv_ok && qi < args.N && (!CAUSAL || kv <= qi) && !(args.mask_diag && kv == qi);
                     p[c] = keep ? p[c] : 0.f;
                 }
             }
@@ -617,6 +619,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     a.Hp = s.Hp();
     a.Cp = s.Cp();
     a.n_qtiles = Npad / kTile;
+    a.mask_diag = s.mask_diag ? 1 : 0;
     a.c2 = 2.0f * s.scale * kLog2e;
     a.two_scale = 2.0f * s.scale;
     a.neg_scale = -s.scale;

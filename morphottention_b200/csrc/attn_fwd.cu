@@ -60,6 +60,7 @@ struct FwdCfg {
 
 struct FwdArgs {
     int N, Npad, H, D, n_qtiles;
+    int mask_diag;  // also drop key j == query i
     float c2;  // 2 * scale * log2(e)
     const float* qb;
     __half* out;
@@ -261,12 +262,12 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             // t = c2 * S.  The row max of t is c2 * (max or min of S, by the sign of c2);
             // masked keys get -inf / +inf so that c2 * S - m is -inf for them.
             const float masked = pos ? -INFINITY : INFINITY;
-            const bool need_mask = (kv0 + kTile > args.N) || (CAUSAL && j == qt);
+            const bool need_mask = (kv0 + kTile > args.N) || ((CAUSAL || args.mask_diag) && j == qt);
             if (need_mask) {
 #pragma unroll
                 for (int c = 0; c < kTile; ++c) {
                     const int kv = kv0 + c;
-                    const bool drop = kv >= args.N || (CAUSAL && kv > q);
+                    const bool drop = kv >= args.N || (CAUSAL && kv > q) || (args.mask_diag && kv == q);
                     sv[c] = drop ? __float_as_uint(masked) : sv[c];
                 }
             }
@@ -321,9 +322,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             }
             l *= alpha;
             m_ref = m_new;
-            // m_ref is finite here: every row has at least one unmasked key.
+            // m_ref is -inf only while every key of the row so far was masked (causal plus
+            // diagonal mask at query 0): then all of this tile's P are 0, and l stays 0.
             float lsum = 0.f;
-            const float nm = -m_ref;
+            const float nm = m_ref == -INFINITY ? 0.f : -m_ref;
 #pragma unroll
             for (int c = 0; c < kTile; c += 32) {
                 uint32_t pk[16];
@@ -399,6 +401,7 @@ int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out
     a.H = s.H;
     a.D = s.D;
     a.n_qtiles = Npad / kTile;
+    a.mask_diag = s.mask_diag ? 1 : 0;
     a.c2 = 2.0f * s.scale * kLog2e;
     a.qb = p.qb;
     a.out = out;

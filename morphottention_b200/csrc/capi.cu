@@ -4,8 +4,8 @@
 //
 // Forward  (2 launches): projection GEMM+epilogue -> attention forward.
 // Backward (7 launches + 1 memset): projection recompute (+phi) -> delta/L ->
-//   zero dq -> attention backward -> dZ + gate partials -> dX GEMM -> dW GEMM (split-K)
-//   -> deterministic reduction of dW / gate partials.
+//   zero dq -> attention backward -> dZ + gate partials -> dW GEMM (split-K) ->
+//   deterministic reduction of dW / gate partials -> dX GEMM.
 #include <string.h>
 
 #include "kernels.h"
@@ -15,6 +15,9 @@ using namespace morpho;
 namespace {
 
 constexpr int kTile = 128;
+static_assert(kProjSigmoid == MORPHO_PROJ_SIGMOID && kProjHardTanh01 == MORPHO_PROJ_HARDTANH01 &&
+                  kProjIdentity == MORPHO_PROJ_IDENTITY,
+              "projection codes");
 
 int validate(const morpho_problem_t* p, Shape* s) {
     if (p == nullptr) return set_error(MORPHO_ERR_INVALID, "problem is NULL");
@@ -28,6 +31,11 @@ int validate(const morpho_problem_t* p, Shape* s) {
         return set_error(MORPHO_ERR_INVALID, "cube_m = %d not supported (16, 32 or 64)", p->cube_m);
     if (p->grad_mode != MORPHO_GRAD_FULL && p->grad_mode != MORPHO_GRAD_REFERENCE)
         return set_error(MORPHO_ERR_INVALID, "grad_mode %d unknown", p->grad_mode);
+    if (p->projection != MORPHO_PROJ_SIGMOID && p->projection != MORPHO_PROJ_HARDTANH01 &&
+        p->projection != MORPHO_PROJ_IDENTITY)
+        return set_error(MORPHO_ERR_INVALID, "projection %d unknown", p->projection);
+    if (p->mask_diag != 0 && p->mask_diag != 1)
+        return set_error(MORPHO_ERR_INVALID, "mask_diag must be 0 or 1 (got %d)", p->mask_diag);
     const long long T = static_cast<long long>(p->B) * p->N;
     if (T > (1LL << 30) || static_cast<long long>(p->B) * p->H * p->N * 128 > (1LL << 40))
         return set_error(MORPHO_ERR_INVALID, "problem too large: B*N = %lld", T);
@@ -43,6 +51,8 @@ int validate(const morpho_problem_t* p, Shape* s) {
     s->scale = p->scale;
     s->causal = p->causal != 0;
     s->grad_mode = p->grad_mode;
+    s->proj = p->projection;
+    s->mask_diag = p->mask_diag != 0;
     return MORPHO_OK;
 }
 

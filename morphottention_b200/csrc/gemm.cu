@@ -68,8 +68,22 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
     for (int i = 0; i < NC; ++i) out[i] = u2f(r[i]);
 }
 
+// phi = proj(z) in place (reference morfology/cube.cuh:12-26); the choice is uniform, so
+// each branch is one unrolled loop.
+template <int NC>
+__device__ __forceinline__ void cube_project(float* z, int proj) {
+    if (proj == kProjSigmoid) {
+#pragma unroll
+        for (int i = 0; i < NC; ++i) z[i] = __fdividef(1.0f, 1.0f + __expf(-z[i]));
+    } else if (proj == kProjHardTanh01) {
+#pragma unroll
+        for (int i = 0; i < NC; ++i) z[i] = fminf(1.0f, fmaxf(0.0f, 0.5f * (z[i] + 1.0f)));
+    }
+}
+
 struct ProjParams {
     int T, N, Npad, H, hd, Hp, D;
+    int proj;  // kProj*
     float c;  // scale * log2(e)
     const __half* gq;
     const __half* gk;
@@ -102,15 +116,14 @@ struct EpiProj {
                 for (int q = 0; q < MC / CW; ++q) {
                     float zr[CW];
                     tmem_load_cols<CW>(tacc + hc * MC + q * CW, zr);
+                    cube_project<CW>(zr, p.proj);  // zr = phi from here on
                     uint32_t qpk[CW / 2], kpk[CW / 2], hpk[CW / 2], lpk[CW / 2];
 #pragma unroll
                     for (int c = 0; c < CW; c += 2) {
                         const float2 gq = __half22float2(gq2[(q * CW + c) / 2]);
                         const float2 gk = __half22float2(gk2[(q * CW + c) / 2]);
-                        const float p0 = __fdividef(1.0f, 1.0f + __expf(-zr[c]));
-                        const float p1 = __fdividef(1.0f, 1.0f + __expf(-zr[c + 1]));
-                        zr[c] = p0;
-                        zr[c + 1] = p1;
+                        const float p0 = zr[c];
+                        const float p1 = zr[c + 1];
                         const float q0 = gq.x * p0, q1 = gq.y * p1;
                         const float k0 = gk.x * p0, k1 = gk.y * p1;
                         qb = fmaf(gk.x, q0, fmaf(gk.y, q1, qb));
@@ -494,6 +507,7 @@ int launch_proj(const DeviceInfo& dev, const Shape& s, const __half* X, const __
     p.Hp = Hp;
     p.D = s.D;
     p.c = s.scale * kLog2e;
+    p.proj = s.proj;
     p.gq = gate_q;
     p.gk = gate_k;
     p.o = o;

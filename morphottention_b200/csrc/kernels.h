@@ -11,11 +11,18 @@ namespace morpho {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Hypercube projections (the values of MORPHO_PROJ_* in morpho_sm100.h).
+constexpr int kProjSigmoid = 0;
+constexpr int kProjHardTanh01 = 1;
+constexpr int kProjIdentity = 2;
+
 struct Shape {
     int B, N, D, H, m, hd;
     float scale;
     bool causal;
     int grad_mode;
+    int proj = 0;            // MORPHO_PROJ_*
+    bool mask_diag = false;  // drop key j == query i
     long long tokens() const { return static_cast<long long>(B) * N; }
     int Hm() const { return H * m; }
     // dZ columns are padded to a multiple of 64 so that no 64-wide K block of the dX

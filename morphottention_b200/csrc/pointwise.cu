@@ -79,7 +79,16 @@ __global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ d
 // Block = 256 threads, a contiguous run of tokens.  Thread k owns columns
 // 4k .. 4k+3 (+1024 per loop) of the padded dZ space [0, Hp).  Writes dcat[:, 0:Hp) and
 // the block's gate partials gate_part[blk][0|1][H*m].
-template <bool FULL>
+// dphi/dz from phi alone (reference morfology/cube.cuh:28-45): sigmoid phi (1 - phi);
+// hardtanh01 1/2 where 0 < phi < 1 (i.e. -1 < z < 1), else 0; identity 1.
+template <int PROJ>
+__device__ __forceinline__ float cube_grad(float phi) {
+    if (PROJ == kProjSigmoid) return phi * (1.0f - phi);
+    if (PROJ == kProjHardTanh01) return (phi > 0.0f && phi < 1.0f) ? 0.5f : 0.0f;
+    return 1.0f;
+}
+
+template <bool FULL, int PROJ>
 __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, const float* __restrict__ dq,
                                                  const float* __restrict__ dk, const float* __restrict__ dcb,
                                                  const __half* __restrict__ gq, const __half* __restrict__ gk,
@@ -127,7 +136,7 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
                     // (the query-bias terms are identically 0)
                     float dphi = kv[i] * g_k[i];
                     if (FULL) dphi = fmaf(qv[i], g_q[i], dphi);
-                    dz[i] = dphi * fv[i] * (1.0f - fv[i]);
+                    dz[i] = dphi * cube_grad<PROJ>(fv[i]);
                     float gqi = db * g_k[i] * fv[i];
                     if (FULL) gqi = fmaf(qv[i], fv[i], gqi);
                     aq[i] += gqi;
@@ -271,13 +280,16 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
               cudaStream_t stream) {
     const int T = static_cast<int>(s.tokens());
     const int tpb = (T + gate_blocks - 1) / gate_blocks;
+    auto kern = s.grad_mode == MORPHO_GRAD_FULL
+                    ? (s.proj == kProjSigmoid      ? dz_kernel<true, kProjSigmoid>
+                       : s.proj == kProjHardTanh01 ? dz_kernel<true, kProjHardTanh01>
+                                                   : dz_kernel<true, kProjIdentity>)
+                    : (s.proj == kProjSigmoid      ? dz_kernel<false, kProjSigmoid>
+                       : s.proj == kProjHardTanh01 ? dz_kernel<false, kProjHardTanh01>
+                                                   : dz_kernel<false, kProjIdentity>);
     prof_begin(stream);
-    if (s.grad_mode == MORPHO_GRAD_FULL)
-        dz_kernel<true><<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
-                                                         npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
-    else
-        dz_kernel<false><<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
-                                                          npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
+    kern<<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+                                                    npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     MORPHO_LAUNCH_CHECK("dz");
     return MORPHO_OK;
 }

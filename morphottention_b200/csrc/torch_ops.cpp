@@ -7,7 +7,9 @@
 // has none), workspace from the torch caching allocator on the current stream, no
 // zero-fill of the gradient outputs (the kernels overwrite them), and extra ops:
 // set_grad_mode / get_grad_mode select full gradients (default) or the reference
-// kernel's gradient semantics; forward_save / backward_saved keep the projection of the
+// kernel's gradient semantics; set_cube_projection / set_mask_diag (and their getters)
+// select the reference's compile-time variants (HardTanh01 / Identity projection, the
+// diagonal mask) for the calls that follow; forward_save / backward_saved keep the projection of the
 // forward for the backward instead of recomputing it (the autograd Function uses them).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -22,6 +24,8 @@
 namespace {
 
 std::atomic<int> g_grad_mode{MORPHO_GRAD_FULL};
+std::atomic<int> g_projection{MORPHO_PROJ_SIGMOID};
+std::atomic<int> g_mask_diag{0};
 
 void check(const at::Tensor& t, const char* name) {
     TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
@@ -39,6 +43,8 @@ morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double 
     p.scale = static_cast<float>(scale);
     p.causal = causal ? 1 : 0;
     p.grad_mode = g_grad_mode.load();
+    p.projection = g_projection.load();
+    p.mask_diag = g_mask_diag.load();
     return p;
 }
 
@@ -176,6 +182,21 @@ int64_t set_grad_mode(int64_t mode) {
 
 int64_t get_grad_mode() { return g_grad_mode.load(); }
 
+int64_t set_cube_projection(int64_t proj) {
+    TORCH_CHECK(proj == MORPHO_PROJ_SIGMOID || proj == MORPHO_PROJ_HARDTANH01 || proj == MORPHO_PROJ_IDENTITY,
+                "cube projection must be 0 (sigmoid), 1 (hardtanh01) or 2 (identity)");
+    return g_projection.exchange(static_cast<int>(proj));
+}
+
+int64_t get_cube_projection() { return g_projection.load(); }
+
+int64_t set_mask_diag(int64_t on) {
+    TORCH_CHECK(on == 0 || on == 1, "mask_diag must be 0 or 1");
+    return g_mask_diag.exchange(static_cast<int>(on));
+}
+
+int64_t get_mask_diag() { return g_mask_diag.load(); }
+
 }  // namespace
 
 TORCH_LIBRARY(morphottention, m) {
@@ -193,6 +214,10 @@ TORCH_LIBRARY(morphottention, m) {
         "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
     m.def("set_grad_mode(int mode) -> int", &set_grad_mode);
     m.def("get_grad_mode() -> int", &get_grad_mode);
+    m.def("set_cube_projection(int proj) -> int", &set_cube_projection);
+    m.def("get_cube_projection() -> int", &get_cube_projection);
+    m.def("set_mask_diag(int on) -> int", &set_mask_diag);
+    m.def("get_mask_diag() -> int", &get_mask_diag);
 }
 
 TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {

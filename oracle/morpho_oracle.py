@@ -12,12 +12,18 @@ the reference project root (``packages/morphottention/...``).
 Math, per head ``h`` with token features ``x`` [N, D]:
 
 * ``z = x @ W_phi[:, h*m:(h+1)*m]`` and ``phi = sigmoid(z)``
-  (``csrc/cuda/sm120/project.cuh:26-34``, ``csrc/cuda/morfology/cube.cuh:12-14``)
+  (``csrc/cuda/sm120/project.cuh:26-34``, ``csrc/cuda/morfology/cube.cuh:12-14``), or
+  the reference's other compile-time projections ``hardtanh01(z) = min(1, max(0, (z+1)/2))``
+  with gradient 1/2 on ``-1 < z < 1`` only, and ``identity`` (``cube.cuh:15-45``)
 * ``q = gate_q[h] * phi``, ``k = gate_k[h] * phi`` (``project.cuh:36-37``)
 * ``qbias_i = sum_c gate_k[c] q_ic`` and ``cbias_j = sum_c gate_q[c] k_jc``
   (``project.cuh:39-44``; called with swapped gates at ``attention.cu:78-79``, ``:102-103``)
 * ``S_ij = scale * (2 q_i.k_j - qbias_i - cbias_j)`` (``attention.cu:125``), causal mask
-  ``j > i`` (``attention.cu:129-130``), softmax over j (``attention.cu:138-158``)
+  ``j > i`` (``attention.cu:129-130``), optional diagonal mask ``j == i``
+  (``MORPHO_MASK_DIAG``, ``attention.cu:131-132``), softmax over j (``attention.cu:138-158``).
+  A row with every key masked (causal plus diagonal mask at i = 0) is defined here as
+  ``out = 0``, ``lse = -FLT_MAX`` and no gradient; the reference kernel's forward instead
+  turns such a row into a uniform average (all its scores are ``-FLT_MAX``)
 * ``V = x @ W_V[:, h*hd:(h+1)*hd]`` (``attention.cu:106-111``) and
   ``out[:, :, h*hd:(h+1)*hd] = P @ V`` (``attention.cu:163-183``)
 * ``lse[b*H+h, i]`` in the log2 domain: ``max_j(s_ij) + log2(sum_j 2^(s_ij - max))``
@@ -43,9 +49,36 @@ import torch
 LOG2E = 1.4426950408889634  # csrc/cuda/utils/declarations.cuh:7
 
 GRAD_MODES = ("full", "reference")
+PROJECTIONS = ("sigmoid", "hardtanh01", "identity")
+FLT_LOWEST = -3.4028234663852886e38
 
 
-def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int):
+class _HardTanh01(torch.autograd.Function):
+    """``min(1, max(0, (z+1)/2))`` with the reference's gradient: 1/2 strictly inside
+    ``-1 < z < 1``, else 0 (``cube.cuh:15-17``, ``:33-35``)."""
+
+    @staticmethod
+    def forward(ctx, z):
+        ctx.save_for_backward(z)
+        return (0.5 * (z + 1.0)).clamp(0.0, 1.0)
+
+    @staticmethod
+    def backward(ctx, g):
+        (z,) = ctx.saved_tensors
+        return g * ((z > -1.0) & (z < 1.0)).to(g.dtype) * 0.5
+
+
+def cube_project(z, projection: str = "sigmoid"):
+    if projection == "sigmoid":
+        return torch.sigmoid(z)
+    if projection == "hardtanh01":
+        return _HardTanh01.apply(z)
+    if projection == "identity":
+        return z
+    raise ValueError(f"projection must be one of {PROJECTIONS}")
+
+
+def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, projection: str = "sigmoid"):
     """Per-head hypercube codes, biases and values.
 
     Restates ``project_phi`` (``csrc/cuda/sm120/project.cuh:16-47``) and the value
@@ -56,7 +89,7 @@ def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int):
     B, N, _ = x.shape
     hd = W_V.shape[1] // H
     z = (x @ W_phi).view(B, N, H, cube_m).permute(0, 2, 1, 3)  # [B,H,N,m]
-    phi = torch.sigmoid(z)
+    phi = cube_project(z, projection)
     gq = gate_q.view(1, H, 1, cube_m)
     gk = gate_k.view(1, H, 1, cube_m)
     q = gq * phi
@@ -67,21 +100,31 @@ def project(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int):
     return phi, q, k, qbias, cbias, v
 
 
-def _attend(q, k, qbias, cbias, v, scale: float, causal: bool):
+def _attend(q, k, qbias, cbias, v, scale: float, causal: bool, mask_diag: bool = False):
     """Score, mask, softmax and P.V; ``attention.cu:113-188``."""
     N = q.shape[2]
     s = scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))
+    mask = None
     if causal:
         mask = torch.ones(N, N, dtype=torch.bool, device=q.device).triu(1)
+    if mask_diag:
+        eye = torch.eye(N, dtype=torch.bool, device=q.device)
+        mask = eye if mask is None else (mask | eye)
+    if mask is None:
+        p = torch.softmax(s, dim=-1)
+        lse2 = torch.logsumexp(s, dim=-1) * LOG2E  # [B,H,N], log2 domain
+    else:
         s = s.masked_fill(mask, float("-inf"))
-    p = torch.softmax(s, dim=-1)
+        dead = mask.all(dim=-1)  # rows without any key
+        s_safe = s.masked_fill(dead.unsqueeze(-1), 0.0)
+        p = torch.softmax(s_safe, dim=-1).masked_fill(dead.unsqueeze(-1), 0.0)
+        lse2 = (torch.logsumexp(s_safe, dim=-1) * LOG2E).masked_fill(dead, FLT_LOWEST)
     o = p @ v  # [B,H,N,hd]
-    lse2 = torch.logsumexp(s, dim=-1) * LOG2E  # [B,H,N], log2 domain
     return o, lse2
 
 
 def forward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
-            causal: bool = False, grad_mode: str = "full"):
+            causal: bool = False, grad_mode: str = "full", projection: str = "sigmoid", mask_diag: bool = False):
     """Eager forward.  Returns ``(out [B,N,D], lse [B*H,N])`` like ``morphottention::forward``
     (``csrc/cuda/binder.cpp:7-8``, ``csrc/cuda/attention/attention.cpp:40-56``).
 
@@ -91,25 +134,25 @@ def forward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1
     if grad_mode not in GRAD_MODES:
         raise ValueError(f"grad_mode must be one of {GRAD_MODES}")
     B, N, D = x.shape
-    _, q, k, qbias, cbias, v = project(x, W_phi, gate_q, gate_k, W_V, H, cube_m)
+    _, q, k, qbias, cbias, v = project(x, W_phi, gate_q, gate_k, W_V, H, cube_m, projection)
     if grad_mode == "reference":
         q = q.detach()
         qbias = qbias.detach()
-    o, lse2 = _attend(q, k, qbias, cbias, v, scale, causal)
+    o, lse2 = _attend(q, k, qbias, cbias, v, scale, causal, mask_diag)
     out = o.permute(0, 2, 1, 3).reshape(B, N, D)
     return out, lse2.reshape(B * H, N)
 
 
 def forward_backward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
                      causal: bool = False, grad_out=None, grad_mode: str = "full",
-                     dtype=torch.float32):
+                     dtype=torch.float32, projection: str = "sigmoid", mask_diag: bool = False):
     """Forward plus the backward of ``sum(out * grad_out)`` (``out.sum()`` when
     ``grad_out`` is None).  Returns a dict with ``out, lse, dX, dW_phi, d_gate_q,
     d_gate_k, dW_V`` in ``dtype`` on the inputs' device.
     """
     leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in (x, W_phi, gate_q, gate_k, W_V)]
     with torch.enable_grad():
-        out, lse = forward(*leaves, H, cube_m, scale, causal, grad_mode)
+        out, lse = forward(*leaves, H, cube_m, scale, causal, grad_mode, projection, mask_diag)
         g = torch.ones_like(out) if grad_out is None else grad_out.detach().to(dtype)
         grads = torch.autograd.grad(out, leaves, grad_outputs=g)
     names = ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V")

@@ -15,11 +15,13 @@ TOL_GRAD = 5e-3
 TOL_LSE = 1e-3  # lse (log2 units) inherits the fp16 rounding of the codes
 
 
-def run_cuda(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", backward: bool = True):
+def run_cuda(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", backward: bool = True,
+             projection: str = "sigmoid", mask_diag: bool = False):
     """Forward (+ backward) through libmorpho_sm100.so.  Inputs are fp16 CUDA tensors."""
     dev = inp["x"].device
     mode = capi.MORPHO_GRAD_FULL if grad_mode == "full" else capi.MORPHO_GRAD_REFERENCE
-    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, mode)
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, mode, projection=projection,
+                     mask_diag=mask_diag)
     x = inp["x"]
     out = torch.empty_like(x)
     lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
@@ -41,11 +43,13 @@ def run_cuda(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full
     return res
 
 
-def run_oracle(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", device="cpu"):
+def run_oracle(cfg: MorphoConfig, inp: dict, grad_out=None, grad_mode: str = "full", device="cpu",
+               projection: str = "sigmoid", mask_diag: bool = False):
     t = {k: v.to(device) for k, v in inp.items()}
     g = None if grad_out is None else grad_out.to(device)
     return O.forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m, cfg.scale,
-                              cfg.causal, grad_out=g, grad_mode=grad_mode)
+                              cfg.causal, grad_out=g, grad_mode=grad_mode, projection=projection,
+                              mask_diag=mask_diag)
 
 
 def gate_tolerance(cfg: MorphoConfig) -> float:

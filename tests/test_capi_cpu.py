@@ -45,7 +45,11 @@ def test_workspace_sizes():
 def test_invalid_problems_rejected():
     L = capi.lib()
     bad = [capi.problem(0, 16, 64, 2, 16), capi.problem(1, 16, 65, 2, 16), capi.problem(1, 16, 96, 2, 16),
-           capi.problem(1, 16, 64, 2, 24), capi.problem(1, 16, 64, 2, 16, grad_mode=7)]
+           capi.problem(1, 16, 64, 2, 24), capi.problem(1, 16, 64, 2, 16, grad_mode=7),
+           capi.problem(1, 16, 64, 2, 16, projection=3), capi.problem(1, 16, 64, 2, 16, projection=-1)]
+    bad_mask = capi.problem(1, 16, 64, 2, 16)
+    bad_mask.mask_diag = 2
+    bad.append(bad_mask)
     for p in bad:
         assert L.morpho_sm100_forward_workspace_size(ctypes.byref(p)) == 0
         rc = L.morpho_sm100_forward(ctypes.byref(p), *([None] * 8), 0, None)

@@ -1,0 +1,97 @@
+"""The reference's compile-time variants as run-time options: the HardTanh01 and Identity
+hypercube projections (reference csrc/cuda/morfology/cube.cuh:10-45) and the diagonal
+mask (MORPHO_MASK_DIAG, csrc/cuda/utils/declarations.cuh:79-82, attention.cu:131, :363),
+through the C ABI and through the module API, against the fp32 oracle with the same
+tolerances as the default path (rel-L2 <= 1e-3 out / lse, <= 5e-3 gradients)."""
+
+import pytest
+import torch
+
+import morphottention_b200 as M
+from morphottention_b200.configs import MorphoConfig
+from oracle import morpho_oracle as O
+
+from .helpers import compare, gate_tolerance, inputs, run_cuda, run_oracle
+
+pytestmark = pytest.mark.gpu
+
+# The HardTanh01 and Identity codes spread wider than the sigmoid's, so at cube_m = 64 the
+# self-score S_ii = 2 scale |phi_i - 1/2|^2 dominates every row at scale 1: the softmax
+# saturates, the weight gradients through it vanish (~1e-5 of their usual size) and a
+# relative error of them measures fp16 noise only.  The m = 64 case uses scale 0.2 (and 0.03
+# for the unbounded Identity codes, whose |phi - 1/2|^2 is about 1.25 per column).
+CASES = [
+    MorphoConfig("m16_hd64", 2, 197, 128, 2, 16, 1.0, False, 31),
+    MorphoConfig("m32_causal", 1, 300, 256, 4, 32, 0.5, True, 32),
+    MorphoConfig("m64_hd128", 1, 256, 256, 2, 64, 0.2, False, 33),
+]
+
+
+@pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
+@pytest.mark.parametrize("projection", ["hardtanh01", "identity"])
+def test_projection_parity(cuda, cfg, projection):
+    if projection == "identity" and cfg.cube_m == 64:
+        cfg = cfg.with_(scale=0.03)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    ours = run_cuda(cfg, inp, grad_out=g, projection=projection)
+    ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_out=g.cpu(), projection=projection)
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def _compare_masked(ours, ref, cfg):
+    """lse of rows without any key is -FLT_MAX on both sides; compare the others."""
+    dead = ref["lse"] <= O.FLT_LOWEST / 2
+    assert torch.equal(dead, ours["lse"].cpu() <= O.FLT_LOWEST / 2)
+    live = {k: v for k, v in ours.items() if k != "lse"}
+    errs = compare(live, ref, keys=[k for k in live], tol_gate=gate_tolerance(cfg))
+    lse_err = O.rel_l2(ours["lse"].cpu()[~dead].double(), ref["lse"][~dead].double())
+    assert lse_err <= 1e-3, lse_err
+    if dead.any():
+        assert torch.all(ours["out"].float().view(cfg.B, cfg.N, cfg.H, -1).permute(0, 2, 1, 3)
+                         .reshape(cfg.B * cfg.H, cfg.N, -1)[dead.to(ours["out"].device)] == 0)
+    return errs
+
+
+@pytest.mark.parametrize("cfg", CASES + [MorphoConfig("n15_causal", 2, 15, 64, 2, 32, 2.0, True, 34)],
+                         ids=lambda c: c.name)
+def test_mask_diag_parity(cuda, cfg):
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    ours = run_cuda(cfg, inp, grad_out=g, mask_diag=True)
+    ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_out=g.cpu(), mask_diag=True)
+    _compare_masked(ours, ref, cfg)
+
+
+def test_options_through_module(cuda):
+    """attention_options() reaches the torch ops: the module matches the oracle with a
+    non-default projection and the diagonal mask, and the settings are restored after."""
+    cfg = MorphoConfig("mod", 2, 160, 128, 4, 16, 0.8, True, 35)
+    inp = inputs(cfg, cuda, random_gates=True)
+    mod = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=cuda)
+    with torch.no_grad():
+        for n in ("W_phi", "W_V", "gate_q", "gate_k"):
+            getattr(mod, n).copy_(inp[n])
+    x = inp["x"].clone().requires_grad_(True)
+    with M.attention_options(projection="hardtanh01", mask_diag=True):
+        assert M.get_cube_projection() == "hardtanh01" and M.get_mask_diag()
+        out = mod(x)
+        out.float().sum().backward()
+    assert M.get_cube_projection() == "sigmoid" and not M.get_mask_diag()
+    ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, projection="hardtanh01", mask_diag=True)
+    ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
+            "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_invalid_options_are_rejected(cuda):
+    from morphottention_b200 import capi
+    with pytest.raises(ValueError):
+        M.set_cube_projection("relu")
+    p = capi.problem(1, 128, 128, 2, 16, projection=7)
+    x = torch.zeros(1, 128, 128, dtype=torch.float16, device=cuda)
+    w = torch.zeros(128, 32, dtype=torch.float16, device=cuda)
+    gq = torch.ones(2, 16, dtype=torch.float16, device=cuda)
+    with pytest.raises(capi.MorphoError, match="projection"):
+        capi.forward(p, x, w, gq, gq, torch.zeros(128, 128, dtype=torch.float16, device=cuda), torch.empty_like(x),
+                     torch.empty(2, 128, device=cuda))

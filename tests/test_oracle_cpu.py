@@ -107,3 +107,47 @@ def test_seeded_inputs_are_deterministic():
     for k in a:
         assert torch.equal(a[k], b[k])
         assert a[k].dtype == torch.float16
+
+
+def test_gradcheck_projections_and_diagonal_mask_fp64():
+    """Autograd of the oracle with the HardTanh01 / Identity projections and the diagonal
+    mask matches finite differences (the kinks of HardTanh01 at z = +-1 are not hit)."""
+    for projection, causal, mask_diag in (("hardtanh01", False, False), ("identity", True, False),
+                                          ("sigmoid", False, True), ("hardtanh01", True, True)):
+        cfg = TINY.with_(causal=causal)
+        inp = _inputs(cfg)
+        args = [inp[k].clone().requires_grad_(True) for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+
+        def f(*a):
+            out, lse = O.forward(*a, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, projection=projection,
+                                 mask_diag=mask_diag)
+            return out, lse.clamp_min(-1e30)
+
+        assert torch.autograd.gradcheck(f, args, eps=1e-6, atol=1e-6), (projection, causal, mask_diag)
+
+
+def test_hardtanh01_gradient_is_strict():
+    """Gradient 1/2 strictly inside -1 < z < 1, 0 at and beyond the ends (cube.cuh:33-35)."""
+    z = torch.tensor([-2.0, -1.0, -0.5, 0.0, 0.999, 1.0, 3.0], dtype=torch.float64, requires_grad=True)
+    phi = O.cube_project(z, "hardtanh01")
+    phi.sum().backward()
+    assert torch.equal(phi.detach(), torch.tensor([0.0, 0.0, 0.25, 0.5, 0.9995, 1.0, 1.0], dtype=torch.float64))
+    assert torch.equal(z.grad, torch.tensor([0.0, 0.0, 0.5, 0.5, 0.5, 0.0, 0.0], dtype=torch.float64))
+
+
+def test_diagonal_mask_rows():
+    """With the diagonal mask every query loses its own key; with causal masking as well,
+    query 0 has no key left: out = 0, lse = -FLT_MAX, and it passes no gradient."""
+    cfg = TINY.with_(causal=True)
+    inp = _inputs(cfg)
+    r = O.forward_backward(inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], cfg.H, cfg.cube_m,
+                           cfg.scale, True, dtype=torch.float64, mask_diag=True)
+    lse = r["lse"].view(cfg.B, cfg.H, cfg.N)
+    assert torch.all(lse[:, :, 0] == O.FLT_LOWEST)
+    assert torch.all(torch.isfinite(lse[:, :, 1:]))
+    assert torch.all(r["out"][:, 0] == 0)
+    # query 1 attends to key 0 only: its output is head-wise V of token 0
+    v = (inp["x"] @ inp["W_V"])
+    assert torch.allclose(r["out"][:, 1], v[:, 0], atol=1e-12)
+    for k in ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"):
+        assert torch.all(torch.isfinite(r[k]))
