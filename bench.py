@@ -403,13 +403,244 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+VIT_DEPTH = 12
+VIT_MLP_RATIO = 4
+
+
+def _vit_flops(cfg):
+    """Tensor FLOPs of one ViT encoder training step: per block the attention layer's
+    (projection GEMMs and attention, fwd + bwd) plus the MLP's two Linear layers, forward and
+    the two backward GEMMs: 3 * 2 * 2 * T * D * (4 D)."""
+    mlp = 3.0 * 2.0 * 2.0 * cfg.tokens * cfg.D * (VIT_MLP_RATIO * cfg.D)
+    return VIT_DEPTH * (cfg.tensor_flops_fwd_bwd() + mlp)
+
+
+class _OracleAttention:
+    """CPU attention for the reference arm of the encoder workload (the oracle, fp32)."""
+
+    def __init__(self, mod):
+        self.mod = mod
+
+    def __call__(self, x):
+        from oracle import morpho_oracle as O
+        m = self.mod
+        return O.forward(x, m.W_phi, m.gate_q, m.gate_k, m.W_V, m.num_heads, m.cube_m, m.scale, m.causal)[0]
+
+
+def _vit_cpu_step_seconds(cfg, steps=2, warmup=1):
+    """fp32 CPU encoder (oracle attention) on one sequence: seconds per training step."""
+    import torch
+    from morphottention_b200.encoder import Encoder
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(cfg.seed)
+    model = Encoder(depth=VIT_DEPTH, dim=cfg.D, num_heads=cfg.H, cube_m=cfg.cube_m, mlp_ratio=VIT_MLP_RATIO,
+                    scale=cfg.scale, dtype=torch.float32, device="cpu")
+    for blk in model.blocks:
+        blk.attn.forward = _OracleAttention(blk.attn)
+    g = torch.Generator().manual_seed(cfg.seed)
+    x = torch.randn(1, cfg.N, cfg.D, generator=g)
+    target = torch.randn(1, cfg.N, cfg.D, generator=g)
+    opt = torch.optim.SGD(model.parameters(), lr=1e-4)
+
+    def step():
+        loss = torch.nn.functional.mse_loss(model(x), target)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    return (time.perf_counter() - t0) / steps, torch.get_num_threads()
+
+
+def _vit_config(cfg, world):
+    return {"workload": f"c4_vit_train: {VIT_DEPTH}-block pre-norm ViT-B encoder (LayerNorm -> MorphoAttention -> "
+                        f"LayerNorm -> GELU MLP {VIT_MLP_RATIO * cfg.D}, residuals), MSE loss, SGD step",
+            "B_per_gpu": cfg.B, "N": cfg.N, "D": cfg.D, "H": cfg.H, "cube_m": cfg.cube_m, "head_dim": cfg.head_dim,
+            "scale": cfg.scale, "causal": cfg.causal, "depth": VIT_DEPTH, "global_batch": cfg.B * world,
+            "seq_len": cfg.N, "parallelism": f"dp{world} (DistributedDataParallel)",
+            "l2": "activations of 12 blocks (> 1 GB) per step, no flush"}
+
+
+def run_vit(args):
+    """--config c4vit: the 12-block ViT-B encoder training step around the attention layers."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from morphottention_b200 import capi
+    from morphottention_b200.configs import CONFIGS
+    from morphottention_b200.encoder import Encoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = CONFIGS["c4"]
+    if args.batch is not None:
+        cfg = cfg.with_(B=args.batch)
+    torch.manual_seed(cfg.seed)
+    model = Encoder(depth=VIT_DEPTH, dim=cfg.D, num_heads=cfg.H, cube_m=cfg.cube_m, mlp_ratio=VIT_MLP_RATIO,
+                    scale=cfg.scale, device=dev)
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local])
+    opt = torch.optim.SGD(model.parameters(), lr=1e-4, foreach=True)
+    g = torch.Generator().manual_seed(cfg.seed * 1000 + rank)
+    x_host = torch.randn(cfg.B, cfg.N, cfg.D, generator=g).half().pin_memory()
+    target = torch.randn(cfg.B, cfg.N, cfg.D, generator=g).to(dev)
+    x = x_host.to(dev)
+
+    def step(xd):
+        loss = torch.nn.functional.mse_loss(model(xd).float(), target)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def timed(fn, n):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for k in range(n):
+            fn(k)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    status = capi.device_status(reset=True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    capi.profile_enable(True)
+    ms = timed(lambda k: step(x), args.steps)
+    clocks = sampler.stop()
+    prof = capi.profile_collect()
+    capi.profile_enable(False)
+    status |= capi.device_status(reset=True)
+    tokens_total = cfg.tokens * world * args.steps
+    value = tokens_total / (ms / 1000.0)
+    ours_ms = sum(v[0] for v in prof.values()) / args.steps
+    launches = sum(v[1] for v in prof.values()) / args.steps
+
+    # end to end: the input copied from pinned host memory every step (next step's copy on a
+    # copy stream, two device buffers) and the loss read back one step later
+    e2e = None
+    if not args.no_e2e:
+        copy_stream = torch.cuda.Stream(device=dev)
+        x_dev = [torch.empty_like(x) for _ in range(2)]
+        landed = [torch.cuda.Event() for _ in range(2)]
+        released = [torch.cuda.Event() for _ in range(2)]
+        fetched = [torch.cuda.Event() for _ in range(2)]
+        loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
+        for ev in released:
+            ev.record()
+
+        def prefetch(k):
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(released[k % 2])
+                x_dev[k % 2].copy_(x_host, non_blocking=True)
+                landed[k % 2].record(copy_stream)
+
+        def e2e_step(k, n):
+            if k == 0:
+                prefetch(0)
+            if k + 1 < n:
+                prefetch(k + 1)
+            torch.cuda.current_stream().wait_event(landed[k % 2])
+            loss = step(x_dev[k % 2])
+            released[k % 2].record()
+            loss_host[k % 2].copy_(loss.detach(), non_blocking=True)
+            fetched[k % 2].record()
+            if k > 0:
+                fetched[(k - 1) % 2].synchronize()
+                assert float(loss_host[(k - 1) % 2]) == float(loss_host[(k - 1) % 2])
+
+        for k in range(2):
+            e2e_step(k, 2)
+        ems = timed(lambda k: e2e_step(k, args.steps), args.steps)
+        e2e = {"value": tokens_total / (ems / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4,
+               "api": "morphottention_b200.encoder.Encoder training step (MorphoAttention modules)",
+               "input_copy": "step k+1's pinned host->device copy on a copy stream during step k"}
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peaks = _peaks()
+    flops = _vit_flops(cfg)
+    achieved = flops / (ms / args.steps / 1000.0) / 1e12
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic: x, target ~ N(0,1) seeded, default init",
+            "config": _vit_config(cfg, world),
+            "roofline": {"kernel": "whole training step (torch LayerNorm/GELU/cuBLAS MLP + this library's "
+                                   "attention)", "bound": "tensor", "achieved": achieved,
+                         "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops_sustained"], "traffic": None,
+                         "flops_per_step": flops},
+            "e2e": e2e, "gpu_launches": int(round(launches)), "clocks": clocks,
+            "attention_ms_per_step": ours_ms, "attention_share": ours_ms / (ms / args.steps),
+            "kernels": {k: {"ms_per_launch": v[0] / v[1], "launches_per_step": v[1] / args.steps}
+                        for k, v in prof.items()},
+            "device_status": status}
+    if world == 1 and not args.no_cpu_baseline:
+        sec, cores = _vit_cpu_step_seconds(cfg)
+        line["cpu_baseline"] = {"value": cfg.N / sec, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": "1 of %d sequences, fp32 CPU encoder with the oracle attention, "
+                                          "training step" % cfg.B, "seconds_per_sequence": sec}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_vit_reference(args):
+    """--impl reference --config c4vit: the fp32 CPU encoder (oracle attention), 1 sequence per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from morphottention_b200.configs import CONFIGS
+    cfg = CONFIGS["c4"]
+    sec, cores = _vit_cpu_step_seconds(cfg, steps=args.steps, warmup=args.warmup)
+    value = cfg.N / sec
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sec, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic: x, target ~ N(0,1) seeded",
+            "config": _vit_config(cfg, args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"1 of {cfg.B} sequences per step"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c4", "c5", "c4vit"],
+                    help="c1..c5: one MorphoAttention layer; c4vit: the 12-block ViT-B encoder training step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
@@ -417,7 +648,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.config == "c4vit":
+        run_vit_reference(args) if args.impl == "reference" else run_vit(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -1,0 +1,58 @@
+"""The ViT-style encoder around MorphoAttention (the caller of the attention path): a small
+fp16 encoder on the GPU against the same encoder in fp32 on the CPU with the oracle as its
+attention, same weights and inputs, MSE-loss training step.  LayerNorm, the MLP and the
+residual stream also run in fp16 on the GPU, so the model-level tolerances (rel-L2 3e-3 for
+the output, 1.5e-2 for every parameter gradient) are looser than the attention layer's own."""
+
+import pytest
+import torch
+from torch import nn
+
+from morphottention_b200.encoder import Encoder
+from oracle import morpho_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+class OracleAttention(nn.Module):
+    def __init__(self, ref) -> None:
+        super().__init__()
+        self.num_heads, self.cube_m, self.scale, self.causal = ref.num_heads, ref.cube_m, ref.scale, ref.causal
+        for n in ("W_phi", "gate_q", "gate_k", "W_V"):
+            setattr(self, n, nn.Parameter(getattr(ref, n).detach().float().cpu().clone()))
+
+    def forward(self, x):
+        out, _ = O.forward(x, self.W_phi, self.gate_q, self.gate_k, self.W_V, self.num_heads, self.cube_m, self.scale,
+                           self.causal)
+        return out
+
+
+@pytest.mark.parametrize("out_proj", [False, True])
+def test_encoder_step_matches_oracle_model(cuda, out_proj):
+    torch.manual_seed(3)
+    gpu = Encoder(depth=2, dim=128, num_heads=2, cube_m=16, scale=0.5, out_proj=out_proj, device=cuda)
+    cpu = Encoder(depth=2, dim=128, num_heads=2, cube_m=16, scale=0.5, out_proj=out_proj, dtype=torch.float32,
+                  device="cpu")
+    cpu.load_state_dict({k: v.float().cpu() for k, v in gpu.state_dict().items()})
+    for bg, bc in zip(gpu.blocks, cpu.blocks):
+        bc.attn = OracleAttention(bg.attn)
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 50, 128, generator=g).half()
+    target = torch.randn(2, 50, 128, generator=g)
+
+    out_g = gpu(x.to(cuda))
+    loss_g = nn.functional.mse_loss(out_g.float(), target.to(cuda))
+    loss_g.backward()
+    out_c = cpu(x.float())
+    loss_c = nn.functional.mse_loss(out_c, target)
+    loss_c.backward()
+    torch.cuda.synchronize()
+
+    assert O.rel_l2(out_g.float().cpu(), out_c.detach()) <= 3e-3
+    assert abs(loss_g.item() - loss_c.item()) <= 3e-3 * abs(loss_c.item())
+    params_c = dict(cpu.named_parameters())
+    for name, p in gpu.named_parameters():
+        pc = params_c[name]
+        assert p.grad is not None and pc.grad is not None, name
+        err = O.rel_l2(p.grad.float().cpu(), pc.grad)
+        assert err <= 1.5e-2, f"{name}: {err:.2e}"
