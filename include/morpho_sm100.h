@@ -50,6 +50,11 @@ extern "C" {
 #define MORPHO_PROJ_HARDTANH01 1  /* min(1, max(0, (z + 1) / 2)), gradient 1/2 on -1 < z < 1 */
 #define MORPHO_PROJ_IDENTITY 2    /* z */
 
+/* Score / aggregation (the reference's morfology/soft_morph.cuh:10-77, dead code there). */
+#define MORPHO_SCORE_SOFTMAX 0   /* out = softmax_j(S_ij) . V (the reference attention kernels) */
+#define MORPHO_SCORE_DILATION 1  /* out_ic = tau log sum_j exp((S_ij + V_jc) / tau): soft max-plus */
+#define MORPHO_SCORE_EROSION 2   /* out_ic = -tau log sum_j exp(-(S_ij + V_jc) / tau): soft min-plus */
+
 /* Gradient semantics of the backward. */
 #define MORPHO_GRAD_FULL 0      /* true gradient of the forward (default) */
 #define MORPHO_GRAD_REFERENCE 1 /* reference kernel semantics: query-code and query-bias
@@ -68,6 +73,10 @@ typedef struct morpho_problem {
     int32_t mask_diag;  /* 1: also drop key j == query i (reference MORPHO_MASK_DIAG,
                            utils/declarations.cuh:79-82, attention.cu:131, :363); a query row
                            left with no key gives out = 0, lse = -FLT_MAX and no gradient */
+    int32_t score;      /* MORPHO_SCORE_* (0 = softmax attention).  With DILATION / EROSION the
+                           forward writes lse = 0 (not defined for them), grad_mode must be FULL,
+                           and tau is a fixed hyper-parameter (no gradient) */
+    float tau;          /* temperature of DILATION / EROSION, > 0 (ignored for SOFTMAX) */
 } morpho_problem_t;
 
 /* Bytes of device workspace the forward / backward need for problem p (0 on invalid p). */

@@ -6,9 +6,9 @@ backed by hand-written tcgen05/TMA kernels behind the C ABI in ``include/morpho_
 """
 
 from .autograd import (MorphoAttention, MorphoAttentionFunction, attention_options, get_cube_projection,
-                       get_grad_mode, get_mask_diag, grad_mode, morpho_attention, set_cube_projection, set_grad_mode,
-                       set_mask_diag)
+                       get_grad_mode, get_mask_diag, get_score, grad_mode, morpho_attention, set_cube_projection,
+                       set_grad_mode, set_mask_diag, set_score)
 
 __all__ = ["MorphoAttention", "MorphoAttentionFunction", "morpho_attention", "set_grad_mode", "get_grad_mode",
            "grad_mode", "set_cube_projection", "get_cube_projection", "set_mask_diag", "get_mask_diag",
-           "attention_options"]
+           "set_score", "get_score", "attention_options"]

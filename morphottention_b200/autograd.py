@@ -102,11 +102,34 @@ def get_mask_diag() -> bool:
     return bool(ops.get_mask_diag())
 
 
+SCORES = {"softmax": 0, "dilation": 1, "erosion": 2}
+
+
+def set_score(score: str, tau: float = 1.0) -> tuple:
+    """Select how the keys are aggregated for subsequent calls: ``"softmax"`` (attention,
+    the default), or the soft-morphology score of the reference's
+    ``csrc/cuda/morfology/soft_morph.cuh`` (unused there): ``"dilation"``,
+    ``out_ic = tau * logsumexp_j((S_ij + V_jc) / tau)``, and ``"erosion"``, its min-plus mirror.
+    ``tau`` is a fixed temperature (no gradient).  Process-wide; returns the previous
+    ``(score, tau)``."""
+    if score not in SCORES:
+        raise ValueError(f"score must be one of {tuple(SCORES)}")
+    prev = get_score()
+    ops.set_score(SCORES[score], float(tau))
+    return prev
+
+
+def get_score() -> tuple:
+    return {v: k for k, v in SCORES.items()}[int(ops.get_score())], float(ops.get_score_tau())
+
+
 @contextlib.contextmanager
-def attention_options(projection: str | None = None, mask_diag: bool | None = None):
-    """Scoped :func:`set_cube_projection` / :func:`set_mask_diag`."""
+def attention_options(projection: str | None = None, mask_diag: bool | None = None, score: str | None = None,
+                      tau: float = 1.0):
+    """Scoped :func:`set_cube_projection` / :func:`set_mask_diag` / :func:`set_score`."""
     prev_p = set_cube_projection(projection) if projection is not None else None
     prev_m = set_mask_diag(mask_diag) if mask_diag is not None else None
+    prev_s = set_score(score, tau) if score is not None else None
     try:
         yield
     finally:
@@ -114,6 +137,8 @@ def attention_options(projection: str | None = None, mask_diag: bool | None = No
             set_cube_projection(prev_p)
         if prev_m is not None:
             set_mask_diag(prev_m)
+        if prev_s is not None:
+            set_score(*prev_s)
 
 
 @contextlib.contextmanager

@@ -26,6 +26,10 @@ MORPHO_PROJ_HARDTANH01 = 1
 MORPHO_PROJ_IDENTITY = 2
 PROJECTIONS = {"sigmoid": MORPHO_PROJ_SIGMOID, "hardtanh01": MORPHO_PROJ_HARDTANH01,
                "identity": MORPHO_PROJ_IDENTITY}
+MORPHO_SCORE_SOFTMAX = 0
+MORPHO_SCORE_DILATION = 1
+MORPHO_SCORE_EROSION = 2
+SCORES = {"softmax": MORPHO_SCORE_SOFTMAX, "dilation": MORPHO_SCORE_DILATION, "erosion": MORPHO_SCORE_EROSION}
 
 EXPORTED = (
     "morpho_sm100_forward_workspace_size",
@@ -54,7 +58,8 @@ EXPORTED = (
 class MorphoProblem(ctypes.Structure):
     _fields_ = [("B", ctypes.c_int32), ("N", ctypes.c_int32), ("D", ctypes.c_int32), ("H", ctypes.c_int32),
                 ("cube_m", ctypes.c_int32), ("scale", ctypes.c_float), ("causal", ctypes.c_int32),
-                ("grad_mode", ctypes.c_int32), ("projection", ctypes.c_int32), ("mask_diag", ctypes.c_int32)]
+                ("grad_mode", ctypes.c_int32), ("projection", ctypes.c_int32), ("mask_diag", ctypes.c_int32),
+                ("score", ctypes.c_int32), ("tau", ctypes.c_float)]
 
 
 class MorphoError(RuntimeError):
@@ -122,11 +127,13 @@ def lib() -> ctypes.CDLL:
 
 
 def problem(B, N, D, H, cube_m, scale=1.0, causal=False, grad_mode=MORPHO_GRAD_FULL, projection=MORPHO_PROJ_SIGMOID,
-            mask_diag=False) -> MorphoProblem:
+            mask_diag=False, score=MORPHO_SCORE_SOFTMAX, tau=1.0) -> MorphoProblem:
     if isinstance(projection, str):
         projection = PROJECTIONS[projection]
+    if isinstance(score, str):
+        score = SCORES[score]
     return MorphoProblem(B, N, D, H, cube_m, float(scale), 1 if causal else 0, int(grad_mode), int(projection),
-                         1 if mask_diag else 0)
+                         1 if mask_diag else 0, int(score), float(tau))
 
 
 def last_error() -> str:

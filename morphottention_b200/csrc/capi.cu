@@ -18,6 +18,9 @@ constexpr int kTile = 128;
 static_assert(kProjSigmoid == MORPHO_PROJ_SIGMOID && kProjHardTanh01 == MORPHO_PROJ_HARDTANH01 &&
                   kProjIdentity == MORPHO_PROJ_IDENTITY,
               "projection codes");
+static_assert(kScoreSoftmax == MORPHO_SCORE_SOFTMAX && kScoreDilation == MORPHO_SCORE_DILATION &&
+                  kScoreErosion == MORPHO_SCORE_EROSION,
+              "score codes");
 
 int validate(const morpho_problem_t* p, Shape* s) {
     if (p == nullptr) return set_error(MORPHO_ERR_INVALID, "problem is NULL");
@@ -36,6 +39,14 @@ int validate(const morpho_problem_t* p, Shape* s) {
         return set_error(MORPHO_ERR_INVALID, "projection %d unknown", p->projection);
     if (p->mask_diag != 0 && p->mask_diag != 1)
         return set_error(MORPHO_ERR_INVALID, "mask_diag must be 0 or 1 (got %d)", p->mask_diag);
+    if (p->score != MORPHO_SCORE_SOFTMAX && p->score != MORPHO_SCORE_DILATION && p->score != MORPHO_SCORE_EROSION)
+        return set_error(MORPHO_ERR_INVALID, "score %d unknown", p->score);
+    if (p->score != MORPHO_SCORE_SOFTMAX) {
+        if (!(p->tau > 0.0f) || p->tau > 1e30f)
+            return set_error(MORPHO_ERR_INVALID, "tau must be positive and finite (got %g)", static_cast<double>(p->tau));
+        if (p->grad_mode != MORPHO_GRAD_FULL)
+            return set_error(MORPHO_ERR_INVALID, "grad_mode reference applies to the softmax score only");
+    }
     const long long T = static_cast<long long>(p->B) * p->N;
     if (T > (1LL << 30) || static_cast<long long>(p->B) * p->H * p->N * 128 > (1LL << 40))
         return set_error(MORPHO_ERR_INVALID, "problem too large: B*N = %lld", T);
@@ -53,7 +64,18 @@ int validate(const morpho_problem_t* p, Shape* s) {
     s->grad_mode = p->grad_mode;
     s->proj = p->projection;
     s->mask_diag = p->mask_diag != 0;
+    s->score = p->score;
+    s->tau = p->tau;
     return MORPHO_OK;
+}
+
+// The attention step of the forward: softmax . V, or the soft-morphology aggregation (which
+// has no lse: 0 is written).
+int run_attention_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& proj, __half* out, float* lse,
+                      cudaStream_t st) {
+    if (s.score == kScoreSoftmax) return launch_attn_fwd(dev, s, proj, out, lse, st);
+    MORPHO_CUDA_TRY(cudaMemsetAsync(lse, 0, static_cast<size_t>(s.B) * s.H * s.N * sizeof(float), st));
+    return launch_soft_morph_fwd(s, proj, out, proj.o2, st);  // o2 kept by forward_save only
 }
 
 int check_ptr(const void* ptr, const char* name) {
@@ -95,6 +117,7 @@ struct BwdPlan {
     ProjOut proj;
     __half* qaug;
     float* L;
+    float* dqb;  // soft-morphology score: dL/dqbias, [B*H, Npad]
     float* dq;
     float* dk;
     float* dcb;
@@ -111,6 +134,7 @@ void plan_saved(Carve& c, const Shape& s, ProjOut* o) {
     plan_proj(c, s, o);
     o->phi = c.take<float>(BH * s.N * s.m);
     o->kdq = c.take<__half>(BH * s.N * 2 * s.m);
+    o->o2 = s.score != kScoreSoftmax ? c.take<float>(BH * s.N * s.hd) : nullptr;
 }
 
 // The backward's own buffers, after the projection outputs.
@@ -119,6 +143,7 @@ void plan_bwd_rest(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     const size_t Npad = (s.N + kTile - 1) / kTile * kTile;
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
+    b->dqb = s.score != kScoreSoftmax ? c.take<float>(BH * Npad) : nullptr;
     b->dq = c.take<float>(BH * s.N * s.m);
     b->dk = c.take<float>(BH * s.N * s.m);
     b->dcb = c.take<float>(BH * Npad);
@@ -169,25 +194,33 @@ int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan
                             const void* X, const void* W_phi, const void* gate_q, const void* gate_k,
                             const void* W_V, const void* out, const float* lse, void* dX, void* dW_phi,
                             void* d_gate_q, void* d_gate_k, void* dW_V, float* dweights_f32, cudaStream_t st,
-                            cudaEvent_t bucket_ready = nullptr) {
+                            cudaEvent_t bucket_ready = nullptr, bool o2_ready = false) {
     const __half* x = static_cast<const __half*>(X);
     const __half* wphi = static_cast<const __half*>(W_phi);
     const __half* wv = static_cast<const __half*>(W_V);
     const __half* gq = static_cast<const __half*>(gate_q);
     const __half* gk = static_cast<const __half*>(gate_k);
-    MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse, b.proj.qb,
-                            b.L, b.qaug, st));
-    MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
-    AttnBwdIO io;
-    io.dO = static_cast<const __half*>(grad_out);
-    io.L = b.L;
-    io.qaug = b.qaug;
-    io.dcat = b.dcat;
-    io.dk = b.dk;
-    io.dcb = b.dcb;
-    io.dq = b.dq;
-    MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
-    MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
+    if (s.score == kScoreSoftmax) {
+        MORPHO_TRY(launch_delta(s, static_cast<const __half*>(grad_out), static_cast<const __half*>(out), lse,
+                                b.proj.qb, b.L, b.qaug, st));
+        MORPHO_CUDA_TRY(cudaMemsetAsync(b.dq, 0, static_cast<size_t>(s.B) * s.H * s.N * s.m * sizeof(float), st));
+        AttnBwdIO io;
+        io.dO = static_cast<const __half*>(grad_out);
+        io.L = b.L;
+        io.qaug = b.qaug;
+        io.dcat = b.dcat;
+        io.dk = b.dk;
+        io.dcb = b.dcb;
+        io.dq = b.dq;
+        MORPHO_TRY(launch_attn_bwd(dev, s, b.proj, io, st));
+    } else {
+        // soft-morphology score: the forward's m + log2(l) (kept by forward_save, else
+        // recomputed), then the two backward kernels
+        if (!o2_ready) MORPHO_TRY(launch_soft_morph_fwd(s, b.proj, nullptr, b.proj.o2, st));
+        MORPHO_TRY(launch_soft_morph_bwd(s, b.proj, static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb,
+                                         b.dk, b.dcb, b.dcat, st));
+    }
+    MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, b.dqb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
     MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
     MORPHO_TRY(launch_reduce_weights(s, b.dw_part, b.splits, b.gate_part, b.gate_blocks, dweights_f32,
                                      static_cast<__half*>(dW_phi), static_cast<__half*>(dW_V),
@@ -263,7 +296,7 @@ int morpho_sm100_forward(const morpho_problem_t* p, const void* X, const void* W
     const __half* x = static_cast<const __half*>(X);
     MORPHO_TRY(launch_proj(dev, s, x, static_cast<const __half*>(W_phi), static_cast<const __half*>(W_V),
                            static_cast<const __half*>(gate_q), static_cast<const __half*>(gate_k), f.proj, st));
-    MORPHO_TRY(launch_attn_fwd(dev, s, f.proj, static_cast<__half*>(out), lse, st));
+    MORPHO_TRY(run_attention_fwd(dev, s, f.proj, static_cast<__half*>(out), lse, st));
     return MORPHO_OK;
 }
 
@@ -341,7 +374,7 @@ int morpho_sm100_forward_save(const morpho_problem_t* p, const void* X, const vo
     MORPHO_TRY(launch_proj(dev, s, static_cast<const __half*>(X), static_cast<const __half*>(W_phi),
                            static_cast<const __half*>(W_V), static_cast<const __half*>(gate_q),
                            static_cast<const __half*>(gate_k), o, st));
-    MORPHO_TRY(launch_attn_fwd(dev, s, o, static_cast<__half*>(out), lse, st));
+    MORPHO_TRY(run_attention_fwd(dev, s, o, static_cast<__half*>(out), lse, st));
     return MORPHO_OK;
 }
 
@@ -376,7 +409,7 @@ int backward_saved_impl(const morpho_problem_t* p, const void* grad_out, const v
     plan_bwd_rest(c, s, dev.sms, &b);
     return run_backward_after_proj(dev, s, b, grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q,
                                    d_gate_k, dW_V, dweights_f32, static_cast<cudaStream_t>(stream),
-                                   static_cast<cudaEvent_t>(bucket_ready));
+                                   static_cast<cudaEvent_t>(bucket_ready), /*o2_ready=*/true);
 }
 }  // namespace
 

@@ -15,6 +15,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kProjSigmoid = 0;
 constexpr int kProjHardTanh01 = 1;
 constexpr int kProjIdentity = 2;
+// Scores (the values of MORPHO_SCORE_*).
+constexpr int kScoreSoftmax = 0;
+constexpr int kScoreDilation = 1;
+constexpr int kScoreErosion = 2;
 
 struct Shape {
     int B, N, D, H, m, hd;
@@ -23,6 +27,8 @@ struct Shape {
     int grad_mode;
     int proj = 0;            // MORPHO_PROJ_*
     bool mask_diag = false;  // drop key j == query i
+    int score = 0;           // kScore*
+    float tau = 1.0f;        // soft-morphology temperature
     long long tokens() const { return static_cast<long long>(B) * N; }
     int Hm() const { return H * m; }
     // dZ columns are padded to a multiple of 64 so that no 64-wide K block of the dX
@@ -49,6 +55,9 @@ struct ProjOut {
     // dS . hi + dS . lo: every row of dS sums to zero, so the centering term drops out
     // exactly while the fp16 rounding of the large mean of k no longer leaks into dq.
     __half* kdq = nullptr;
+    // Soft-morphology score (training pair / backward only): m + log2(l) per (row, channel),
+    // fp32 [B*H, N, hd], written by the forward for the backward.
+    float* o2 = nullptr;
 };
 
 // X [T, D] @ [W_phi | W_V] with the sigmoid / gating / bias epilogue.
@@ -93,9 +102,18 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
                  __half* qaug, cudaStream_t stream);
 
 // dZ = dL/dphi * phi (1 - phi) into dcat[:, h*m + c] and per-block gate partials.
+// Soft-morphology score (softmorph.cu): forward out (fp16, may be NULL) and o2 = m + log2(l)
+// per (row, channel) [B*H, N, hd] fp32 (may be NULL); backward dq, dqb ([B*H, Npad]), dk, dcb
+// and the dV columns of dcat from the forward's o2.
+int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, cudaStream_t stream);
+int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, float* dq, float* dqb,
+                          float* dk, float* dcb, __half* dcat, cudaStream_t stream);
+
+// dqb (dL/dqbias, [B*H, Npad]) may be NULL: the softmax score's rows are shift-invariant, so
+// its query-bias gradient is identically 0.
 int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,
-              const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part, int gate_blocks,
-              cudaStream_t stream);
+              const float* dqb, const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part,
+              int gate_blocks, cudaStream_t stream);
 int dz_gate_blocks(const Shape& s);
 
 // Sum the dW split partials and gate partials: either into an fp32 bucket (layout of

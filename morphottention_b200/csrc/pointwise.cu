@@ -91,6 +91,7 @@ __device__ __forceinline__ float cube_grad(float phi) {
 template <bool FULL, int PROJ>
 __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, const float* __restrict__ dq,
                                                  const float* __restrict__ dk, const float* __restrict__ dcb,
+                                                 const float* __restrict__ dqb,
                                                  const __half* __restrict__ gq, const __half* __restrict__ gk,
                                                  __half* __restrict__ dcat, float* __restrict__ gate_part, int T,
                                                  int N, int Npad, int H, int m, int Hp, int Cp, int tokens_per_block) {
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
                 const float4 f = *reinterpret_cast<const float4*>(phi + off);
                 const float4 kk = *reinterpret_cast<const float4*>(dk + off);
                 const float db = dcb[row * Npad + n];
+                const float dqbv = dqb != nullptr ? dqb[row * Npad + n] : 0.f;
                 float4 qq = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (FULL) qq = *reinterpret_cast<const float4*>(dq + off);
                 const float fv[4] = {f.x, f.y, f.z, f.w};
@@ -133,14 +135,15 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
                     //   dL/dphi = dq*gq + dk*gk + dcb*gq*gk = dq*gq + dk_c*gk
                     //   d gate_k += dk*phi + dcb*gq*phi = dk_c*phi
                     //   d gate_q += dq*phi + dcb*gk*phi
-                    // (the query-bias terms are identically 0)
+                    //   d gate_k += dqb*q = dqb*gq*phi  (qbias = sum_c gk q: 0 for the softmax
+                    //   score, whose rows are shift-invariant; dq already holds the q path)
                     float dphi = kv[i] * g_k[i];
                     if (FULL) dphi = fmaf(qv[i], g_q[i], dphi);
                     dz[i] = dphi * cube_grad<PROJ>(fv[i]);
                     float gqi = db * g_k[i] * fv[i];
                     if (FULL) gqi = fmaf(qv[i], fv[i], gqi);
                     aq[i] += gqi;
-                    ak[i] += kv[i] * fv[i];
+                    ak[i] += (kv[i] + dqbv * g_q[i]) * fv[i];
                 }
                 out = make_uint2(pack_half2(dz[0], dz[1]), pack_half2(dz[2], dz[3]));
             }
@@ -276,8 +279,8 @@ int dz_gate_blocks(const Shape& s) {
 int dz_threads(const Shape& s) { return min(256, (s.Hp() / 4 + 31) / 32 * 32); }
 
 int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk, const float* dcb,
-              const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part, int gate_blocks,
-              cudaStream_t stream) {
+              const float* dqb, const __half* gate_q, const __half* gate_k, __half* dcat, float* gate_part,
+              int gate_blocks, cudaStream_t stream) {
     const int T = static_cast<int>(s.tokens());
     const int tpb = (T + gate_blocks - 1) / gate_blocks;
     auto kern = s.grad_mode == MORPHO_GRAD_FULL
@@ -288,7 +291,7 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
                        : s.proj == kProjHardTanh01 ? dz_kernel<false, kProjHardTanh01>
                                                    : dz_kernel<false, kProjIdentity>);
     prof_begin(stream);
-    kern<<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, gate_q, gate_k, dcat, gate_part, T, s.N,
+    kern<<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, dqb, gate_q, gate_k, dcat, gate_part, T, s.N,
                                                     npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     MORPHO_LAUNCH_CHECK("dz");
     return MORPHO_OK;

@@ -9,7 +9,8 @@
 // set_grad_mode / get_grad_mode select full gradients (default) or the reference
 // kernel's gradient semantics; set_cube_projection / set_mask_diag (and their getters)
 // select the reference's compile-time variants (HardTanh01 / Identity projection, the
-// diagonal mask) for the calls that follow; forward_save / backward_saved keep the projection of the
+// diagonal mask) for the calls that follow; set_score / get_score / get_score_tau select the
+// soft-morphology aggregation (the reference's unused morfology/soft_morph.cuh); forward_save / backward_saved keep the projection of the
 // forward for the backward instead of recomputing it (the autograd Function uses them).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -26,6 +27,8 @@ namespace {
 std::atomic<int> g_grad_mode{MORPHO_GRAD_FULL};
 std::atomic<int> g_projection{MORPHO_PROJ_SIGMOID};
 std::atomic<int> g_mask_diag{0};
+std::atomic<int> g_score{MORPHO_SCORE_SOFTMAX};
+std::atomic<float> g_tau{1.0f};
 
 void check(const at::Tensor& t, const char* name) {
     TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
@@ -45,6 +48,8 @@ morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double 
     p.grad_mode = g_grad_mode.load();
     p.projection = g_projection.load();
     p.mask_diag = g_mask_diag.load();
+    p.score = g_score.load();
+    p.tau = g_tau.load();
     return p;
 }
 
@@ -197,6 +202,18 @@ int64_t set_mask_diag(int64_t on) {
 
 int64_t get_mask_diag() { return g_mask_diag.load(); }
 
+int64_t set_score(int64_t score, double tau) {
+    TORCH_CHECK(score == MORPHO_SCORE_SOFTMAX || score == MORPHO_SCORE_DILATION || score == MORPHO_SCORE_EROSION,
+                "score must be 0 (softmax), 1 (dilation) or 2 (erosion)");
+    TORCH_CHECK(score == MORPHO_SCORE_SOFTMAX || (tau > 0.0 && tau < 1e30), "tau must be positive and finite");
+    g_tau.store(static_cast<float>(tau));
+    return g_score.exchange(static_cast<int>(score));
+}
+
+int64_t get_score() { return g_score.load(); }
+
+double get_score_tau() { return static_cast<double>(g_tau.load()); }
+
 }  // namespace
 
 TORCH_LIBRARY(morphottention, m) {
@@ -218,6 +235,9 @@ TORCH_LIBRARY(morphottention, m) {
     m.def("get_cube_projection() -> int", &get_cube_projection);
     m.def("set_mask_diag(int on) -> int", &set_mask_diag);
     m.def("get_mask_diag() -> int", &get_mask_diag);
+    m.def("set_score(int score, float tau) -> int", &set_score);
+    m.def("get_score() -> int", &get_score);
+    m.def("get_score_tau() -> float", &get_score_tau);
 }
 
 TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {

@@ -86,13 +86,15 @@ class _DataParallelFunction(torch.autograd.Function):
         if not x.is_cuda:
             raise ValueError("MorphoAttention expects a CUDA tensor")
         x = x.contiguous()
-        from .autograd import CUBE_PROJECTIONS, get_cube_projection, get_mask_diag
+        from .autograd import CUBE_PROJECTIONS, SCORES, get_cube_projection, get_mask_diag, get_score
         out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
         ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
         ctx.H, ctx.cube_m, ctx.scale, ctx.causal, ctx.group = H, cube_m, scale, causal, group
         # the options the forward ran with, for the backward's problem
         ctx.projection = CUBE_PROJECTIONS[get_cube_projection()]
         ctx.mask_diag = get_mask_diag()
+        name, tau = get_score()
+        ctx.score, ctx.tau = SCORES[name], tau
         return out
 
     @staticmethod
@@ -103,7 +105,7 @@ class _DataParallelFunction(torch.autograd.Function):
         grad_out = grad_out.contiguous()
         B, N, D = x.shape
         p = capi.problem(B, N, D, ctx.H, ctx.cube_m, ctx.scale, ctx.causal, grad_mode=GRAD_MODES[get_grad_mode()],
-                         projection=ctx.projection, mask_diag=ctx.mask_diag)
+                         projection=ctx.projection, mask_diag=ctx.mask_diag, score=ctx.score, tau=ctx.tau)
         dX = torch.empty_like(x)
         grads = [torch.empty_like(t) for t in (W_phi, gate_q, gate_k, W_V)]
         bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=x.device)

@@ -204,3 +204,58 @@ def soft_hamming_score(phi_i, phi_j, gate_q, gate_k, scale: float):
 
 __all__ = ["LOG2E", "GRAD_MODES", "project", "forward", "forward_backward", "forward_chunked",
            "rel_l2", "soft_hamming_score"]
+
+
+SCORES = ("softmax", "dilation", "erosion")
+
+
+def soft_morph_forward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+                       causal: bool = False, score: str = "dilation", tau: float = 1.0,
+                       projection: str = "sigmoid", mask_diag: bool = False):
+    """The soft-morphology score of ``csrc/cuda/morfology/soft_morph.cuh:10-77`` (dead code in
+    the reference: no kernel calls it) in place of softmax . V:
+    ``out[i, c] = sgn * tau * logsumexp_j(sgn * (S_ij + V_jc) / tau)``, a soft max-plus
+    (``dilation``, sgn = +1) or min-plus (``erosion``, sgn = -1) aggregation of the values
+    over the keys (``morph_accumulate`` / ``lse_finalize``, ``:33-61``), with the
+    morphological score ``S_ij = scale * (2 q_i.k_j - qbias_i - cbias_j)`` of the attention
+    path.  Masked keys (causal, diagonal, padding) are left out; a row without keys gives 0.
+    Returns ``out [B,N,D]``.  The gradient w.r.t. S and V is ``P_ijc = exp(sgn (S_ij + V_jc -
+    out_ic) / tau)`` (``morph_weight``, ``:63-67``); ``tau`` is a fixed hyper-parameter here.
+    """
+    if score not in ("dilation", "erosion"):
+        raise ValueError("score must be 'dilation' or 'erosion'")
+    sgn = 1.0 if score == "dilation" else -1.0
+    B, N, D = x.shape
+    _, q, k, qbias, cbias, v = project(x, W_phi, gate_q, gate_k, W_V, H, cube_m, projection)
+    s = scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))  # [B,H,N,N]
+    a = sgn * (s.unsqueeze(-1) + v.unsqueeze(-3)) / tau  # [B,H,N(i),N(j),hd]
+    mask = None
+    if causal:
+        mask = torch.ones(N, N, dtype=torch.bool, device=x.device).triu(1)
+    if mask_diag:
+        eye = torch.eye(N, dtype=torch.bool, device=x.device)
+        mask = eye if mask is None else (mask | eye)
+    if mask is not None:
+        a = a.masked_fill(mask.unsqueeze(-1), float("-inf"))
+        dead = mask.all(dim=-1)  # [N]
+        a = a.masked_fill(dead.view(N, 1, 1), 0.0)
+        o = sgn * tau * torch.logsumexp(a, dim=-2)
+        o = o.masked_fill(dead.view(N, 1), 0.0)
+    else:
+        o = sgn * tau * torch.logsumexp(a, dim=-2)  # [B,H,N,hd]
+    return o.permute(0, 2, 1, 3).reshape(B, N, D)
+
+
+def soft_morph_forward_backward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+                                causal: bool = False, score: str = "dilation", tau: float = 1.0, grad_out=None,
+                                dtype=torch.float32, projection: str = "sigmoid", mask_diag: bool = False):
+    """Forward plus the backward of ``sum(out * grad_out)`` for :func:`soft_morph_forward`."""
+    leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in (x, W_phi, gate_q, gate_k, W_V)]
+    with torch.enable_grad():
+        out = soft_morph_forward(*leaves, H, cube_m, scale, causal, score, tau, projection, mask_diag)
+        g = torch.ones_like(out) if grad_out is None else grad_out.detach().to(dtype)
+        grads = torch.autograd.grad(out, leaves, grad_outputs=g)
+    names = ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V")
+    res = {"out": out.detach()}
+    res.update({n: gr.detach() for n, gr in zip(names, grads)})
+    return res

@@ -1,0 +1,100 @@
+"""The soft-morphology score (reference csrc/cuda/morfology/soft_morph.cuh:10-77, unused by
+the reference's kernels): out_ic = sgn tau logsumexp_j(sgn (S_ij + V_jc) / tau), soft dilation
+(sgn = +1) and erosion (sgn = -1), through the C ABI and the module, against the fp32 oracle
+restatement with the attention path's tolerances (rel-L2 <= 1e-3 out, <= 5e-3 gradients)."""
+
+import pytest
+import torch
+
+import morphottention_b200 as M
+from morphottention_b200 import capi
+from morphottention_b200.configs import MorphoConfig
+from oracle import morpho_oracle as O
+
+from .helpers import compare, gate_tolerance, inputs
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    MorphoConfig("m16_hd64", 2, 197, 128, 2, 16, 1.0, False, 41),
+    MorphoConfig("m32_causal", 1, 300, 256, 4, 32, 0.5, True, 42),
+    MorphoConfig("m64_hd128", 1, 130, 256, 2, 64, 0.3, False, 43),
+    MorphoConfig("m16_hd32", 2, 64, 128, 4, 16, 1.0, True, 44),
+]
+
+
+def run_cuda_morph(cfg, inp, grad_out, score, tau, mask_diag=False, projection="sigmoid"):
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score=score, tau=tau,
+                     mask_diag=mask_diag, projection=projection)
+    x = inp["x"]
+    out = torch.empty_like(x)
+    lse = torch.full((cfg.B * cfg.H, cfg.N), 7.0, dtype=torch.float32, device=x.device)
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    capi.forward(p, *args, out, lse)
+    grads = [torch.empty_like(t) for t in args]
+    capi.backward(p, grad_out, *args, out, lse, *grads)
+    torch.cuda.synchronize()
+    assert capi.device_status(reset=True) == 0
+    assert torch.all(lse == 0), "lse is not defined for the soft-morphology score: 0 is written"
+    res = {"out": out}
+    res.update(dict(zip(("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), grads)))
+    return res
+
+
+def oracle(cfg, inp, grad_out, score, tau, mask_diag=False, projection="sigmoid"):
+    t = {k: v.cpu() for k, v in inp.items()}
+    return O.soft_morph_forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m,
+                                         cfg.scale, cfg.causal, score, tau, grad_out=grad_out.cpu(),
+                                         projection=projection, mask_diag=mask_diag)
+
+
+@pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
+@pytest.mark.parametrize("score,tau", [("dilation", 1.0), ("erosion", 0.5)])
+def test_soft_morph_parity(cuda, cfg, score, tau):
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    ours = run_cuda_morph(cfg, inp, g, score, tau)
+    ref = oracle(cfg, inp, g, score, tau)
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_soft_morph_with_diagonal_mask_and_projection(cuda):
+    cfg = MorphoConfig("diag", 1, 150, 128, 2, 32, 0.8, True, 45)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    ours = run_cuda_morph(cfg, inp, g, "dilation", 0.8, mask_diag=True, projection="hardtanh01")
+    ref = oracle(cfg, inp, g, "dilation", 0.8, mask_diag=True, projection="hardtanh01")
+    # query 0 has no key (causal + diagonal): out 0 there
+    assert torch.all(ours["out"][:, 0] == 0)
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_soft_morph_through_module(cuda):
+    cfg = MorphoConfig("mod", 2, 100, 128, 4, 16, 1.0, False, 46)
+    inp = inputs(cfg, cuda, random_gates=True)
+    mod = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=cuda)
+    with torch.no_grad():
+        for n in ("W_phi", "W_V", "gate_q", "gate_k"):
+            getattr(mod, n).copy_(inp[n])
+    x = inp["x"].clone().requires_grad_(True)
+    with M.attention_options(score="erosion", tau=0.6):
+        assert M.get_score() == ("erosion", pytest.approx(0.6))
+        out = mod(x)
+        out.float().sum().backward()
+    assert M.get_score()[0] == "softmax"
+    ref = oracle(cfg, inp, torch.ones_like(inp["x"]), "erosion", 0.6)
+    ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
+            "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_soft_morph_invalid_problems(cuda):
+    L = capi.lib()
+    import ctypes
+    for p in (capi.problem(1, 64, 128, 2, 16, score=3), capi.problem(1, 64, 128, 2, 16, score="dilation", tau=0.0),
+              capi.problem(1, 64, 128, 2, 16, score="erosion", tau=-1.0),
+              capi.problem(1, 64, 128, 2, 16, score="dilation", grad_mode=capi.MORPHO_GRAD_REFERENCE)):
+        assert L.morpho_sm100_forward_workspace_size(ctypes.byref(p)) == 0
+        assert capi.last_error()
+    with pytest.raises(ValueError):
+        M.set_score("max")
