@@ -50,6 +50,10 @@ def test_invalid_problems_rejected():
     bad_mask = capi.problem(1, 16, 64, 2, 16)
     bad_mask.mask_diag = 2
     bad.append(bad_mask)
+    # soft-morphology score: unknown score, non-positive tau, reference gradient mode
+    bad += [capi.problem(1, 16, 64, 2, 16, score=3), capi.problem(1, 16, 64, 2, 16, score="dilation", tau=0.0),
+            capi.problem(1, 16, 64, 2, 16, score="erosion", tau=-2.0),
+            capi.problem(1, 16, 64, 2, 16, score="dilation", grad_mode=capi.MORPHO_GRAD_REFERENCE)]
     for p in bad:
         assert L.morpho_sm100_forward_workspace_size(ctypes.byref(p)) == 0
         rc = L.morpho_sm100_forward(ctypes.byref(p), *([None] * 8), 0, None)
@@ -73,3 +77,13 @@ def test_misaligned_pointer_rejected():
     rc = L.morpho_sm100_forward(ctypes.byref(p), *ptrs, 1 << 30, None)
     assert rc == capi.MORPHO_ERR_INVALID
     assert "aligned" in capi.last_error()
+
+
+def test_soft_morph_workspace_keeps_statistics():
+    """With the soft-morphology score the training pair's saved buffer also holds the forward's
+    m + log2(l) per (row, channel) (fp32 [B*H, N, hd]); the softmax score does not need it."""
+    L = capi.lib()
+    a = capi.problem(2, 100, 128, 2, 16)
+    b = capi.problem(2, 100, 128, 2, 16, score="dilation", tau=0.5)
+    extra = L.morpho_sm100_saved_bytes(ctypes.byref(b)) - L.morpho_sm100_saved_bytes(ctypes.byref(a))
+    assert 2 * 2 * 100 * 64 * 4 <= extra <= 2 * 2 * 100 * 64 * 4 + 256
