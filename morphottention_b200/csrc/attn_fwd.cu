@@ -300,6 +300,22 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             const bool grow = mt > m_ref + kRescaleThreshold;
             const float m_new = grow ? mt : m_ref;
             const float alpha = grow ? ex2(m_ref - m_new) : 1.0f;  // 0 when m_ref = -inf
+            l *= alpha;
+            m_ref = m_new;
+            // The exponentials first, packed in place into sv[0, 64): they only need the new
+            // reference max, so they overlap the previous P.V MMA, which still reads P and O.
+            // m_ref is -inf only while every key of the row so far was masked (causal plus
+            // diagonal mask at query 0): then all of this tile's P are 0, and l stays 0.
+            float lsum = 0.f;
+            const float nm = m_ref == -INFINITY ? 0.f : -m_ref;
+#pragma unroll
+            for (int i = 0; i < kTile / 2; ++i) {
+                const float p0 = ex2(fmaf(u2f(sv[2 * i]), c2, nm));
+                const float p1 = ex2(fmaf(u2f(sv[2 * i + 1]), c2, nm));
+                lsum += p0 + p1;
+                sv[i] = pack_half2(p0, p1);
+            }
+            l += lsum;
             if (j > 0) {
                 // P and O are both used by the previous P.V MMA: wait for it.
                 if (!mbar_wait_warp(o_done, (j - 1) & 1, args.status, K_ATTN_FWD, 10)) {
@@ -320,25 +336,8 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     tmem_st_wait();
                 }
             }
-            l *= alpha;
-            m_ref = m_new;
-            // m_ref is -inf only while every key of the row so far was masked (causal plus
-            // diagonal mask at query 0): then all of this tile's P are 0, and l stays 0.
-            float lsum = 0.f;
-            const float nm = m_ref == -INFINITY ? 0.f : -m_ref;
 #pragma unroll
-            for (int c = 0; c < kTile; c += 32) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2(fmaf(u2f(sv[c + 2 * i]), c2, nm));
-                    const float p1 = ex2(fmaf(u2f(sv[c + 2 * i + 1]), c2, nm));
-                    lsum += p0 + p1;
-                    pk[i] = pack_half2(p0, p1);
-                }
-                tmem_st16(lane_base + Cfg::TMEM_P + c / 2, pk);
-            }
-            l += lsum;
+            for (int c = 0; c < kTile / 2; c += 16) tmem_st16(lane_base + Cfg::TMEM_P + c, sv + c);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();

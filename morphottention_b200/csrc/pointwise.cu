@@ -17,6 +17,7 @@ namespace morpho {
 namespace {
 
 constexpr int kTile = 128;
+constexpr int kDzLanes = 2;  // token lanes of a dz block
 
 inline int npad_of(int N) { return (N + kTile - 1) / kTile * kTile; }
 
@@ -76,9 +77,13 @@ __global__ void __launch_bounds__(256) delta_kernel(const __half* __restrict__ d
     }
 }
 
-// Block = 256 threads, a contiguous run of tokens.  Thread k owns columns
-// 4k .. 4k+3 (+1024 per loop) of the padded dZ space [0, Hp).  Writes dcat[:, 0:Hp) and
-// the block's gate partials gate_part[blk][0|1][H*m].
+// Block = (column threads) x kDzLanes token lanes.  Column thread x owns the columns
+// 4x .. 4x+3 (+4*blockDim.x per loop) of the padded dZ space [0, Hp); token lane y takes
+// the tokens t0 + y, t0 + y + kDzLanes, ... of the block's contiguous run, so a warp reads
+// kDzLanes consecutive tokens of each head per round.  Writes dcat[:, 0:Hp) and the
+// block's gate partials, summed over the token lanes in shared memory in a fixed order
+// and stored column-major: gate_part[(g * H*m + col) * gridDim.x + block], g = 0 for
+// gate_q, 1 for gate_k, so that the reduction reads each column contiguously.
 // dphi/dz from phi alone (reference morfology/cube.cuh:28-45): sigmoid phi (1 - phi);
 // hardtanh01 1/2 where 0 < phi < 1 (i.e. -1 < z < 1), else 0; identity 1.
 template <int PROJ>
@@ -89,16 +94,21 @@ __device__ __forceinline__ float cube_grad(float phi) {
 }
 
 template <bool FULL, int PROJ>
-__global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, const float* __restrict__ dq,
+__global__ void __launch_bounds__(kDzLanes * 256) dz_kernel(const float* __restrict__ phi, const float* __restrict__ dq,
                                                  const float* __restrict__ dk, const float* __restrict__ dcb,
                                                  const float* __restrict__ dqb,
                                                  const __half* __restrict__ gq, const __half* __restrict__ gk,
                                                  __half* __restrict__ dcat, float* __restrict__ gate_part, int T,
                                                  int N, int Npad, int H, int m, int Hp, int Cp, int tokens_per_block) {
+    __shared__ float4 red[kDzLanes - 1][2][256];
     const int Hm = H * m;
+    const int tl = threadIdx.y;
     const int t0 = blockIdx.x * tokens_per_block;
     const int t1 = min(T, t0 + tokens_per_block);
-    for (int col0 = threadIdx.x * 4; col0 < Hp; col0 += blockDim.x * 4) {
+    // every thread runs the same number of column rounds (the block synchronises in each)
+    for (int base = 0; base < Hp; base += blockDim.x * 4) {
+        const int col0 = base + threadIdx.x * 4;
+        const bool cols = col0 < Hp;
         const bool live = col0 < Hm;  // m is a multiple of 16, so 4 columns never straddle heads
         const int h = live ? col0 / m : 0;
         const int c = col0 - h * m;
@@ -112,7 +122,7 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
             }
         }
 #pragma unroll 4
-        for (int t = t0; t < t1; ++t) {
+        for (int t = t0 + tl; cols && t < t1; t += kDzLanes) {
             uint2 out = make_uint2(0u, 0u);
             if (live) {
                 const int b = t / N;
@@ -149,15 +159,28 @@ __global__ void __launch_bounds__(256) dz_kernel(const float* __restrict__ phi, 
             }
             *reinterpret_cast<uint2*>(dcat + static_cast<size_t>(t) * Cp + col0) = out;
         }
-        if (live) {
-            float* pq = gate_part + (static_cast<size_t>(blockIdx.x) * 2) * Hm + col0;
-            float* pk = pq + Hm;
+        // token lanes 1.. hand their partials to lane 0, which adds them in lane order
+        if (tl > 0) {
+            red[tl - 1][0][threadIdx.x] = make_float4(aq[0], aq[1], aq[2], aq[3]);
+            red[tl - 1][1][threadIdx.x] = make_float4(ak[0], ak[1], ak[2], ak[3]);
+        }
+        __syncthreads();
+        if (tl == 0 && live) {
+#pragma unroll
+            for (int y = 0; y < kDzLanes - 1; ++y) {
+                const float4 vq = red[y][0][threadIdx.x];
+                const float4 vk = red[y][1][threadIdx.x];
+                aq[0] += vq.x, aq[1] += vq.y, aq[2] += vq.z, aq[3] += vq.w;
+                ak[0] += vk.x, ak[1] += vk.y, ak[2] += vk.z, ak[3] += vk.w;
+            }
+            const size_t nb = gridDim.x;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                pq[i] = aq[i];
-                pk[i] = ak[i];
+                gate_part[static_cast<size_t>(col0 + i) * nb + blockIdx.x] = aq[i];
+                gate_part[static_cast<size_t>(Hm + col0 + i) * nb + blockIdx.x] = ak[i];
             }
         }
+        __syncthreads();
     }
 }
 
@@ -211,9 +234,20 @@ __global__ void __launch_bounds__(256) reduce_weights_kernel(const float* __rest
     for (int k = (blockIdx.x - main_blocks) * (blockDim.x >> 5) + (threadIdx.x >> 5); k < 2 * Hm; k += warps) {
         const int g = k < Hm ? 0 : 1;
         const int col = k - g * Hm;
+        // the column's gate_blocks partials are contiguous: lane l sums blocks l, l+32, ...
+        // eight loads at a time, then a fixed shuffle tree (deterministic)
+        const float* src = gate_part + static_cast<long long>(k) * gate_blocks;
         float acc = 0.f;
-        for (int blk = lane; blk < gate_blocks; blk += 32)
-            acc += gate_part[(static_cast<long long>(blk) * 2 + g) * Hm + col];
+        for (int blk0 = 0; blk0 < gate_blocks; blk0 += 32 * 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int blk = blk0 + 32 * u + lane;
+                v[u] = blk < gate_blocks ? src[blk] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc += v[u];
+        }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
         if (lane == 0) {
@@ -270,9 +304,9 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
 
 int dz_gate_blocks(const Shape& s) {
     const long long T = s.tokens();
-    // ~16 tokens per block: enough blocks (and loads in flight) to cover HBM latency; the
-    // gate partials stay small (blocks x 2 x H*m floats)
-    return grid_for(T, 16, 8192);
+    // ~32 tokens per block (16 per token lane): enough warps and loads in flight to cover
+    // HBM latency; the gate partials stay small (blocks x 2 x H*m floats)
+    return grid_for(T, 32, 8192);
 }
 
 // Threads per dz block: one per 4 columns of [0, Hp), a multiple of 32, at most 256.
@@ -291,7 +325,7 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
                        : s.proj == kProjHardTanh01 ? dz_kernel<false, kProjHardTanh01>
                                                    : dz_kernel<false, kProjIdentity>);
     prof_begin(stream);
-    kern<<<gate_blocks, dz_threads(s), 0, stream>>>(phi, dq, dk, dcb, dqb, gate_q, gate_k, dcat, gate_part, T, s.N,
+    kern<<<gate_blocks, dim3(dz_threads(s), kDzLanes), 0, stream>>>(phi, dq, dk, dcb, dqb, gate_q, gate_k, dcat, gate_part, T, s.N,
                                                     npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     MORPHO_LAUNCH_CHECK("dz");
     return MORPHO_OK;
