@@ -243,10 +243,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         float l = 0.f;
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            const int s = j % kKvStages;
             const int kv0 = j * kTile;
-            if (!mbar_wait_warp(s_full, j & 1, args.status, K_ATTN_FWD, 8) ||
-                !mbar_wait_warp(kv_full0 + 8 * s, (j / kKvStages) & 1, args.status, K_ATTN_FWD, 9)) {
+            // (S_j is the only input: the MMA thread already waited for the K/V tile)
+            if (!mbar_wait_warp(s_full, j & 1, args.status, K_ATTN_FWD, 8)) {
                 ok = false;
                 break;
             }
