@@ -75,7 +75,7 @@ int run_attention_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& proj
                       cudaStream_t st) {
     if (s.score == kScoreSoftmax) return launch_attn_fwd(dev, s, proj, out, lse, st);
     MORPHO_CUDA_TRY(cudaMemsetAsync(lse, 0, static_cast<size_t>(s.B) * s.H * s.N * sizeof(float), st));
-    return launch_soft_morph_fwd(s, proj, out, proj.o2, st);  // o2 kept by forward_save only
+    return launch_soft_morph_fwd_tc(dev, s, proj, out, proj.o2, st);  // o2 kept by forward_save only
 }
 
 int check_ptr(const void* ptr, const char* name) {
@@ -111,6 +111,13 @@ void plan_proj(Carve& c, const Shape& s, ProjOut* o) {
     o->v = c.take<__half>(BH * s.N * s.hd);
     o->qb = c.take<float>(BH * Npad);
     o->cb = c.take<float>(BH * Npad);
+    if (s.score != kScoreSoftmax) {
+        o->evt = c.take<float>(BH * s.hd * Npad);
+        o->rv = c.take<float>(BH * s.hd);
+        o->vpart = c.take<float>(BH * ((s.N + 255) / 256) * s.hd);
+        o->smflag = c.take<uint32_t>(64);
+        o->mrow = c.take<float>(BH * Npad);
+    }
 }
 
 struct BwdPlan {
@@ -216,7 +223,7 @@ int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan
     } else {
         // soft-morphology score: the forward's m + log2(l) (kept by forward_save, else
         // recomputed), then the two backward kernels
-        if (!o2_ready) MORPHO_TRY(launch_soft_morph_fwd(s, b.proj, nullptr, b.proj.o2, st));
+        if (!o2_ready) MORPHO_TRY(launch_soft_morph_fwd_tc(dev, s, b.proj, nullptr, b.proj.o2, st));
         MORPHO_TRY(launch_soft_morph_bwd(s, b.proj, static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb,
                                          b.dk, b.dcb, b.dcat, st));
     }

@@ -58,6 +58,13 @@ struct ProjOut {
     // Soft-morphology score (training pair / backward only): m + log2(l) per (row, channel),
     // fp32 [B*H, N, hd], written by the forward for the backward.
     float* o2 = nullptr;
+    // Soft-morphology tensor-core forward scratch: E_V^T [B*H, hd, Npad] fp32, R [B*H, hd],
+    // per-256-key column maxima [B*H, ceil(N/256), hd], and the fallback flag.
+    float* evt = nullptr;
+    float* rv = nullptr;
+    float* vpart = nullptr;
+    uint32_t* smflag = nullptr;
+    float* mrow = nullptr;  // [B*H, Npad] the split forward's row reference m_i
 };
 
 // X [T, D] @ [W_phi | W_V] with the sigmoid / gating / bias epilogue.
@@ -105,7 +112,16 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
 // Soft-morphology score (softmorph.cu): forward out (fp16, may be NULL) and o2 = m + log2(l)
 // per (row, channel) [B*H, N, hd] fp32 (may be NULL); backward dq, dqb ([B*H, Npad]), dk, dcb
 // and the dV columns of dcat from the forward's o2.
-int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, cudaStream_t stream);
+// Exact CUDA-core forward; with only_if set it runs only when *only_if != 0 (device-side).
+int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, const uint32_t* only_if,
+                          cudaStream_t stream);
+// Soft-morphology path choice: the environment variable MORPHO_SOFT_MORPH_EXACT (set and not
+// "0") selects the exact CUDA-core kernels only; otherwise the split (tensor-core forward,
+// FMA backward) runs, guarded by the exact kernels.
+bool soft_morph_exact_only();
+// Tensor-core forward (E_S . E_V split) followed by the exact forward as its guard.
+int launch_soft_morph_fwd_tc(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* o2,
+                             cudaStream_t stream);
 int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, float* dq, float* dqb,
                           float* dk, float* dcb, __half* dcat, cudaStream_t stream);
 

@@ -17,7 +17,7 @@ namespace morpho {
 // ------------------------------------------------------------------------------------
 // Layout of the 32-bit device status word: bits 0-7 kernel id, bits 8-15 wait site,
 // bit 31 "timeout".  The first failing wait wins (atomicCAS from 0).
-enum KernelId : uint32_t { K_GEMM = 1, K_ATTN_FWD = 2, K_ATTN_BWD = 3, K_SELFTEST = 15 };
+enum KernelId : uint32_t { K_GEMM = 1, K_ATTN_FWD = 2, K_ATTN_BWD = 3, K_SOFT_MORPH = 4, K_SELFTEST = 15 };
 constexpr uint32_t STATUS_TIMEOUT = 0x80000000u;
 constexpr uint64_t WAIT_LIMIT_NS = 1000ull * 1000ull * 1000ull;  // 1 s per wait
 constexpr uint32_t WAIT_PARK_NS = 100u * 1000u;                      // re-check the clock every 0.1 ms
@@ -186,6 +186,18 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::tf32: A is M x K fp32 with row m in TMEM lane m and one
+// element per 32-bit column, B a K-major fp32 shared-memory tile; K = 8 per instruction.
+__device__ __forceinline__ void umma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this thread finish.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -272,6 +284,19 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_byte
 __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::tf32 with K-major A/B and fp32 D.
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// fp32 rounded to the nearest tf32 (10 mantissa bits), as fp32 bits.
+__device__ __forceinline__ uint32_t round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
 }
 
 // Fire-and-forget vector fp32 add to global memory (no return value, so the issuing

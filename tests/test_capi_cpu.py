@@ -81,9 +81,14 @@ def test_misaligned_pointer_rejected():
 
 def test_soft_morph_workspace_keeps_statistics():
     """With the soft-morphology score the training pair's saved buffer also holds the forward's
-    m + log2(l) per (row, channel) (fp32 [B*H, N, hd]); the softmax score does not need it."""
+    m + log2(l) per (row, channel) (fp32 [B*H, N, hd]) and the tensor-core forward's scratch
+    (E_V^T fp32 [B*H, hd, Npad], the column maxima R [B*H, hd], per-256-key partial maxima
+    [B*H, ceil(N/256), hd], the fallback flag and the row references m [B*H, Npad]); the softmax
+    score needs none of it."""
     L = capi.lib()
     a = capi.problem(2, 100, 128, 2, 16)
     b = capi.problem(2, 100, 128, 2, 16, score="dilation", tau=0.5)
     extra = L.morpho_sm100_saved_bytes(ctypes.byref(b)) - L.morpho_sm100_saved_bytes(ctypes.byref(a))
-    assert 2 * 2 * 100 * 64 * 4 <= extra <= 2 * 2 * 100 * 64 * 4 + 256
+    BH, N, Npad, hd = 4, 100, 128, 64
+    need = BH * N * hd * 4 + BH * hd * Npad * 4 + BH * hd * 4 + BH * 1 * hd * 4 + 64 * 4 + BH * Npad * 4
+    assert need <= extra <= need + 6 * 256

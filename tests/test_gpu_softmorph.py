@@ -1,7 +1,11 @@
 """The soft-morphology score (reference csrc/cuda/morfology/soft_morph.cuh:10-77, unused by
 the reference's kernels): out_ic = sgn tau logsumexp_j(sgn (S_ij + V_jc) / tau), soft dilation
 (sgn = +1) and erosion (sgn = -1), through the C ABI and the module, against the fp32 oracle
-restatement with the attention path's tolerances (rel-L2 <= 1e-3 out, <= 5e-3 gradients)."""
+restatement with the attention path's tolerances (rel-L2 <= 1e-3 out, <= 5e-3 gradients).
+
+Both paths are checked: the split one (tensor-core forward over E_S . E_V, FMA backward, with
+the exact kernels as a device-side guard) and the exact CUDA-core kernels alone, selected with
+the MORPHO_SOFT_MORPH_EXACT environment variable."""
 
 import pytest
 import torch
@@ -21,6 +25,15 @@ CASES = [
     MorphoConfig("m64_hd128", 1, 130, 256, 2, 64, 0.3, False, 43),
     MorphoConfig("m16_hd32", 2, 64, 128, 4, 16, 1.0, True, 44),
 ]
+
+
+@pytest.fixture(params=["split", "exact"])
+def path(request, monkeypatch):
+    if request.param == "exact":
+        monkeypatch.setenv("MORPHO_SOFT_MORPH_EXACT", "1")
+    else:
+        monkeypatch.delenv("MORPHO_SOFT_MORPH_EXACT", raising=False)
+    return request.param
 
 
 def run_cuda_morph(cfg, inp, grad_out, score, tau, mask_diag=False, projection="sigmoid"):
@@ -50,7 +63,7 @@ def oracle(cfg, inp, grad_out, score, tau, mask_diag=False, projection="sigmoid"
 
 @pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
 @pytest.mark.parametrize("score,tau", [("dilation", 1.0), ("erosion", 0.5)])
-def test_soft_morph_parity(cuda, cfg, score, tau):
+def test_soft_morph_parity(cuda, path, cfg, score, tau):
     inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
     g = inp.pop("grad_out")
     ours = run_cuda_morph(cfg, inp, g, score, tau)
@@ -58,7 +71,7 @@ def test_soft_morph_parity(cuda, cfg, score, tau):
     compare(ours, ref, tol_gate=gate_tolerance(cfg))
 
 
-def test_soft_morph_with_diagonal_mask_and_projection(cuda):
+def test_soft_morph_with_diagonal_mask_and_projection(cuda, path):
     cfg = MorphoConfig("diag", 1, 150, 128, 2, 32, 0.8, True, 45)
     inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
     g = inp.pop("grad_out")
@@ -69,7 +82,7 @@ def test_soft_morph_with_diagonal_mask_and_projection(cuda):
     compare(ours, ref, tol_gate=gate_tolerance(cfg))
 
 
-def test_soft_morph_through_module(cuda):
+def test_soft_morph_through_module(cuda, path):
     cfg = MorphoConfig("mod", 2, 100, 128, 4, 16, 1.0, False, 46)
     inp = inputs(cfg, cuda, random_gates=True)
     mod = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=cuda)
@@ -86,6 +99,59 @@ def test_soft_morph_through_module(cuda):
     ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
             "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
     compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def _both_paths(cfg, inp, g, score, tau, monkeypatch):
+    monkeypatch.delenv("MORPHO_SOFT_MORPH_EXACT", raising=False)
+    split = run_cuda_morph(cfg, inp, g, score, tau)
+    monkeypatch.setenv("MORPHO_SOFT_MORPH_EXACT", "1")
+    exact = run_cuda_morph(cfg, inp, g, score, tau)
+    monkeypatch.delenv("MORPHO_SOFT_MORPH_EXACT")
+    return split, exact
+
+
+def test_soft_morph_small_tau_guard(cuda, monkeypatch):
+    """tau = 0.02 stretches the exponent range to hundreds of log2 units across a column of V,
+    where the split's accumulators fall below their floor: the guard must hand the whole problem
+    to the exact kernels, so the split run is bit-identical to the exact-only run (and matches
+    the oracle).  At tau = 1 the two runs differ (the split path ran) and both match the oracle.
+    (Much smaller tau is ill-conditioned for the fp16 projection itself: the weights become
+    one-hot and a 2^-11 change of V moves them by tens of percent.)"""
+    cfg = MorphoConfig("small_tau", 1, 200, 128, 2, 16, 1.0, False, 47)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    split, exact = _both_paths(cfg, inp, g, "dilation", 0.02, monkeypatch)
+    for k in split:
+        assert torch.equal(split[k], exact[k]), k
+    compare(split, oracle(cfg, inp, g, "dilation", 0.02), tol_gate=gate_tolerance(cfg))
+    split, exact = _both_paths(cfg, inp, g, "dilation", 1.0, monkeypatch)
+    assert not torch.equal(split["out"], exact["out"])
+    ref = oracle(cfg, inp, g, "dilation", 1.0)
+    compare(split, ref, tol_gate=gate_tolerance(cfg))
+    compare(exact, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_soft_morph_exact_forward_then_split_backward(cuda, monkeypatch):
+    """The training pair with the exact switch on for the forward only: the backward, run with
+    the switch off, must see that the forward left no split statistics and take the exact pair."""
+    cfg = MorphoConfig("mixed", 1, 160, 128, 2, 16, 1.0, True, 48)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score="erosion", tau=0.7)
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty((cfg.B * cfg.H, cfg.N), dtype=torch.float32, device=cuda)
+    saved = torch.empty(capi.saved_bytes(p), dtype=torch.uint8, device=cuda)
+    monkeypatch.setenv("MORPHO_SOFT_MORPH_EXACT", "1")
+    capi.forward_save(p, *args, out, lse, saved)
+    monkeypatch.delenv("MORPHO_SOFT_MORPH_EXACT")
+    grads = [torch.empty_like(t) for t in args]
+    capi.backward_saved(p, g, saved, *args, out, lse, *grads)
+    torch.cuda.synchronize()
+    assert capi.device_status(reset=True) == 0
+    ours = {"out": out}
+    ours.update(dict(zip(("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), grads)))
+    compare(ours, oracle(cfg, inp, g, "erosion", 0.7), tol_gate=gate_tolerance(cfg))
 
 
 def test_soft_morph_invalid_problems(cuda):
