@@ -125,6 +125,7 @@ struct BwdPlan {
     __half* qaug;
     float* L;
     float* dqb;  // soft-morphology score: dL/dqbias, [B*H, Npad]
+    SmBwdScratch smx;  // soft-morphology tensor-core backward operands (hd <= 64)
     float* dq;
     float* dk;
     float* dcb;
@@ -151,6 +152,13 @@ void plan_bwd_rest(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dqb = s.score != kScoreSoftmax ? c.take<float>(BH * Npad) : nullptr;
+    if (s.score != kScoreSoftmax && s.hd <= 64) {
+        b->smx.g = c.take<float>(BH * s.N * s.hd);
+        b->smx.gt = c.take<float>(BH * s.hd * Npad);
+        b->smx.evn = c.take<float>(BH * Npad * s.hd);
+        b->smx.kdt = c.take<float>(BH * s.m * Npad);
+        b->smx.qct = c.take<float>(BH * s.m * Npad);
+    }
     b->dq = c.take<float>(BH * s.N * s.m);
     b->dk = c.take<float>(BH * s.N * s.m);
     b->dcb = c.take<float>(BH * Npad);
@@ -224,8 +232,9 @@ int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan
         // soft-morphology score: the forward's m + log2(l) (kept by forward_save, else
         // recomputed), then the two backward kernels
         if (!o2_ready) MORPHO_TRY(launch_soft_morph_fwd_tc(dev, s, b.proj, nullptr, b.proj.o2, st));
-        MORPHO_TRY(launch_soft_morph_bwd(s, b.proj, static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb,
-                                         b.dk, b.dcb, b.dcat, st));
+        MORPHO_TRY(launch_soft_morph_bwd(s, b.proj, b.smx.g != nullptr ? &b.smx : nullptr, dev.status,
+                                         static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb, b.dk, b.dcb,
+                                         b.dcat, st));
     }
     MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, b.dqb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
     MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));

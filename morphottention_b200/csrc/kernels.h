@@ -122,7 +122,22 @@ bool soft_morph_exact_only();
 // Tensor-core forward (E_S . E_V split) followed by the exact forward as its guard.
 int launch_soft_morph_fwd_tc(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* o2,
                              cudaStream_t stream);
-int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, float* dq, float* dqb,
+// fp32 operand layouts of the tensor-core soft-morphology backward (head dims 32 and 64):
+// G [B*H, N, hd], G^T [B*H, hd, Npad], E_V [B*H, Npad, hd], kd^T and qc^T [B*H, m, Npad].
+struct SmBwdScratch {
+    float* g = nullptr;
+    float* gt = nullptr;
+    float* evn = nullptr;
+    float* kdt = nullptr;
+    float* qct = nullptr;
+};
+int launch_soft_morph_bwd_tc(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __half* dO,
+                             const float* o2, float* dq, float* dqb, float* dk, float* dcb, __half* dcat,
+                             uint32_t* status, cudaStream_t stream);
+// Soft-morphology backward: split (tensor cores for hd <= 64 when tcx is given, CUDA cores
+// otherwise) gated against the exact kernels by the forward's flag; exact alone under the switch.
+int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* tcx, uint32_t* status,
+                          const __half* dO, const float* o2, float* dq, float* dqb,
                           float* dk, float* dcb, __half* dcat, cudaStream_t stream);
 
 // dqb (dL/dqbias, [B*H, Npad]) may be NULL: the softmax score's rows are shift-invariant, so

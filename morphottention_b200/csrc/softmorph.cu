@@ -597,6 +597,10 @@ template <int MC, int HD>
 struct Bwd {
     static int run(const SmArgs& a, int BH, cudaStream_t st) { return run_bwd<MC, HD>(a, BH, st); }
 };
+template <int MC, int HD>
+struct BwdExact {
+    static int run(const SmArgs& a, int BH, cudaStream_t st) { return run_bwd_pair<MC, HD, false>(a, BH, st); }
+};
 
 }  // namespace
 
@@ -615,8 +619,9 @@ int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* 
     return dispatch<Fwd>(s, a, stream);
 }
 
-int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, float* dq, float* dqb,
-                          float* dk, float* dcb, __half* dcat, cudaStream_t stream) {
+int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* tcx, uint32_t* status,
+                          const __half* dO, const float* o2, float* dq, float* dqb, float* dk, float* dcb,
+                          __half* dcat, cudaStream_t stream) {
     if (p.kdq == nullptr)
         return set_error(MORPHO_ERR_INVALID, "internal: soft-morphology backward needs the centered key codes");
     SmArgs a = make_args(s, p);
@@ -631,6 +636,11 @@ int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const __half* dO, co
         a.flag = p.smflag;
         a.mrow = p.mrow;
         a.rv = p.rv;
+        if (tcx != nullptr && s.hd <= 64) {  // tensor-core split pair, then the gated exact pair
+            MORPHO_TRY(launch_soft_morph_bwd_tc(s, p, *tcx, dO, o2, dq, dqb, dk, dcb, dcat, status, stream));
+            a.run_if_flag = 1;
+            return dispatch<BwdExact>(s, a, stream);
+        }
     }
     return dispatch<Bwd>(s, a, stream);
 }
