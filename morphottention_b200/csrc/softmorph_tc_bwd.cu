@@ -30,7 +30,7 @@ namespace morpho {
 namespace {
 
 constexpr int kTile = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 0-3: TMA, MMA, 2 idle; 4-11: two exponent warps per TMEM lane quarter
 
 inline int npad_of(int N) { return (N + kTile - 1) / kTile * kTile; }
 
@@ -129,9 +129,9 @@ struct QCfg {
     static constexpr int OFF_SK = 0, OFF_SEV = align1k(K_BYTES), OFF_SKD = OFF_SEV + EV_BYTES;
     static constexpr int STAGE = OFF_SKD + KD_BYTES;
     static constexpr int OFF_Q = 0, OFF_G = align1k(Q_BYTES), OFF_STAGE = OFF_G + G_BYTES;
-    static constexpr int STAGES = (OFF_STAGE + 2 * STAGE + 2048 <= 220 * 1024) ? 2 : 1;
+    static constexpr int STAGES = (OFF_STAGE + 2 * STAGE + 3072 <= 220 * 1024) ? 2 : 1;
     static constexpr int OFF_BAR = OFF_STAGE + STAGES * STAGE;
-    static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+    static constexpr int SMEM_BYTES = OFF_BAR + 1024 + 1024;  // barriers, TMEM slot, 128 row sums; alignment
     static constexpr int TX_STAGE = K_BYTES + EV_BYTES + KD_BYTES;
     static constexpr uint32_t TM_S = 0, TM_X = 128, TM_D = 256, TM_DQ = 384;
     static constexpr uint32_t QK_ROW = MC * 2;
@@ -160,8 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,ST) kv_full, [ST,2ST) kv_empty, 2ST q_full, +1 sx_full, +2 sx_free, +3 d_full, +4 dq_done, +5 drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 6);
+    // bars: [0,ST) kv_full, [ST,2ST) kv_empty, 2ST q_full, +1 sx_full, +2 sx_free, +3 d_full, +4 dq_done, +5 drain,
+    //       +6 rs_full (the second exponent half's row sums are in shared memory)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
+    float* rs_half = reinterpret_cast<float*>(tmem_slot + 2);  // [128]
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t kv_full0 = smem_u32(bars), kv_empty0 = smem_u32(bars + ST);
     const uint32_t q_full = smem_u32(bars + 2 * ST);
     const uint32_t sx_full = q_full + 8, sx_free = q_full + 16, d_full = q_full + 24, dq_done = q_full + 32,
-                   drain = q_full + 40;
+                   drain = q_full + 40, rs_full = q_full + 48;
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
             mbar_init(kv_full0 + 8 * s, 1);
@@ -181,10 +183,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(q_full, 1);
         mbar_init(sx_full, 1);
-        mbar_init(sx_free, 4);
-        mbar_init(d_full, 4);
+        mbar_init(sx_free, 8);
+        mbar_init(d_full, 8);
         mbar_init(dq_done, 1);
         mbar_init(drain, 1);
+        mbar_init(rs_full, 4);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -304,9 +307,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         const int quad = warp & 3;
+        const int half = (warp - 4) >> 2;  // this warp's 64 key columns
         const int r = quad * 32 + lane;
         const int q = q0 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
         float m_r = 0.f;
         if (q < args.N) {
             const float mm = args.mrow[static_cast<size_t>(bh) * args.Npad + q];
@@ -323,9 +327,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const bool need_mask = (kv0 + kTile > args.N) || ((CAUSAL || args.mask_diag) && j == qt);
-            uint32_t d[kTile];
+            uint32_t d[kTile / 2];
 #pragma unroll
-            for (int c = 0; c < kTile; c += 32) {
+            for (int c = 0; c < kTile / 2; c += 32) {
                 uint32_t sv[32], xv[32];
                 tmem_ld32(lane_base + Cfg::TM_S + c, sv);
                 tmem_ld32(lane_base + Cfg::TM_X + c, xv);
@@ -334,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < 32; ++k) {
                     float e = ex2(fmaf(u2f(sv[k]), kf2, -m_r));
                     if (need_mask) {
-                        const int kv = kv0 + c + k;
+                        const int kv = kv0 + half * 64 + c + k;
                         if (kv >= args.N || (CAUSAL && kv > q) || (args.mask_diag && kv == q)) e = 0.f;
                     }
                     const float dd = e * u2f(xv[k]);
@@ -353,18 +357,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
             }
 #pragma unroll
-            for (int c = 0; c < kTile; c += 16) tmem_st16(lane_base + Cfg::TM_D + c, d + c);
+            for (int c = 0; c < kTile / 2; c += 16) tmem_st16(lane_base + Cfg::TM_D + c, d + c);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(d_full);
         }
-        if (ok && n_kv > 0 && mbar_wait_warp(dq_done, (n_kv - 1) & 1, args.status, K_SOFT_MORPH, 51)) {
+        // the second half hands its row sums to the first, which writes the outputs
+        if (half == 1) {
+            rs_half[r] = rowsum;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rs_full);
+        } else if (ok && n_kv > 0 && mbar_wait_warp(dq_done, (n_kv - 1) & 1, args.status, K_SOFT_MORPH, 51) &&
+                   mbar_wait_warp(rs_full, 0, args.status, K_SOFT_MORPH, 52)) {
             tc_fence_after();
+            rowsum += rs_half[r];
+            const uint32_t acc_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
-                tmem_ld16(lane_base + Cfg::TM_DQ + c, rr);
+                tmem_ld16(acc_base + Cfg::TM_DQ + c, rr);
                 tmem_ld_wait();
                 if (q < args.N) {
                     float4* dst = reinterpret_cast<float4*>(args.dq + (static_cast<size_t>(bh) * args.N + q) * MC + c);
@@ -400,9 +412,9 @@ struct KCfg {
     static constexpr int OFF_SQC = 0, OFF_SG = align1k(QC_BYTES), OFF_SGT = OFF_SG + G_BYTES,
                          OFF_SQT = OFF_SGT + GT_BYTES;
     static constexpr int STAGE = OFF_SQT + QT_BYTES;
-    static constexpr int STAGES = (OFF_STAGE + 2 * STAGE + 2048 <= 220 * 1024) ? 2 : 1;
+    static constexpr int STAGES = (OFF_STAGE + 2 * STAGE + 3072 <= 220 * 1024) ? 2 : 1;
     static constexpr int OFF_BAR = OFF_STAGE + STAGES * STAGE;
-    static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+    static constexpr int SMEM_BYTES = OFF_BAR + 1024 + 1024;  // barriers, TMEM slot, 128 row sums; alignment
     static constexpr int TX_STAGE = QC_BYTES + G_BYTES + GT_BYTES + QT_BYTES;
     static constexpr uint32_t TM_S = 0, TM_X = 128, TM_DV = 256, TM_DK = 256 + HD;
     static constexpr uint32_t QK_ROW = MC * 2;
@@ -433,8 +445,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,ST) st_full, [ST,2ST) st_empty, 2ST k_full, +1 sx_full, +2 ed_full, +3 mm_done, +4 drain
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
+    // bars: [0,ST) st_full, [ST,2ST) st_empty, 2ST k_full, +1 sx_full, +2 ed_full, +3 mm_done, +4 drain,
+    //       +5 rs_full (the second exponent half's row sums are in shared memory)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 6);
+    float* rs_half = reinterpret_cast<float*>(tmem_slot + 2);  // [128]
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
@@ -444,7 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_it = args.n_tiles - it0;
     const uint32_t st_full0 = smem_u32(bars), st_empty0 = smem_u32(bars + ST);
     const uint32_t k_full = smem_u32(bars + 2 * ST);
-    const uint32_t sx_full = k_full + 8, ed_full = k_full + 16, mm_done = k_full + 24, drain = k_full + 32;
+    const uint32_t sx_full = k_full + 8, ed_full = k_full + 16, mm_done = k_full + 24, drain = k_full + 32,
+                   rs_full = k_full + 40;
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
             mbar_init(st_full0 + 8 * s, 1);
@@ -452,9 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(k_full, 1);
         mbar_init(sx_full, 1);
-        mbar_init(ed_full, 4);
+        mbar_init(ed_full, 8);
         mbar_init(mm_done, 1);
         mbar_init(drain, 1);
+        mbar_init(rs_full, 4);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -564,9 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         const int quad = warp & 3;
+        const int half = (warp - 4) >> 2;  // this warp's 64 query columns
         const int r = quad * 32 + lane;
         const int j = j0 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
         const float kf2 = args.kf2;
         const float* mrow = args.mrow + static_cast<size_t>(bh) * args.Npad;
         float rowsum = 0.f;
@@ -581,13 +598,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool need_mask = (j0 + kTile > args.N) || (q0 + kTile > args.N) ||
                                    ((CAUSAL || args.mask_diag) && q0 == j0);
 #pragma unroll
-            for (int c = 0; c < kTile; c += 32) {
+            for (int c = 0; c < kTile / 2; c += 32) {
                 uint32_t sv[32], xv[32];
                 tmem_ld32(lane_base + Cfg::TM_S + c, sv);
                 tmem_ld32(lane_base + Cfg::TM_X + c, xv);
+                const int qc = q0 + half * 64 + c;  // first query of this chunk
                 float mv = 0.f;
-                if (q0 + c + lane < args.N) {
-                    const float mm = mrow[q0 + c + lane];
+                if (qc + lane < args.N) {
+                    const float mm = mrow[qc + lane];
                     mv = mm == -INFINITY ? 0.f : mm;
                 }
                 tmem_ld_wait();
@@ -596,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float mq = __shfl_sync(0xffffffffu, mv, k);
                     float e = ex2(fmaf(u2f(sv[k]), kf2, -mq));
                     if (need_mask) {
-                        const int qq = q0 + c + k;
+                        const int qq = qc + k;
                         if (j >= args.N || qq >= args.N || (CAUSAL && j > qq) || (args.mask_diag && j == qq)) e = 0.f;
                     }
                     const float dd = e * u2f(xv[k]);
@@ -614,17 +632,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(ed_full);
         }
-        // epilogue: dV = E_V (.) acc -> dcat, dk, dcb (E_V from the shared-memory tile: wait for it)
-        if (ok && mbar_wait_warp(mm_done, 0, args.status, K_SOFT_MORPH, 68) &&
-            mbar_wait_warp(k_full, 0, args.status, K_SOFT_MORPH, 69) && !*abort_flag) {
+        // epilogue by the first half: dV = E_V (.) acc -> dcat, dk, dcb (E_V from the shared-memory
+        // tile: wait for it; the second half's row sums from shared memory)
+        if (half == 1) {
+            rs_half[r] = rowsum;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rs_full);
+        } else if (ok && mbar_wait_warp(mm_done, 0, args.status, K_SOFT_MORPH, 68) &&
+                   mbar_wait_warp(k_full, 0, args.status, K_SOFT_MORPH, 69) &&
+                   mbar_wait_warp(rs_full, 0, args.status, K_SOFT_MORPH, 70) && !*abort_flag) {
             tc_fence_after();
+            rowsum += rs_half[r];
+            const uint32_t acc_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
             const int b = bh / args.H;
             const int h = bh - b * args.H;
             const uint8_t* ev_tile = smem + Cfg::OFF_EV;
 #pragma unroll
             for (int c = 0; c < HD; c += 16) {
                 uint32_t rr[16];
-                tmem_ld16(lane_base + Cfg::TM_DV + c, rr);
+                tmem_ld16(acc_base + Cfg::TM_DV + c, rr);
                 tmem_ld_wait();
                 uint32_t pk[8];
 #pragma unroll
@@ -648,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
-                tmem_ld16(lane_base + Cfg::TM_DK + c, rr);
+                tmem_ld16(acc_base + Cfg::TM_DK + c, rr);
                 tmem_ld_wait();
                 if (j < args.N) {
                     float4* dst = reinterpret_cast<float4*>(args.dk + (static_cast<size_t>(bh) * args.N + j) * MC + c);
