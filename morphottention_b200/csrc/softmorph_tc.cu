@@ -32,7 +32,7 @@ namespace morpho {
 namespace {
 
 constexpr int kTile = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // warps 0-3: TMA, MMA, 2 idle; 4-11: two exponent warps per TMEM lane quarter
 constexpr int kStages = 2;
 constexpr int kVBlock = 256;                 // keys per ev_partial block
 constexpr float kGrowThreshold = 32.0f;      // log2 units: E_S <= 2^32, acc <= 2^32 * N
@@ -130,7 +130,7 @@ struct TcCfg {
     static constexpr int K_STRIDE = (K_BYTES + 1023) / 1024 * 1024;
     static constexpr int OFF_EV = OFF_K + kStages * K_STRIDE;
     static constexpr int OFF_BAR = OFF_EV + kStages * EV_BYTES;
-    static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+    static constexpr int SMEM_BYTES = OFF_BAR + 3072 + 1024;  // barriers, TMEM slot, 2 x 2 x 128 partial maxima; alignment
     static constexpr uint32_t TMEM_S = 0;
     static constexpr uint32_t TMEM_E = 128;
     static constexpr uint32_t TMEM_ACC = 256;
@@ -162,9 +162,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, +1 s_full, +2 e_full, +3 o_done, +4 drain, +5 s_free
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 6);
+    // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, +1 s_full, +2 e_full, +3 o_done, +4 drain, +5 s_free,
+    //       +6 mx_full (both halves' partial row maxima of the tile are in shared memory)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 7);
     volatile uint32_t* abort_flag = tmem_slot + 1;
+    float* pmax = reinterpret_cast<float*>(tmem_slot + 4);  // [tile parity][half][row]
 
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t o_done = q_full + 24;
     const uint32_t drain = q_full + 32;
     const uint32_t s_free = q_full + 40;
+    const uint32_t mx_full = q_full + 48;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -190,10 +193,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(q_full, 1);
         mbar_init(s_full, 1);
-        mbar_init(e_full, 4);
+        mbar_init(e_full, 8);
         mbar_init(o_done, 1);
         mbar_init(drain, 1);
-        mbar_init(s_free, 4);
+        mbar_init(s_free, 8);
+        mbar_init(mx_full, 8);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -307,9 +311,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 4) {
         // ---------------- exponentials + epilogue (warps 4..7) ----------------
         const int quad = warp & 3;
+        const int half = (warp - 4) >> 2;  // key columns half*64 .. +64, acc columns half*HD/2 .. +HD/2
         const int r = quad * 32 + lane;
         const int q = q0 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const uint32_t row_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        const uint32_t lane_base = row_base + half * 64;
+        const uint32_t acc_base = row_base + Cfg::TMEM_ACC + half * (HD / 2);
         const float kf2 = args.kf2;
         const bool pos = kf2 >= 0.f;
         float m_ref = -INFINITY;
@@ -321,9 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            uint32_t sv[kTile];
+            constexpr int W = kTile / 2;  // this warp's columns
+            uint32_t sv[W];
 #pragma unroll
-            for (int c = 0; c < kTile; c += 32) tmem_ld32(lane_base + Cfg::TMEM_S + c, sv + c);
+            for (int c = 0; c < W; c += 32) tmem_ld32(lane_base + Cfg::TMEM_S + c, sv + c);
             tmem_ld_wait();
             tc_fence_before();
             __syncwarp();
@@ -332,8 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool need_mask = (kv0 + kTile > args.N) || ((CAUSAL || args.mask_diag) && j == qt);
             if (need_mask) {
 #pragma unroll
-                for (int c = 0; c < kTile; ++c) {
-                    const int kv = kv0 + c;
+                for (int c = 0; c < W; ++c) {
+                    const int kv = kv0 + half * W + c;
                     const bool drop = kv >= args.N || (CAUSAL && kv > q) || (args.mask_diag && kv == q);
                     sv[c] = drop ? __float_as_uint(masked) : sv[c];
                 }
@@ -342,20 +350,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             {
                 float a0 = u2f(sv[0]), a1 = u2f(sv[1]), a2 = u2f(sv[2]), a3 = u2f(sv[3]);
 #pragma unroll
-                for (int c = 4; c < kTile; c += 8) {
+                for (int c = 4; c < W; c += 8) {
                     if (pos) {
                         a0 = fmax3(a0, u2f(sv[c]), u2f(sv[c + 1]));
                         a1 = fmax3(a1, u2f(sv[c + 2]), u2f(sv[c + 3]));
-                        if (c + 4 < kTile) a2 = fmax3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
-                        if (c + 6 < kTile) a3 = fmax3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
+                        if (c + 4 < W) a2 = fmax3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
+                        if (c + 6 < W) a3 = fmax3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
                     } else {
                         a0 = fmin3(a0, u2f(sv[c]), u2f(sv[c + 1]));
                         a1 = fmin3(a1, u2f(sv[c + 2]), u2f(sv[c + 3]));
-                        if (c + 4 < kTile) a2 = fmin3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
-                        if (c + 6 < kTile) a3 = fmin3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
+                        if (c + 4 < W) a2 = fmin3(a2, u2f(sv[c + 4]), u2f(sv[c + 5]));
+                        if (c + 6 < W) a3 = fmin3(a3, u2f(sv[c + 6]), u2f(sv[c + 7]));
                     }
                 }
                 ms = pos ? fmax3(a0, a1, fmaxf(a2, a3)) : fmin3(a0, a1, fminf(a2, a3));
+            }
+            // the row's extreme over both halves: exchange through shared memory (double-buffered
+            // by tile parity, so a warp one tile ahead never overwrites a value still to be read)
+            {
+                float* slot = pmax + (j & 1) * 2 * kTile;
+                slot[half * kTile + r] = ms;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(mx_full);
+                if (!mbar_wait_warp(mx_full, j & 1, args.status, K_SOFT_MORPH, 32)) {
+                    ok = false;
+                    break;
+                }
+                const float other = slot[(1 - half) * kTile + r];
+                ms = pos ? fmaxf(ms, other) : fminf(ms, other);
             }
             const float mt = kf2 * ms;  // -inf when every key of the tile is masked
             const bool grow = mt > m_ref + kGrowThreshold;
@@ -366,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // E_S = 2^(kf2 S - m) in fp32, in place (masked keys give 0); they overlap the
             // previous E_S . E_V, which still reads the E columns
 #pragma unroll
-            for (int c = 0; c < kTile; ++c) sv[c] = __float_as_uint(ex2(fmaf(u2f(sv[c]), kf2, nm)));
+            for (int c = 0; c < W; ++c) sv[c] = __float_as_uint(ex2(fmaf(u2f(sv[c]), kf2, nm)));
             if (j > 0) {
                 if (!mbar_wait_warp(o_done, (j - 1) & 1, args.status, K_SOFT_MORPH, 30)) {
                     ok = false;
@@ -375,19 +397,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-                    for (int c = 0; c < HD; c += 16) {
+                    for (int c = 0; c < HD / 2; c += 16) {
                         uint32_t rr[16];
-                        tmem_ld16(lane_base + Cfg::TMEM_ACC + c, rr);
+                        tmem_ld16(acc_base + c, rr);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(u2f(rr[i]) * alpha);
-                        tmem_st16(lane_base + Cfg::TMEM_ACC + c, rr);
+                        tmem_st16(acc_base + c, rr);
                     }
                     tmem_st_wait();
                 }
             }
 #pragma unroll
-            for (int c = 0; c < kTile; c += 16) tmem_st16(lane_base + Cfg::TMEM_E + c, sv + c);
+            for (int c = 0; c < W; c += 16) tmem_st16(lane_base + Cfg::TMEM_E + c, sv + c);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
@@ -401,15 +423,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool live = q < args.N;
             const bool dead = m_ref == -INFINITY;  // no key at all: out 0, t +inf
             const float qbl = live ? kLn2 * args.qb[static_cast<size_t>(bh) * args.Npad + q] : 0.f;
-            const float* R = args.rv + static_cast<size_t>(bh) * HD;
-            __half* orow =
-                args.out == nullptr ? nullptr : args.out + (static_cast<size_t>(b) * args.N + q) * args.D + h * HD;
-            float* o2row = args.o2 == nullptr ? nullptr : args.o2 + (static_cast<size_t>(bh) * args.N + q) * HD;
+            const float* R = args.rv + static_cast<size_t>(bh) * HD + half * (HD / 2);
+            __half* orow = args.out == nullptr
+                               ? nullptr
+                               : args.out + (static_cast<size_t>(b) * args.N + q) * args.D + h * HD + half * (HD / 2);
+            float* o2row =
+                args.o2 == nullptr ? nullptr : args.o2 + (static_cast<size_t>(bh) * args.N + q) * HD + half * (HD / 2);
             bool low = false;
 #pragma unroll
-            for (int c = 0; c < HD; c += 16) {
+            for (int c = 0; c < HD / 2; c += 16) {
                 uint32_t rr[16];
-                tmem_ld16(lane_base + Cfg::TMEM_ACC + c, rr);
+                tmem_ld16(acc_base + c, rr);
                 tmem_ld_wait();
                 float t[16];
                 uint32_t pk[8];
@@ -434,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 4; ++i) d2[i] = make_float4(t[4 * i], t[4 * i + 1], t[4 * i + 2], t[4 * i + 3]);
                 }
             }
-            if (live) args.mrow[static_cast<size_t>(bh) * args.Npad + q] = m_ref;
+            if (live && half == 0) args.mrow[static_cast<size_t>(bh) * args.Npad + q] = m_ref;
             if (live && !dead && low) atomicOr(args.flag, 1u);
         } else if (!ok) {
             *abort_flag = 1u;
