@@ -151,3 +151,48 @@ def test_diagonal_mask_rows():
     assert torch.allclose(r["out"][:, 1], v[:, 0], atol=1e-12)
     for k in ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"):
         assert torch.all(torch.isfinite(r[k]))
+
+
+def _split_soft_morph(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, score, tau, dtype):
+    """The soft-morphology aggregation through the split the CUDA path uses (log2 units):
+    sum_j 2^(x_ij + y_jc) = 2^(m_i + R_c) (E_S . E_V)_ic with E_S = 2^(x - m), E_V = 2^(y - R),
+    m_i the row maximum of x, R_c the column maximum of y; returns out and the accumulators."""
+    sgn = 1.0 if score == "dilation" else -1.0
+    B, N, D = x.shape
+    _, q, k, qbias, cbias, v = O.project(x, W_phi, gate_q, gate_k, W_V, H, cube_m)
+    s = scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))
+    log2e = 1.4426950408889634
+    xs = (sgn * s * log2e / tau).to(dtype)
+    ys = (sgn * v * log2e / tau).to(dtype)
+    m = xs.amax(dim=-1, keepdim=True)
+    R = ys.amax(dim=-2, keepdim=True)
+    acc = torch.exp2(xs - m) @ torch.exp2(ys - R)
+    t = m + R + torch.log2(acc)
+    out = sgn * tau * 0.6931471805599453 * t
+    return out.permute(0, 2, 1, 3).reshape(B, N, D), acc
+
+
+def test_soft_morph_split_identity():
+    """The split of the exponential (softmorph_tc.cu, softmorph_tc_bwd.cu) reproduces the
+    direct log-sum-exp of the oracle: in float64 to 1e-12 relative, in float32 to 1e-5."""
+    cfg = MorphoConfig("split", 1, 48, 64, 2, 16, 0.7, False, 21)
+    inp = {k: v.double() for k, v in make_inputs(cfg, device="cpu", random_gates=True).items()}
+    args = (inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], cfg.H, cfg.cube_m)
+    for score, tau in (("dilation", 1.0), ("erosion", 0.4)):
+        ref = O.soft_morph_forward(*args, scale=cfg.scale, score=score, tau=tau)
+        out64, _ = _split_soft_morph(*args, cfg.scale, score, tau, torch.float64)
+        assert O.rel_l2(out64, ref) < 1e-12
+        out32, acc32 = _split_soft_morph(*args, cfg.scale, score, tau, torch.float32)
+        assert O.rel_l2(out32.double(), ref) < 1e-5
+        assert acc32.min() >= 2.0 ** -90  # the guard's floor holds: the split path is taken
+
+
+def test_soft_morph_split_guard_floor():
+    """With tau small enough that a dominant term lies more than 90 log2 units below its two
+    stabilisers, the float32 accumulator falls below 2^-90 (or to 0): the CUDA path's guard
+    then hands the problem to the exact kernels."""
+    cfg = MorphoConfig("guard", 1, 48, 64, 2, 16, 1.0, False, 22)
+    inp = {k: v.double() for k, v in make_inputs(cfg, device="cpu", random_gates=True).items()}
+    args = (inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], cfg.H, cfg.cube_m)
+    _, acc32 = _split_soft_morph(*args, cfg.scale, "dilation", 0.005, torch.float32)
+    assert acc32.min() < 2.0 ** -90
