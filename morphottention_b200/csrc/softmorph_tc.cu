@@ -33,7 +33,6 @@ namespace {
 
 constexpr int kTile = 128;
 constexpr int kThreads = 384;  // warps 0-3: TMA, MMA, 2 idle; 4-11: two exponent warps per TMEM lane quarter
-constexpr int kStages = 2;
 constexpr int kVBlock = 256;                 // keys per ev_partial block
 constexpr float kGrowThreshold = 32.0f;      // log2 units: E_S <= 2^32, acc <= 2^32 * N
 constexpr float kAccFloor = 8.0779356e-28f;  // 2^-90: below it the split may have lost the dominant term
@@ -128,8 +127,9 @@ struct TcCfg {
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = (Q_BYTES + 1023) / 1024 * 1024;
     static constexpr int K_STRIDE = (K_BYTES + 1023) / 1024 * 1024;
-    static constexpr int OFF_EV = OFF_K + kStages * K_STRIDE;
-    static constexpr int OFF_BAR = OFF_EV + kStages * EV_BYTES;
+    static constexpr int ST = HD <= 64 ? 4 : 2;  // TMA ring depth (K codes + E_V^T per tile)
+    static constexpr int OFF_EV = OFF_K + ST * K_STRIDE;
+    static constexpr int OFF_BAR = OFF_EV + ST * EV_BYTES;
     static constexpr int SMEM_BYTES = OFF_BAR + 3072 + 1024;  // barriers, TMEM slot, 2 x 2 x 128 partial maxima; alignment
     static constexpr uint32_t TMEM_S = 0;
     static constexpr uint32_t TMEM_E = 128;
@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm_tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmE, const TcArgs args) {
     using Cfg = TcCfg<MC, HD>;
+    constexpr int kStages = Cfg::ST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);

@@ -129,7 +129,9 @@ struct QCfg {
     static constexpr int OFF_SK = 0, OFF_SEV = align1k(K_BYTES), OFF_SKD = OFF_SEV + EV_BYTES;
     static constexpr int STAGE = OFF_SKD + KD_BYTES;
     static constexpr int OFF_Q = 0, OFF_G = align1k(Q_BYTES), OFF_STAGE = OFF_G + G_BYTES;
-    static constexpr int STAGES = (OFF_STAGE + 2 * STAGE + 3072 <= 220 * 1024) ? 2 : 1;
+    static constexpr int STAGES = (OFF_STAGE + 3 * STAGE + 3072 <= 220 * 1024)   ? 3
+                                  : (OFF_STAGE + 2 * STAGE + 3072 <= 220 * 1024) ? 2
+                                                                                 : 1;
     static constexpr int OFF_BAR = OFF_STAGE + STAGES * STAGE;
     static constexpr int SMEM_BYTES = OFF_BAR + 1024 + 1024;  // barriers, TMEM slot, 128 row sums; alignment
     static constexpr int TX_STAGE = K_BYTES + EV_BYTES + KD_BYTES;
