@@ -24,7 +24,11 @@
 //                       contiguous: the K-major B operand), 0 past N
 //   sm_tc_fwd_kernel  : one CTA per 128-query tile: S = qc . k^T (kind::f16, as the softmax
 //                       forward), E_S = 2^(kf2 S - m) written to TMEM as fp32, acc += E_S . E_V
-//                       (kind::tf32, A from TMEM), lazy rescale of acc when m grows by 2^32.
+//                       (kind::tf32, A from TMEM), lazy rescale of acc when m grows by 2^32;
+//                       12 warps (TMA producer, MMA issuer, two idle, eight exponent warps:
+//                       two per TMEM lane quarter, 64 key columns each, which exchange their
+//                       partial row maxima through shared memory every tile), a 4-stage ring
+//                       of K codes and E_V^T tiles (2 stages at hd 128).
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp >= 4) {
-        // ---------------- exponentials + epilogue (warps 4..7) ----------------
+        // ---------------- exponentials + epilogue (warps 4..11, two per TMEM lane quarter) ----------------
         const int quad = warp & 3;
         const int half = (warp - 4) >> 2;  // key columns half*64 .. +64, acc columns half*HD/2 .. +HD/2
         const int r = quad * 32 + lane;
