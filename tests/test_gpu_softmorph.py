@@ -24,6 +24,8 @@ CASES = [
     MorphoConfig("m32_causal", 1, 300, 256, 4, 32, 0.5, True, 42),
     MorphoConfig("m64_hd128", 1, 130, 256, 2, 64, 0.3, False, 43),
     MorphoConfig("m16_hd32", 2, 64, 128, 4, 16, 1.0, True, 44),
+    MorphoConfig("n1", 1, 1, 128, 2, 16, 1.0, False, 49),
+    MorphoConfig("n15_causal", 2, 15, 128, 4, 32, 0.8, True, 50),
 ]
 
 
