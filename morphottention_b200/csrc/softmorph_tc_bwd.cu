@@ -418,7 +418,7 @@ struct KCfg {
     static constexpr int OFF_BAR = OFF_STAGE + STAGES * STAGE;
     static constexpr int SMEM_BYTES = OFF_BAR + 1024 + 1024;  // barriers, TMEM slot, 128 row sums; alignment
     static constexpr int TX_STAGE = QC_BYTES + G_BYTES + GT_BYTES + QT_BYTES;
-    static constexpr uint32_t TM_S = 0, TM_X = 128, TM_DV = 256, TM_DK = 256 + HD;
+    static constexpr uint32_t TM_DV = 256, TM_DK = 256 + HD;  // [0, 256): two slots of S^T | X^T halves
     static constexpr uint32_t QK_ROW = MC * 2;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
     static_assert(TM_DK + MC <= 512, "TMEM");
@@ -447,9 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,ST) st_full, [ST,2ST) st_empty, 2ST k_full, +1 sx_full, +2 ed_full, +3 mm_done, +4 drain,
-    //       +5 rs_full (the second exponent half's row sums are in shared memory)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 6);
+    // bars: [0,ST) st_full, [ST,2ST) st_empty, 2ST k_full, +1/+2 sx_full of TMEM slot 0/1, +3/+4 ed_full
+    //       of slot 0/1, +5 mm_done, +6 drain, +7 rs_full (the second exponent half's row sums are in
+    //       shared memory)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 8);
     float* rs_half = reinterpret_cast<float*>(tmem_slot + 2);  // [128]
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const int warp = warp_id();
@@ -460,16 +461,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_it = args.n_tiles - it0;
     const uint32_t st_full0 = smem_u32(bars), st_empty0 = smem_u32(bars + ST);
     const uint32_t k_full = smem_u32(bars + 2 * ST);
-    const uint32_t sx_full = k_full + 8, ed_full = k_full + 16, mm_done = k_full + 24, drain = k_full + 32,
-                   rs_full = k_full + 40;
+    const uint32_t sx_full0 = k_full + 8, sx_full1 = k_full + 16, ed_full0 = k_full + 24, ed_full1 = k_full + 32,
+                   mm_done = k_full + 40, drain = k_full + 48, rs_full = k_full + 56;
+    const int n_u = 2 * n_it;  // 64-query half tiles, alternating between two TMEM slots
     if (threadIdx.x == 0) {
         for (int s = 0; s < ST; ++s) {
             mbar_init(st_full0 + 8 * s, 1);
             mbar_init(st_empty0 + 8 * s, 1);
         }
         mbar_init(k_full, 1);
-        mbar_init(sx_full, 1);
-        mbar_init(ed_full, 8);
+        mbar_init(sx_full0, 1);
+        mbar_init(sx_full1, 1);
+        mbar_init(ed_full0, 8);
+        mbar_init(ed_full1, 8);
         mbar_init(mm_done, 1);
         mbar_init(drain, 1);
         mbar_init(rs_full, 4);
@@ -522,54 +526,78 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);
-            constexpr uint32_t id_x = make_idesc_tf32(128, 128);
+            // Half tile u (queries (u/2)*128 + (u%2)*64 .. +64) uses TMEM slot u%2: S^T in its columns
+            // [0, 64), X^T in [64, 128); the warps write E_S^T and dS^T over them, which dV and dk
+            // read.  While the warps work on one slot the tensor pipe runs the other slot's dV / dk
+            // and the next half tile's S^T / X^T (issued after those in the same thread, so in order).
+            constexpr uint32_t id_s = make_idesc_f16(128, 64, false, false);
+            constexpr uint32_t id_x = make_idesc_tf32(128, 64);
             constexpr uint32_t id_dv = make_idesc_tf32(128, HD);
             constexpr uint32_t id_dk = make_idesc_tf32(128, MC);
             constexpr uint32_t qk_sw = swizzle_code_for_row_bytes(Cfg::QK_ROW);
             constexpr uint32_t qk_sbo = 8 * Cfg::QK_ROW;
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K), sEV = smem_u32(smem + Cfg::OFF_EV);
-            bool ok = mbar_wait(k_full, 0, args.status, K_SOFT_MORPH, 63);
-            for (int i = 0; ok && i < n_it; ++i) {
-                const int s = i % ST;
+            auto issue_sx = [&](int u) -> bool {
+                const int i = u >> 1, h = u & 1, s = i % ST;
                 const uint32_t sb = stage_base(s);
-                if (!mbar_wait(st_full0 + 8 * s, (i / ST) & 1, args.status, K_SOFT_MORPH, 64)) {
-                    ok = false;
-                    break;
+                if (h == 0) {
+                    if (!mbar_wait(st_full0 + 8 * s, (i / ST) & 1, args.status, K_SOFT_MORPH, 64)) return false;
+                    tc_fence_after();
                 }
-                tc_fence_after();
-                // S^T and X^T over the columns the previous dV / dK read: MMAs of one thread
-                // execute in order, so these writes follow those reads
+                const uint32_t dst = tmem + (u & 1) * 128;
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks)
-                    umma_ss(tmem + Cfg::TM_S, make_sdesc(sK + ks * 32, 16, qk_sbo, qk_sw),
-                            make_sdesc(sb + Cfg::OFF_SQC + ks * 32, 16, qk_sbo, qk_sw), id_s, ks > 0 ? 1u : 0u);
+                    umma_ss(dst, make_sdesc(sK + ks * 32, 16, qk_sbo, qk_sw),
+                            make_sdesc(sb + Cfg::OFF_SQC + h * 64 * Cfg::QK_ROW + ks * 32, 16, qk_sbo, qk_sw), id_s,
+                            ks > 0 ? 1u : 0u);
 #pragma unroll
                 for (int kb = 0; kb < HD / 32; ++kb)
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        umma_ss_tf32(tmem + Cfg::TM_X, make_sdesc(sEV + kb * 16384 + ks * 32, 16, 1024, SW_128),
-                                     make_sdesc(sb + Cfg::OFF_SG + kb * 16384 + ks * 32, 16, 1024, SW_128), id_x,
-                                     (kb > 0 || ks > 0) ? 1u : 0u);
-                umma_commit(sx_full);
-                if (!mbar_wait(ed_full, i & 1, args.status, K_SOFT_MORPH, 65)) {
+                        umma_ss_tf32(dst + 64, make_sdesc(sEV + kb * 16384 + ks * 32, 16, 1024, SW_128),
+                                     make_sdesc(sb + Cfg::OFF_SG + kb * 16384 + h * 8192 + ks * 32, 16, 1024, SW_128),
+                                     id_x, (kb > 0 || ks > 0) ? 1u : 0u);
+                umma_commit((u & 1) ? sx_full1 : sx_full0);
+                return true;
+            };
+            bool ok = mbar_wait(k_full, 0, args.status, K_SOFT_MORPH, 63);
+            if (ok && n_u > 0) ok = issue_sx(0);
+            if (ok && n_u > 1) ok = issue_sx(1);
+            for (int u = 0; ok && u < n_u; ++u) {
+                const int i = u >> 1, h = u & 1, s = i % ST, b = u & 1;
+                const uint32_t sb = stage_base(s);
+                if (!mbar_wait(b ? ed_full1 : ed_full0, (u >> 1) & 1, args.status, K_SOFT_MORPH, 65)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t src = tmem + b * 128;
 #pragma unroll
-                for (int kb = 0; kb < 4; ++kb)
+                for (int c = 0; c < 2; ++c) {  // the half tile's two 32-query chunks
+                    const int kb = 2 * h + c;
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks) {
-                        const uint32_t acc = (i > 0 || kb > 0 || ks > 0) ? 1u : 0u;
-                        umma_ts_tf32(tmem + Cfg::TM_DV, tmem + Cfg::TM_S + kb * 32 + ks * 8,
+                        const uint32_t acc = (u > 0 || c > 0 || ks > 0) ? 1u : 0u;
+                        umma_ts_tf32(tmem + Cfg::TM_DV, src + c * 32 + ks * 8,
                                      make_sdesc(sb + Cfg::OFF_SGT + kb * HD * 128 + ks * 32, 16, 1024, SW_128), id_dv,
                                      acc);
-                        umma_ts_tf32(tmem + Cfg::TM_DK, tmem + Cfg::TM_X + kb * 32 + ks * 8,
+                        umma_ts_tf32(tmem + Cfg::TM_DK, src + 64 + c * 32 + ks * 8,
                                      make_sdesc(sb + Cfg::OFF_SQT + kb * MC * 128 + ks * 32, 16, 1024, SW_128), id_dk,
                                      acc);
                     }
-                umma_commit(st_empty0 + 8 * s);
+                }
+                if (h == 1) umma_commit(st_empty0 + 8 * s);
+                if (ST > 1) {
+                    if (u + 2 < n_u && !issue_sx(u + 2)) {
+                        ok = false;
+                        break;
+                    }
+                } else if (h == 1) {  // one stage: the next tile loads only after this one's dV / dk
+                    if ((u + 1 < n_u && !issue_sx(u + 1)) || (u + 2 < n_u && !issue_sx(u + 2))) {
+                        ok = false;
+                        break;
+                    }
+                }
             }
             if (ok) {
                 umma_commit(mm_done);
@@ -582,57 +610,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         const int quad = warp & 3;
-        const int half = (warp - 4) >> 2;  // this warp's 64 query columns
+        const int half = (warp - 4) >> 2;  // this warp's 32 of each half tile's 64 query columns
         const int r = quad * 32 + lane;
         const int j = j0 + r;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+        const uint32_t row_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
         const float kf2 = args.kf2;
         const float* mrow = args.mrow + static_cast<size_t>(bh) * args.Npad;
         float rowsum = 0.f;
         bool ok = true;
-        for (int i = 0; i < n_it; ++i) {
+        for (int u = 0; u < n_u; ++u) {
+            const int i = u >> 1, h = u & 1, b = u & 1;
             const int q0 = (it0 + i) * kTile;
-            if (!mbar_wait_warp(sx_full, i & 1, args.status, K_SOFT_MORPH, 67)) {
+            const int qc = q0 + h * 64 + half * 32;  // first query of this warp's 32 columns
+            if (!mbar_wait_warp(b ? sx_full1 : sx_full0, (u >> 1) & 1, args.status, K_SOFT_MORPH, 67)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const bool need_mask = (j0 + kTile > args.N) || (q0 + kTile > args.N) ||
+            const bool need_mask = (j0 + kTile > args.N) || (qc + 32 > args.N) ||
                                    ((CAUSAL || args.mask_diag) && q0 == j0);
-#pragma unroll
-            for (int c = 0; c < kTile / 2; c += 32) {
-                uint32_t sv[32], xv[32];
-                tmem_ld32(lane_base + Cfg::TM_S + c, sv);
-                tmem_ld32(lane_base + Cfg::TM_X + c, xv);
-                const int qc = q0 + half * 64 + c;  // first query of this chunk
-                float mv = 0.f;
-                if (qc + lane < args.N) {
-                    const float mm = mrow[qc + lane];
-                    mv = mm == -INFINITY ? 0.f : mm;
-                }
-                tmem_ld_wait();
-#pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float mq = __shfl_sync(0xffffffffu, mv, k);
-                    float e = ex2(fmaf(u2f(sv[k]), kf2, -mq));
-                    if (need_mask) {
-                        const int qq = qc + k;
-                        if (j >= args.N || qq >= args.N || (CAUSAL && j > qq) || (args.mask_diag && j == qq)) e = 0.f;
-                    }
-                    const float dd = e * u2f(xv[k]);
-                    rowsum += dd;
-                    sv[k] = __float_as_uint(e);
-                    xv[k] = __float_as_uint(dd);
-                }
-                tmem_st16(lane_base + Cfg::TM_S + c, sv);
-                tmem_st16(lane_base + Cfg::TM_S + c + 16, sv + 16);
-                tmem_st16(lane_base + Cfg::TM_X + c, xv);
-                tmem_st16(lane_base + Cfg::TM_X + c + 16, xv + 16);
+            const uint32_t sl = row_base + b * 128 + half * 32;
+            uint32_t sv[32], xv[32];
+            tmem_ld32(sl, sv);
+            tmem_ld32(sl + 64, xv);
+            float mv = 0.f;
+            if (qc + lane < args.N) {
+                const float mm = mrow[qc + lane];
+                mv = mm == -INFINITY ? 0.f : mm;
             }
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const float mq = __shfl_sync(0xffffffffu, mv, k);
+                float e = ex2(fmaf(u2f(sv[k]), kf2, -mq));
+                if (need_mask) {
+                    const int qq = qc + k;
+                    if (j >= args.N || qq >= args.N || (CAUSAL && j > qq) || (args.mask_diag && j == qq)) e = 0.f;
+                }
+                const float dd = e * u2f(xv[k]);
+                rowsum += dd;
+                sv[k] = __float_as_uint(e);
+                xv[k] = __float_as_uint(dd);
+            }
+            tmem_st16(sl, sv);
+            tmem_st16(sl + 16, sv + 16);
+            tmem_st16(sl + 64, xv);
+            tmem_st16(sl + 80, xv + 16);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(ed_full);
+            if (lane == 0) mbar_arrive(b ? ed_full1 : ed_full0);
         }
         // epilogue by the first half: dV = E_V (.) acc -> dcat, dk, dcb (E_V from the shared-memory
         // tile: wait for it; the second half's row sums from shared memory)
