@@ -125,7 +125,7 @@ struct BwdPlan {
     __half* qaug;
     float* L;
     float* dqb;  // soft-morphology score: dL/dqbias, [B*H, Npad]
-    SmBwdScratch smx;  // soft-morphology tensor-core backward operands (hd <= 64)
+    SmBwdScratch smx;  // soft-morphology tensor-core backward operands
     float* dq;
     float* dk;
     float* dcb;
@@ -152,7 +152,7 @@ void plan_bwd_rest(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dqb = s.score != kScoreSoftmax ? c.take<float>(BH * Npad) : nullptr;
-    if (s.score != kScoreSoftmax && s.hd <= 64) {
+    if (s.score != kScoreSoftmax) {
         b->smx.g = c.take<float>(BH * s.N * s.hd);
         b->smx.gt = c.take<float>(BH * s.hd * Npad);
         b->smx.evn = c.take<float>(BH * Npad * s.hd);

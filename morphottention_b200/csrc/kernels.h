@@ -134,8 +134,8 @@ struct SmBwdScratch {
 int launch_soft_morph_bwd_tc(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __half* dO,
                              const float* o2, float* dq, float* dqb, float* dk, float* dcb, __half* dcat,
                              uint32_t* status, cudaStream_t stream);
-// Soft-morphology backward: split (tensor cores for hd <= 64 when tcx is given, CUDA cores
-// otherwise) gated against the exact kernels by the forward's flag; exact alone under the switch.
+// Soft-morphology backward: the tensor-core split kernels and, gated against them by the forward's
+// range flag, the exact kernels; the exact kernels alone under the MORPHO_SOFT_MORPH_EXACT switch.
 int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* tcx, uint32_t* status,
                           const __half* dO, const float* o2, float* dq, float* dqb,
                           float* dk, float* dcb, __half* dcat, cudaStream_t stream);

@@ -1,4 +1,7 @@
-// softmorph.cu -- the soft-morphology score on CUDA cores (sm_100a).
+// softmorph.cu -- the soft-morphology score on CUDA cores (sm_100a): the exact kernels.  The
+// default path is the split one on the tensor cores (softmorph_tc.cu, softmorph_tc_bwd.cu); these
+// kernels are its device-side fallback (they return at once unless its range flag is set) and,
+// under the MORPHO_SOFT_MORPH_EXACT environment switch, the whole path.
 //
 // The reference ships a tropical (max-plus / min-plus) soft aggregation in
 // csrc/cuda/morfology/soft_morph.cuh:10-77 that no kernel of it calls.  Here it is a run-time
@@ -59,8 +62,6 @@ struct SmArgs {
     __half* dcat;      // [B*N, Cp]: dV at columns Hp + h*HD
     const uint32_t* flag;  // fallback flag of the tensor-core forward (null: run unconditionally)
     int run_if_flag;       // 1: run only when *flag != 0 (the exact fallback); 0: only when *flag == 0
-    const float* mrow;     // [BH, Npad] the tensor-core forward's row reference m_i
-    const float* rv;       // [BH, HD] its column maxima R_c
 };
 
 // Gate of the kernels that exist twice (exact and factorized): true = nothing to do here.
@@ -227,11 +228,7 @@ __device__ __forceinline__ void stage_o2(float* dst, const float* src, int r0, i
 }
 
 // ---------------- backward, query side: dq, dqb ----------------
-// FAST (after an unflagged tensor-core forward): P_ijc = E_S[i,j] E_V[j,c] F_ic with
-// E_S = 2^(x_ij - m_i), E_V = 2^(y_jc - R_c), F = 2^(m_i + R_c - t_ic), so that
-// dS_ij = E_S[i,j] sum_c G_ic E_V[j,c] with G = dO F: one FMA per (i, j, c) instead of an
-// exponential (the same split as the forward, whose range check this path relies on).
-template <int MC, int HD, bool FAST>
+template <int MC, int HD>
 __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs a) {
     if (gated_out(a)) return;
     constexpr int CPT = HD / 4;   // value channels per thread
@@ -240,9 +237,8 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
     float* sq = sm;                       // [64][MC+1] query codes
     float* sk = sq + kT * (MC + 1);       // [64][MC+1] key codes
     float* skd = sk + kT * (MC + 1);      // [64][MC] centered key codes (hi + lo)
-    float* sv = skd + kT * MC;            // [64][HD] kf * V (FAST: E_V)
+    float* sv = skd + kT * MC;            // [64][HD] kf * V
     float* st = sv + kT * HD;             // [64][65] scores, then dS
-    float* sR = st + kT * 65;             // [HD] R_c (FAST)
     const int qt = blockIdx.x, bh = blockIdx.y;
     const int b = bh / a.H, h = bh - b * a.H;
     const int r = threadIdx.x >> 2, q4 = threadIdx.x & 3;
@@ -267,17 +263,6 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
             o2r[c] = o[c];
             o2r[c + 1] = o[c + 1];
         }
-    }
-    float m_r = 0.f;  // FAST: dOr becomes G = dO F (0 on rows without keys, where t = +inf)
-    if (FAST) {
-        if (threadIdx.x < HD) sR[threadIdx.x] = a.rv[static_cast<size_t>(bh) * HD + threadIdx.x];
-        if (i < a.N) {
-            const float mm = a.mrow[static_cast<size_t>(bh) * a.Npad + i];
-            m_r = mm == -INFINITY ? 0.f : mm;
-        }
-        const float* R = a.rv + static_cast<size_t>(bh) * HD + q4 * CPT;
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) dOr[c] *= ex2(m_r + R[c] - o2r[c]);
     }
     float dq[MPT];
 #pragma unroll
@@ -309,10 +294,6 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
         }
         stage_rows<HD>(sv, HD, a.v + base * HD, HD, 0, j0, a.N, a.kf);
         __syncthreads();
-        if (FAST) {  // E_V of the tile (keys past N: any value, their E_S is 0)
-            for (int e = threadIdx.x; e < kT * HD; e += kThreads) sv[e] = ex2(sv[e] - sR[e % HD]);
-            __syncthreads();
-        }
         score_tile<MC>(st, sq, sk, r, q4, a.kf2, a, i0, j0, true);
         __syncthreads();
         // dS_rj = sum_c dO_rc P_rjc, summed over the four channel quarters by shuffles
@@ -328,27 +309,20 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
 #pragma unroll
                 for (int c4 = 0; c4 < CPT / 4; ++c4) {
                     const float4 vv = v4[c4];
-                    if (FAST) {
-                        part = fmaf(dOr[4 * c4], vv.x, part);
-                        part = fmaf(dOr[4 * c4 + 1], vv.y, part);
-                        part = fmaf(dOr[4 * c4 + 2], vv.z, part);
-                        part = fmaf(dOr[4 * c4 + 3], vv.w, part);
-                    } else {
-                        part = fmaf(dOr[4 * c4], ex2(s + vv.x - o2r[4 * c4]), part);
-                        part = fmaf(dOr[4 * c4 + 1], ex2(s + vv.y - o2r[4 * c4 + 1]), part);
-                        part = fmaf(dOr[4 * c4 + 2], ex2(s + vv.z - o2r[4 * c4 + 2]), part);
-                        part = fmaf(dOr[4 * c4 + 3], ex2(s + vv.w - o2r[4 * c4 + 3]), part);
-                    }
+                    part = fmaf(dOr[4 * c4], ex2(s + vv.x - o2r[4 * c4]), part);
+                    part = fmaf(dOr[4 * c4 + 1], ex2(s + vv.y - o2r[4 * c4 + 1]), part);
+                    part = fmaf(dOr[4 * c4 + 2], ex2(s + vv.z - o2r[4 * c4 + 2]), part);
+                    part = fmaf(dOr[4 * c4 + 3], ex2(s + vv.w - o2r[4 * c4 + 3]), part);
                 }
                 part += __shfl_xor_sync(0xffffffffu, part, 1);
                 part += __shfl_xor_sync(0xffffffffu, part, 2);
                 dsv[t] = part;
             }
             __syncwarp();
-            // every quarter holds the same sums; quarter t%4 == q4 writes them (FAST: times E_S)
+            // every quarter holds the same sums; quarter t%4 == q4 writes them
 #pragma unroll
             for (int t = 0; t < kT / 4; ++t)
-                if ((t & 3) == q4) srow[jb + t] = FAST ? ex2(srow[jb + t] - m_r) * dsv[t] : dsv[t];
+                if ((t & 3) == q4) srow[jb + t] = dsv[t];
         }
         __syncthreads();
         for (int j = 0; j < kT; ++j) {
@@ -367,9 +341,7 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
 }
 
 // ---------------- backward, key side: dV, dk, dcb ----------------
-// FAST: dV_jc = E_V[j,c] sum_i E_S[i,j] G_ic and dS_ij = E_S[i,j] sum_c G_ic E_V[j,c] (the
-// split of the query-side kernel): two FMAs per (i, j, c), one exponential per (i, j).
-template <int MC, int HD, bool FAST>
+template <int MC, int HD>
 __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs a) {
     if (gated_out(a)) return;
     constexpr int CPT = HD / 4;
@@ -377,11 +349,9 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
     extern __shared__ float sm[];
     float* sk = sm;                       // [64][MC+1] key codes (this CTA's keys)
     float* sq = sk + kT * (MC + 1);       // [64][MC+1] query codes
-    float* sg = sq + kT * (MC + 1);       // [64][HD] dO (FAST: G = dO F)
+    float* sg = sq + kT * (MC + 1);       // [64][HD] dO
     float* so = sg + kT * HD;             // [64][HD] m + log2(l)
     float* st = so + kT * HD;             // [64 keys][65] scores, then dS
-    float* sR = st + kT * 65;             // [HD] R_c (FAST)
-    float* smq = sR + HD;                 // [64] the query rows' m_i (FAST)
     const int kt = blockIdx.x, bh = blockIdx.y;
     const int b = bh / a.H, h = bh - b * a.H;
     const int r = threadIdx.x >> 2, q4 = threadIdx.x & 3;
@@ -400,12 +370,6 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
             vr[c + 1] = a.kf * t.y;
         }
     }
-    if (FAST) {  // vr becomes E_V of this key row
-        if (threadIdx.x < HD) sR[threadIdx.x] = a.rv[static_cast<size_t>(bh) * HD + threadIdx.x];
-        const float* R = a.rv + static_cast<size_t>(bh) * HD + q4 * CPT;
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) vr[c] = ex2(vr[c] - R[c]);
-    }
     float dv[CPT], dk[MPT], dcb = 0.f;
 #pragma unroll
     for (int c = 0; c < CPT; ++c) dv[c] = 0.f;
@@ -418,20 +382,11 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
         stage_rows<MC>(sq, MC + 1, a.qc + base * MC, MC, 0, i0, a.N, 1.0f);
         stage_rows<HD>(sg, HD, a.dO + static_cast<size_t>(b) * a.N * a.D, a.D, h * HD, i0, a.N, 1.0f);
         stage_o2<HD>(so, a.o2 + base * HD, i0, a.N);
-        if (FAST && threadIdx.x < kT) {
-            float mm = 0.f;
-            if (i0 + threadIdx.x < a.N) mm = a.mrow[static_cast<size_t>(bh) * a.Npad + i0 + threadIdx.x];
-            smq[threadIdx.x] = mm == -INFINITY ? 0.f : mm;
-        }
         __syncthreads();
-        if (FAST) {  // G = dO 2^(m_i + R_c - t_ic); 0 on rows past N or without keys (t = +inf)
-            for (int e = threadIdx.x; e < kT * HD; e += kThreads)
-                sg[e] *= ex2(smq[e / HD] + sR[e % HD] - so[e]);
-        }
         score_tile<MC>(st, sk, sq, r, q4, a.kf2, a, i0, j0, false);  // st[key r][query]
         __syncthreads();
         float* srow = st + r * 65;
-        float dsv[kT / 4], esv[kT / 4];
+        float dsv[kT / 4];
         for (int ib = 0; ib < kT; ib += kT / 4) {
 #pragma unroll
             for (int t = 0; t < kT / 4; ++t) {
@@ -440,31 +395,16 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
                 const float4* g4 = reinterpret_cast<const float4*>(sg + ii * HD + q4 * CPT);
                 const float4* o4 = reinterpret_cast<const float4*>(so + ii * HD + q4 * CPT);
                 float part = 0.f;
-                if (FAST) {
-                    const float es = ex2(s - smq[ii]);
-                    esv[t] = es;
 #pragma unroll
-                    for (int c4 = 0; c4 < CPT / 4; ++c4) {
-                        const float4 gg = g4[c4];
-                        dv[4 * c4] = fmaf(es, gg.x, dv[4 * c4]);
-                        dv[4 * c4 + 1] = fmaf(es, gg.y, dv[4 * c4 + 1]);
-                        dv[4 * c4 + 2] = fmaf(es, gg.z, dv[4 * c4 + 2]);
-                        dv[4 * c4 + 3] = fmaf(es, gg.w, dv[4 * c4 + 3]);
-                        part = fmaf(gg.x, vr[4 * c4], fmaf(gg.y, vr[4 * c4 + 1],
-                                    fmaf(gg.z, vr[4 * c4 + 2], fmaf(gg.w, vr[4 * c4 + 3], part))));
-                    }
-                } else {
-#pragma unroll
-                    for (int c4 = 0; c4 < CPT / 4; ++c4) {
-                        const float4 gg = g4[c4], oo = o4[c4];
-                        const float p0 = ex2(s + vr[4 * c4] - oo.x), p1 = ex2(s + vr[4 * c4 + 1] - oo.y);
-                        const float p2 = ex2(s + vr[4 * c4 + 2] - oo.z), p3 = ex2(s + vr[4 * c4 + 3] - oo.w);
-                        dv[4 * c4] = fmaf(gg.x, p0, dv[4 * c4]);
-                        dv[4 * c4 + 1] = fmaf(gg.y, p1, dv[4 * c4 + 1]);
-                        dv[4 * c4 + 2] = fmaf(gg.z, p2, dv[4 * c4 + 2]);
-                        dv[4 * c4 + 3] = fmaf(gg.w, p3, dv[4 * c4 + 3]);
-                        part = fmaf(gg.x, p0, fmaf(gg.y, p1, fmaf(gg.z, p2, fmaf(gg.w, p3, part))));
-                    }
+                for (int c4 = 0; c4 < CPT / 4; ++c4) {
+                    const float4 gg = g4[c4], oo = o4[c4];
+                    const float p0 = ex2(s + vr[4 * c4] - oo.x), p1 = ex2(s + vr[4 * c4 + 1] - oo.y);
+                    const float p2 = ex2(s + vr[4 * c4 + 2] - oo.z), p3 = ex2(s + vr[4 * c4 + 3] - oo.w);
+                    dv[4 * c4] = fmaf(gg.x, p0, dv[4 * c4]);
+                    dv[4 * c4 + 1] = fmaf(gg.y, p1, dv[4 * c4 + 1]);
+                    dv[4 * c4 + 2] = fmaf(gg.z, p2, dv[4 * c4 + 2]);
+                    dv[4 * c4 + 3] = fmaf(gg.w, p3, dv[4 * c4 + 3]);
+                    part = fmaf(gg.x, p0, fmaf(gg.y, p1, fmaf(gg.z, p2, fmaf(gg.w, p3, part))));
                 }
                 part += __shfl_xor_sync(0xffffffffu, part, 1);
                 part += __shfl_xor_sync(0xffffffffu, part, 2);
@@ -473,7 +413,7 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
             __syncwarp();
 #pragma unroll
             for (int t = 0; t < kT / 4; ++t)
-                if ((t & 3) == q4) srow[ib + t] = FAST ? esv[t] * dsv[t] : dsv[t];
+                if ((t & 3) == q4) srow[ib + t] = dsv[t];
         }
         __syncthreads();
         for (int ii = 0; ii < kT; ++ii) {
@@ -482,10 +422,6 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_k_kernel(const SmArgs
 #pragma unroll
             for (int c = 0; c < MPT; ++c) dk[c] = fmaf(ds, sq[ii * (MC + 1) + q4 * MPT + c], dk[c]);
         }
-    }
-    if (FAST) {
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) dv[c] *= vr[c];
     }
     if (j < a.N) {
         __half* dvd = a.dcat + (static_cast<size_t>(b) * a.N + j) * a.Cp + a.Hp + h * HD + q4 * CPT;
@@ -504,11 +440,11 @@ size_t fwd_smem() {
 }
 template <int MC, int HD>
 size_t bwd_q_smem() {
-    return sizeof(float) * (2 * kT * (MC + 1) + kT * MC + kT * HD + kT * 65 + HD);
+    return sizeof(float) * (2 * kT * (MC + 1) + kT * MC + kT * HD + kT * 65);
 }
 template <int MC, int HD>
 size_t bwd_k_smem() {
-    return sizeof(float) * (2 * kT * (MC + 1) + 2 * kT * HD + kT * 65 + HD + kT);
+    return sizeof(float) * (2 * kT * (MC + 1) + 2 * kT * HD + kT * 65);
 }
 
 SmArgs make_args(const Shape& s, const ProjOut& p) {
@@ -547,33 +483,22 @@ int run_fwd(const SmArgs& a, int BH, cudaStream_t stream) {
     return MORPHO_OK;
 }
 
-template <int MC, int HD, bool FAST>
-int run_bwd_pair(const SmArgs& a, int BH, cudaStream_t stream) {
-    auto kq = soft_morph_bwd_q_kernel<MC, HD, FAST>;
-    auto kk = soft_morph_bwd_k_kernel<MC, HD, FAST>;
+// The exact pair; with a.flag set it is the tensor-core backward's guard (runs only when the
+// forward flagged an accumulator).
+template <int MC, int HD>
+int run_bwd(const SmArgs& a, int BH, cudaStream_t stream) {
+    auto kq = soft_morph_bwd_q_kernel<MC, HD>;
+    auto kk = soft_morph_bwd_k_kernel<MC, HD>;
     const size_t sq = bwd_q_smem<MC, HD>(), sk = bwd_k_smem<MC, HD>();
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sq)));
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sk)));
     prof_begin(stream);
     kq<<<dim3(a.n_tiles, BH), kThreads, sq, stream>>>(a);
-    MORPHO_LAUNCH_CHECK(FAST ? "soft_morph_bwd_q_split" : "soft_morph_bwd_q");
+    MORPHO_LAUNCH_CHECK("soft_morph_bwd_q");
     prof_begin(stream);
     kk<<<dim3(a.n_tiles, BH), kThreads, sk, stream>>>(a);
-    MORPHO_LAUNCH_CHECK(FAST ? "soft_morph_bwd_k_split" : "soft_morph_bwd_k");
+    MORPHO_LAUNCH_CHECK("soft_morph_bwd_k");
     return MORPHO_OK;
-}
-
-// With the tensor-core forward's flag: the factorized pair runs when it is clear, the exact
-// pair when it is set (each launch returns at once otherwise).  Without it: the exact pair.
-template <int MC, int HD>
-int run_bwd(const SmArgs& a, int BH, cudaStream_t stream) {
-    if (a.flag == nullptr) return run_bwd_pair<MC, HD, false>(a, BH, stream);
-    SmArgs f = a;
-    f.run_if_flag = 0;
-    MORPHO_TRY((run_bwd_pair<MC, HD, true>(f, BH, stream)));
-    SmArgs e = a;
-    e.run_if_flag = 1;
-    return run_bwd_pair<MC, HD, false>(e, BH, stream);
 }
 
 // (cube_m, head_dim) dispatch
@@ -596,10 +521,6 @@ struct Fwd {
 template <int MC, int HD>
 struct Bwd {
     static int run(const SmArgs& a, int BH, cudaStream_t st) { return run_bwd<MC, HD>(a, BH, st); }
-};
-template <int MC, int HD>
-struct BwdExact {
-    static int run(const SmArgs& a, int BH, cudaStream_t st) { return run_bwd_pair<MC, HD, false>(a, BH, st); }
 };
 
 }  // namespace
@@ -632,15 +553,14 @@ int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* 
     a.dk = dk;
     a.dcb = dcb;
     a.dcat = dcat;
-    if (!soft_morph_exact_only()) {  // the forward that wrote o2 also wrote m, R and the flag
+    if (!soft_morph_exact_only()) {
+        // the split forward that wrote o2 also wrote m, R and the range flag: the tensor-core pair
+        // runs when the flag is clear, the exact pair (below) when it is set
+        if (tcx == nullptr)
+            return set_error(MORPHO_ERR_INVALID, "internal: soft-morphology backward scratch missing");
+        MORPHO_TRY(launch_soft_morph_bwd_tc(s, p, *tcx, dO, o2, dq, dqb, dk, dcb, dcat, status, stream));
         a.flag = p.smflag;
-        a.mrow = p.mrow;
-        a.rv = p.rv;
-        if (tcx != nullptr && s.hd <= 64) {  // tensor-core split pair, then the gated exact pair
-            MORPHO_TRY(launch_soft_morph_bwd_tc(s, p, *tcx, dO, o2, dq, dqb, dk, dcb, dcat, status, stream));
-            a.run_if_flag = 1;
-            return dispatch<BwdExact>(s, a, stream);
-        }
+        a.run_if_flag = 1;
     }
     return dispatch<Bwd>(s, a, stream);
 }

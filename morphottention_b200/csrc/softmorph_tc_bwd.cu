@@ -20,9 +20,10 @@
 //   sm_bwd_k_kernel   : per 128-key tile: S^T = k . qc^T, X^T = E_V . G^T, E_S^T and dS^T written
 //                       over S^T and X^T in TMEM, dV += E_S^T . G and dk += dS^T . qc (A from TMEM),
 //                       dcb (row sums); dV scaled by E_V in the epilogue
-// Head dims 32 and 64 (the shared-memory stages of hd = 128 do not fit); hd = 128 runs the
-// CUDA-core split kernels.  The kernels return at once when the forward set its range flag (the
-// exact kernels then run instead).
+// Every (cube_m, head_dim) of the path: the key side's ring stages hold a whole 128-query tile
+// where two of them fit in shared memory and a 64-query half tile otherwise (head dim 128); the
+// query side runs a 1- to 3-stage ring.  The kernels return at once when the forward set its range
+// flag (the exact kernels then run instead).
 #include "kernels.h"
 #include "sm100.cuh"
 
@@ -406,11 +407,20 @@ template <int MC, int HD>
 struct KCfg {
     static constexpr int K_BYTES = kTile * MC * 2;
     static constexpr int EV_BYTES = HD * kTile * 4;
-    static constexpr int QC_BYTES = kTile * MC * 2;
-    static constexpr int G_BYTES = HD * kTile * 4;
-    static constexpr int GT_BYTES = 4 * HD * 128;   // four 32-query chunks of [HD rows x 128 B]
-    static constexpr int QT_BYTES = 4 * MC * 128;   // four 32-query chunks of [MC rows x 128 B]
     static constexpr int OFF_K = 0, OFF_EV = align1k(K_BYTES), OFF_STAGE = OFF_EV + EV_BYTES;
+    // one ring stage holds QS queries: Qc [QS x MC] f16, G in HD/32 chunks of [QS rows x 128 B],
+    // G^T and Qc^T in QS/32 chunks of [HD or MC rows x 128 B]
+    static constexpr int stage_bytes(int qs) {
+        return align1k(qs * MC * 2) + HD * qs * 4 + (qs / 32) * HD * 128 + (qs / 32) * MC * 128;
+    }
+    // a whole 128-query tile per stage where two such stages fit, else one 64-query half tile
+    static constexpr int QS = (OFF_STAGE + 2 * stage_bytes(128) + 3072 <= 220 * 1024) ? 128 : 64;
+    static constexpr int UPS = QS / 64;  // 64-query units per stage
+    static constexpr int QC_BYTES = QS * MC * 2;
+    static constexpr int G_CHUNK = QS * 128;
+    static constexpr int G_BYTES = HD * QS * 4;
+    static constexpr int GT_BYTES = (QS / 32) * HD * 128;
+    static constexpr int QT_BYTES = (QS / 32) * MC * 128;
     static constexpr int OFF_SQC = 0, OFF_SG = align1k(QC_BYTES), OFF_SGT = OFF_SG + G_BYTES,
                          OFF_SQT = OFF_SGT + GT_BYTES;
     static constexpr int STAGE = OFF_SQT + QT_BYTES;
@@ -498,23 +508,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb < HD / 32; ++kb)
                 tma_load_3d(smem_u32(smem + Cfg::OFF_EV) + kb * 16384, &tmEV, k_full, 32 * kb, j0, bh);
             int issued = 0;
-            for (int i = 0; i < n_it; ++i) {
+            const int n_st = n_u / Cfg::UPS;  // ring fills
+            for (int i = 0; i < n_st; ++i) {
                 const int s = i % ST;
                 if (i >= ST && !mbar_wait(st_empty0 + 8 * s, ((i / ST) & 1) ^ 1, args.status, K_SOFT_MORPH, 61)) {
                     *abort_flag = 1u;
                     break;
                 }
                 if (*abort_flag) break;
-                const int q0 = (it0 + i) * kTile;
+                const int q0 = it0 * kTile + i * Cfg::QS;
                 const uint32_t fb = st_full0 + 8 * s, sb = stage_base(s);
                 mbar_arrive_expect_tx(fb, Cfg::TX_STAGE);
                 tma_load_3d(sb + Cfg::OFF_SQC, &tmQ, fb, 0, q0, bh);
 #pragma unroll
-                for (int kb = 0; kb < HD / 32; ++kb) tma_load_3d(sb + Cfg::OFF_SG + kb * 16384, &tmG, fb, 32 * kb, q0, bh);
+                for (int kb = 0; kb < HD / 32; ++kb)
+                    tma_load_3d(sb + Cfg::OFF_SG + kb * Cfg::G_CHUNK, &tmG, fb, 32 * kb, q0, bh);
 #pragma unroll
-                for (int kb = 0; kb < 4; ++kb) {
-                    tma_load_3d(sb + Cfg::OFF_SGT + kb * HD * 128, &tmGT, fb, q0 + 32 * kb, 0, bh);
-                    tma_load_3d(sb + Cfg::OFF_SQT + kb * MC * 128, &tmQT, fb, q0 + 32 * kb, 0, bh);
+                for (int c = 0; c < Cfg::QS / 32; ++c) {
+                    tma_load_3d(sb + Cfg::OFF_SGT + c * HD * 128, &tmGT, fb, q0 + 32 * c, 0, bh);
+                    tma_load_3d(sb + Cfg::OFF_SQT + c * MC * 128, &tmQT, fb, q0 + 32 * c, 0, bh);
                 }
                 ++issued;
             }
@@ -538,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t qk_sbo = 8 * Cfg::QK_ROW;
             const uint32_t sK = smem_u32(smem + Cfg::OFF_K), sEV = smem_u32(smem + Cfg::OFF_EV);
             auto issue_sx = [&](int u) -> bool {
-                const int i = u >> 1, h = u & 1, s = i % ST;
+                const int i = u / Cfg::UPS, h = u % Cfg::UPS, s = i % ST;  // ring fill, unit within it
                 const uint32_t sb = stage_base(s);
                 if (h == 0) {
                     if (!mbar_wait(st_full0 + 8 * s, (i / ST) & 1, args.status, K_SOFT_MORPH, 64)) return false;
@@ -555,16 +567,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
                         umma_ss_tf32(dst + 64, make_sdesc(sEV + kb * 16384 + ks * 32, 16, 1024, SW_128),
-                                     make_sdesc(sb + Cfg::OFF_SG + kb * 16384 + h * 8192 + ks * 32, 16, 1024, SW_128),
+                                     make_sdesc(sb + Cfg::OFF_SG + kb * Cfg::G_CHUNK + h * 8192 + ks * 32, 16, 1024,
+                                                SW_128),
                                      id_x, (kb > 0 || ks > 0) ? 1u : 0u);
                 umma_commit((u & 1) ? sx_full1 : sx_full0);
                 return true;
             };
-            bool ok = mbar_wait(k_full, 0, args.status, K_SOFT_MORPH, 63);
-            if (ok && n_u > 0) ok = issue_sx(0);
-            if (ok && n_u > 1) ok = issue_sx(1);
+            // S^T / X^T of unit v go out once its slot's previous reader dV / dk(v - 2) has been
+            // issued and its ring fill has been loaded, which needs the fill ST earlier released
+            // (its last unit's dV / dk issued): v <= u + 2 and (v/UPS - ST + 1) * UPS - 1 <= u
+            int next_sx = 0;
+            auto issue_ready = [&](int u) -> bool {
+                while (next_sx < n_u && next_sx <= u + 2 &&
+                       (next_sx / Cfg::UPS - ST + 1) * Cfg::UPS - 1 <= u) {
+                    if (!issue_sx(next_sx)) return false;
+                    ++next_sx;
+                }
+                return true;
+            };
+            bool ok = mbar_wait(k_full, 0, args.status, K_SOFT_MORPH, 63) && issue_ready(-1);
             for (int u = 0; ok && u < n_u; ++u) {
-                const int i = u >> 1, h = u & 1, s = i % ST, b = u & 1;
+                const int i = u / Cfg::UPS, h = u % Cfg::UPS, s = i % ST, b = u & 1;
                 const uint32_t sb = stage_base(s);
                 if (!mbar_wait(b ? ed_full1 : ed_full0, (u >> 1) & 1, args.status, K_SOFT_MORPH, 65)) {
                     ok = false;
@@ -573,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t src = tmem + b * 128;
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {  // the half tile's two 32-query chunks
+                for (int c = 0; c < 2; ++c) {  // the unit's two 32-query chunks of the ring fill
                     const int kb = 2 * h + c;
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks) {
@@ -586,17 +609,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      acc);
                     }
                 }
-                if (h == 1) umma_commit(st_empty0 + 8 * s);
-                if (ST > 1) {
-                    if (u + 2 < n_u && !issue_sx(u + 2)) {
-                        ok = false;
-                        break;
-                    }
-                } else if (h == 1) {  // one stage: the next tile loads only after this one's dV / dk
-                    if ((u + 1 < n_u && !issue_sx(u + 1)) || (u + 2 < n_u && !issue_sx(u + 2))) {
-                        ok = false;
-                        break;
-                    }
+                if (h == Cfg::UPS - 1) umma_commit(st_empty0 + 8 * s);
+                if (!issue_ready(u)) {
+                    ok = false;
+                    break;
                 }
             }
             if (ok) {
@@ -801,7 +817,11 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
     auto kk = sm_bwd_k_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, KCfg<MC, HD>::SMEM_BYTES));
     prof_begin(stream);
-    kk<<<dim3(n_tiles, BH), kThreads, KCfg<MC, HD>::SMEM_BYTES, stream>>>(tK, tQ, tEV, tG, tGT, tQT, ka);
+    // the key side's ring stages hold KCfg::QS queries (Qc and G boxes of that many rows)
+    CUtensorMap tQk, tGk;
+    MORPHO_TRY(make_tmap_3d_f16(&tQk, p.qc, MC, N, BH, MC, static_cast<uint64_t>(N) * MC, MC, KCfg<MC, HD>::QS));
+    MORPHO_TRY(tmap_f32_3d(&tGk, x.g, HD, N, BH, 32, KCfg<MC, HD>::QS));
+    kk<<<dim3(n_tiles, BH), kThreads, KCfg<MC, HD>::SMEM_BYTES, stream>>>(tK, tQk, tEV, tGk, tGT, tQT, ka);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_bwd_k");
     return MORPHO_OK;
 }
@@ -818,9 +838,9 @@ int launch_soft_morph_bwd_tc(const Shape& s, const ProjOut& p, const SmBwdScratc
     if (s.m == M && s.hd == HDV)                                                                              \
         return s.causal ? run_tc_bwd<M, HDV, true>(s, p, x, dO, o2, dq, dqb, dk, dcb, dcat, status, st)       \
                         : run_tc_bwd<M, HDV, false>(s, p, x, dO, o2, dq, dqb, dk, dcb, dcat, status, st);
-    MORPHO_TCB_CASE(16, 32) MORPHO_TCB_CASE(16, 64)
-    MORPHO_TCB_CASE(32, 32) MORPHO_TCB_CASE(32, 64)
-    MORPHO_TCB_CASE(64, 32) MORPHO_TCB_CASE(64, 64)
+    MORPHO_TCB_CASE(16, 32) MORPHO_TCB_CASE(16, 64) MORPHO_TCB_CASE(16, 128)
+    MORPHO_TCB_CASE(32, 32) MORPHO_TCB_CASE(32, 64) MORPHO_TCB_CASE(32, 128)
+    MORPHO_TCB_CASE(64, 32) MORPHO_TCB_CASE(64, 64) MORPHO_TCB_CASE(64, 128)
 #undef MORPHO_TCB_CASE
     return set_error(MORPHO_ERR_INVALID, "soft-morphology tensor-core backward: cube_m %d, head_dim %d not supported",
                      s.m, s.hd);

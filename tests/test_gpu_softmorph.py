@@ -26,7 +26,7 @@ CASES = [
     MorphoConfig("m16_hd32", 2, 64, 128, 4, 16, 1.0, True, 44),
     MorphoConfig("n1", 1, 1, 128, 2, 16, 1.0, False, 49),
     MorphoConfig("n15_causal", 2, 15, 128, 4, 32, 0.8, True, 50),
-    MorphoConfig("m64_hd64_causal", 1, 300, 128, 2, 64, 0.3, True, 51),  # one-stage key-side ring
+    MorphoConfig("m64_hd64_causal", 1, 300, 128, 2, 64, 0.3, True, 51),  # 64-query key-side ring stages
 ]
 
 
