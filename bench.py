@@ -157,13 +157,17 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def _config_dict(cfg, world, per_step_note=None):
-    d = {"workload": f"{cfg.name}: single MorphoAttention layer fwd + backward(out.sum())",
+def _config_dict(cfg, world, per_step_note=None, score="softmax", tau=1.0):
+    d = {"workload": f"{cfg.name}: single MorphoAttention layer fwd + backward(out.sum())"
+                     + ("" if score == "softmax" else f", soft-morphology score {score} (tau {tau})"),
          "B_per_gpu": cfg.B, "N": cfg.N, "D": cfg.D, "H": cfg.H, "cube_m": cfg.cube_m, "head_dim": cfg.head_dim,
          "scale": cfg.scale, "causal": cfg.causal, "global_batch": cfg.B * world, "seq_len": cfg.N,
          "parallelism": f"dp{world}", "l2": "inputs larger than L2 (>300 MB touched per step), no flush"}
     if per_step_note:
         d["step"] = per_step_note
+    if score != "softmax":
+        d["score"] = score
+        d["tau"] = tau
     return d
 
 
@@ -187,7 +191,10 @@ def algorithmic_flops(cfg):
     nn = cfg.pairs()
     gemm = 2.0 * T * cfg.D * (cfg.H * m + cfg.D)
     return {"attn_bwd": 2.0 * nn * (3 * m + 2 * hd), "attn_fwd": 2.0 * nn * (m + hd), "proj": gemm,
-            "dx_gemm": gemm, "dw_gemm": gemm}
+            "dx_gemm": gemm, "dw_gemm": gemm,
+            # soft-morphology split path: S (f16) + E_S.E_V / G.E_V^T, dS.kd / E_S^T.G, dS^T.qc (tf32)
+            "soft_morph_tc_fwd": 2.0 * nn * (m + hd), "soft_morph_tc_bwd_q": 2.0 * nn * (2 * m + hd),
+            "soft_morph_tc_bwd_k": 2.0 * nn * (2 * m + 2 * hd)}
 
 
 def run_ours(args):
@@ -218,7 +225,9 @@ def run_ours(args):
         w["x"] = torch.empty(cfg.B, cfg.N, cfg.D).normal_(0.0, 1.0, generator=g).half()
     t = {k: v.to(dev) for k, v in w.items()}
     x, W_phi, gq, gk, W_V = t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"]
-    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score=args.score, tau=args.tau)
+    if args.score != "softmax":  # the module path (e2e) reads the score from the op settings
+        M.set_score(args.score, args.tau)
     grad = torch.ones_like(x)  # d out.sum() / d out
     out = torch.empty_like(x)
     lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
@@ -376,9 +385,12 @@ def run_ours(args):
         per_launch_s = prof[dom][0] / prof[dom][1] / 1000.0
         achieved = flops.get(dom, 0.0) / per_launch_s / 1e12
         peak = peaks["bf16_tflops_sustained"]
+        note = f"{peaks['source']} dense bf16 (sustained, kernel timed inside a step); fp16 rate equal"
+        if dom.startswith("soft_morph_tc"):  # mostly kind::tf32 MMAs: half the dense 16-bit rate
+            peak /= 2.0
+            note = f"half the {peaks['source']} dense bf16 rate (sustained): the tf32 rate"
         roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": _traffic(dom, args.config, cfg),
-                "peak_note": f"{peaks['source']} dense bf16 (sustained, kernel timed inside a step); fp16 rate equal",
+                "frac": achieved / peak, "traffic": _traffic(dom, args.config, cfg), "peak_note": note,
                 "flops_per_launch": flops.get(dom, 0.0)}
         if dom in ("attn_bwd", "attn_fwd"):
             sm_mhz = clocks.get("sm_mhz") or peaks["sm_max_mhz"]
@@ -390,14 +402,16 @@ def run_ours(args):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic: x~N(0,1) seeded, module default init",
-            "config": _config_dict(cfg, world), "roofline": roof, "e2e": e2e,
+            "config": _config_dict(cfg, world, score=args.score, tau=args.tau), "roofline": roof, "e2e": e2e,
             "gpu_launches": int(sum(v[1] for v in prof.values())), "clocks": clocks, "kernels": kernels,
             "tensor_tflops_step": cfg.tensor_flops_fwd_bwd() / (ms / args.steps / 1000.0) / 1e12,
             "step_roofline_frac": (cfg.tensor_flops_fwd_bwd() / (peaks["bf16_tflops_sustained"] * 1e12))
             / (ms / args.steps / 1000.0),
             "device_status": status}
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.score == "softmax":
         line["cpu_baseline"] = cpu_baseline(cfg)
+    elif args.score != "softmax":  # the fp32 oracle materialises [B, H, N, N, hd]: not at these sizes
+        line["cpu_baseline"] = None
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -645,7 +659,12 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (small cases for profiler captures)")
+    ap.add_argument("--score", choices=["softmax", "dilation", "erosion"], default="softmax",
+                    help="the attention score: softmax (the reference's), or the soft-morphology aggregation")
+    ap.add_argument("--tau", type=float, default=1.0, help="temperature of the soft-morphology score")
     args = ap.parse_args()
+    if args.score != "softmax" and (args.impl == "reference" or args.config == "c4vit"):
+        raise SystemExit("--score applies to the single-layer configurations of --impl ours")
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.config == "c4vit":
