@@ -76,3 +76,18 @@ def test_grad_mode_switch():
     assert M.get_grad_mode() == "full"
     with pytest.raises(ValueError):
         M.set_grad_mode("bogus")
+
+
+def test_bench_rejects_score_outside_single_layer_ours():
+    """`bench.py --score` times the soft-morphology score on the single-layer configurations of
+    this library only: with the reference arm or the encoder step it stops before any work."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for extra in (["--impl", "reference"], ["--config", "c4vit"]):
+        r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--score", "dilation", *extra],
+                           capture_output=True, text=True, timeout=120)
+        assert r.returncode != 0
+        assert "--score applies to the single-layer configurations" in r.stderr
