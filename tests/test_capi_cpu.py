@@ -6,6 +6,8 @@ import glob
 import os
 import re
 
+import pytest
+
 from morphottention_b200 import capi
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -92,3 +94,19 @@ def test_soft_morph_workspace_keeps_statistics():
     BH, N, Npad, hd = 4, 100, 128, 64
     need = BH * N * hd * 4 + BH * hd * Npad * 4 + BH * hd * 4 + BH * 1 * hd * 4 + 64 * 4 + BH * Npad * 4
     assert need <= extra <= need + 6 * 256
+
+
+@pytest.mark.parametrize("H", [4, 2, 1])  # head dims 32, 64, 128 at D = 128
+def test_soft_morph_backward_workspace_holds_tensor_core_operands(H):
+    """The backward workspace of a soft-morphology problem also holds the fp32 operand layouts of
+    its tensor-core kernels (G [B*H, N, hd], G^T and E_V [B*H, hd, Npad], kd^T and qc^T
+    [B*H, m, Npad]) for every head dim; the softmax score needs none of them."""
+    L = capi.lib()
+    B, N, D, m = 2, 100, 128, 16
+    a = capi.problem(B, N, D, H, m)
+    b = capi.problem(B, N, D, H, m, score="erosion", tau=0.7)
+    extra = L.morpho_sm100_backward_workspace_size(ctypes.byref(b)) - L.morpho_sm100_backward_workspace_size(
+        ctypes.byref(a))
+    BH, hd, Npad = B * H, D // H, 128
+    operands = 4 * (BH * N * hd + 2 * BH * hd * Npad + 2 * BH * m * Npad)
+    assert extra >= operands
