@@ -116,13 +116,13 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
 int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, const uint32_t* only_if,
                           cudaStream_t stream);
 // Soft-morphology path choice: the environment variable MORPHO_SOFT_MORPH_EXACT (set and not
-// "0") selects the exact CUDA-core kernels only; otherwise the split (tensor-core forward,
-// FMA backward) runs, guarded by the exact kernels.
+// "0") selects the exact CUDA-core kernels only; otherwise the split (tensor-core forward and
+// backward) runs, guarded by the exact kernels.
 bool soft_morph_exact_only();
 // Tensor-core forward (E_S . E_V split) followed by the exact forward as its guard.
 int launch_soft_morph_fwd_tc(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out, float* o2,
                              cudaStream_t stream);
-// fp32 operand layouts of the tensor-core soft-morphology backward (head dims 32 and 64):
+// fp32 operand layouts of the tensor-core soft-morphology backward (every head dim):
 // G [B*H, N, hd], G^T [B*H, hd, Npad], E_V [B*H, Npad, hd], kd^T and qc^T [B*H, m, Npad].
 struct SmBwdScratch {
     float* g = nullptr;

@@ -3,8 +3,8 @@ the reference's kernels): out_ic = sgn tau logsumexp_j(sgn (S_ij + V_jc) / tau),
 (sgn = +1) and erosion (sgn = -1), through the C ABI and the module, against the fp32 oracle
 restatement with the attention path's tolerances (rel-L2 <= 1e-3 out, <= 5e-3 gradients).
 
-Both paths are checked: the split one (tensor-core forward over E_S . E_V, FMA backward, with
-the exact kernels as a device-side guard) and the exact CUDA-core kernels alone, selected with
+Both paths are checked: the split one (tensor-core forward over E_S . E_V and tensor-core
+backward, with the exact kernels as a device-side guard) and the exact CUDA-core kernels alone, selected with
 the MORPHO_SOFT_MORPH_EXACT environment variable."""
 
 import pytest
@@ -155,6 +155,23 @@ def test_soft_morph_exact_forward_then_split_backward(cuda, monkeypatch):
     ours = {"out": out}
     ours.update(dict(zip(("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), grads)))
     compare(ours, oracle(cfg, inp, g, "erosion", 0.7), tol_gate=gate_tolerance(cfg))
+
+
+@pytest.mark.parametrize("name,score,tau", [("c3", "dilation", 1.0), ("c5", "erosion", 0.5)])
+def test_soft_morph_full_size_split_matches_exact(cuda, monkeypatch, name, score, tau):
+    """One sequence of c3 (N = 4096, hd 64) and of c5 (N = 8192, hd 128, causal): the split
+    tensor-core path against the exact CUDA-core kernels, which the oracle pins at small sizes and
+    whose arithmetic does not depend on N, with the oracle tolerances. The guard must not fire at
+    these taus (the two runs differ), so the comparison covers the tensor-core kernels' long
+    key and query loops and their multi-stage rings."""
+    from morphottention_b200.configs import CONFIGS
+    cfg = CONFIGS[name].with_(B=1)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    split, exact = _both_paths(cfg, inp, g, score, tau, monkeypatch)
+    assert not torch.equal(split["out"], exact["out"])
+    errs = compare(split, exact, tol_gate=gate_tolerance(cfg))
+    print(name, {k: f"{v:.2e}" for k, v in errs.items()})
 
 
 def test_soft_morph_invalid_problems(cuda):
