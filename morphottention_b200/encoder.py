@@ -60,3 +60,53 @@ class Encoder(nn.Module):
         for blk in self.blocks:
             x = blk(x)
         return x
+
+
+class GraphedTrainingStep:
+    """One training step (forward, loss, backward, optimizer step) captured once as a CUDA graph
+    and replayed per batch, so the step's several hundred launches (LayerNorm, GELU, cuBLAS MLP
+    GEMMs, this library's attention kernels, the foreach optimizer update) cost one graph launch
+    on the host instead of one Python dispatch each.
+
+    ``step = GraphedTrainingStep(model, loss_fn, optimizer, x, target)`` runs ``warmup`` ordinary
+    training steps on ``(x, target)`` on a side stream (real updates: they create the optimizer's
+    state, the cuBLAS handles and this library's per-device state before capture, as CUDA graph
+    capture requires), then captures ``loss_fn(model(x), target); loss.backward();
+    optimizer.step()`` with the gradients unset at capture, so every replay assigns them afresh
+    like ``zero_grad(set_to_none=True)`` before an eager step.  ``step(x_batch, target_batch)``
+    copies the batch into the captured input buffers on the current stream, replays, and returns
+    the loss tensor (the same storage every call: copy it out before the next call).
+
+    Parameters, gradients and optimizer state live at fixed addresses from then on; changing the
+    learning rate needs a tensor ``lr`` in the optimizer or a new capture.  The model must not
+    change between calls (no new parameters, no shape change of the batch)."""
+
+    def __init__(self, model: nn.Module, loss_fn, optimizer: torch.optim.Optimizer, x: torch.Tensor,
+                 target: torch.Tensor, warmup: int = 3) -> None:
+        if not x.is_cuda:
+            raise ValueError("GraphedTrainingStep needs CUDA inputs")
+        self.model, self.loss_fn, self.optimizer = model, loss_fn, optimizer
+        self.x = x.detach().clone()
+        self.target = target.detach().clone()
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                optimizer.zero_grad(set_to_none=True)
+                loss_fn(model(self.x), self.target).backward()
+                optimizer.step()
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        optimizer.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.loss = loss_fn(model(self.x), self.target)
+            self.loss.backward()
+            optimizer.step()
+
+    def __call__(self, x: torch.Tensor | None = None, target: torch.Tensor | None = None) -> torch.Tensor:
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        if target is not None:
+            self.target.copy_(target, non_blocking=True)
+        self.graph.replay()
+        return self.loss.detach()

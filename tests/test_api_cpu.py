@@ -91,3 +91,14 @@ def test_bench_rejects_score_outside_single_layer_ours():
                            capture_output=True, text=True, timeout=120)
         assert r.returncode != 0
         assert "--score applies to the single-layer configurations" in r.stderr
+
+
+def test_graphed_training_step_needs_cuda_inputs():
+    import torch
+
+    from morphottention_b200.encoder import GraphedTrainingStep
+
+    lin = torch.nn.Linear(4, 4)
+    opt = torch.optim.SGD(lin.parameters(), lr=0.1)
+    with pytest.raises(ValueError, match="CUDA"):
+        GraphedTrainingStep(lin, torch.nn.functional.mse_loss, opt, torch.zeros(2, 4), torch.zeros(2, 4))

@@ -8,7 +8,7 @@ import pytest
 import torch
 from torch import nn
 
-from morphottention_b200.encoder import Encoder
+from morphottention_b200.encoder import Encoder, GraphedTrainingStep
 from oracle import morpho_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -56,3 +56,55 @@ def test_encoder_step_matches_oracle_model(cuda, out_proj):
         assert p.grad is not None and pc.grad is not None, name
         err = O.rel_l2(p.grad.float().cpu(), pc.grad)
         assert err <= 1.5e-2, f"{name}: {err:.2e}"
+
+
+def test_graphed_training_step_matches_eager(cuda):
+    """GraphedTrainingStep (the training step captured once as a CUDA graph, attention kernels
+    included) against eager steps from the same initial weights: after its 3 warm-up steps and
+    after 3 replays on new batches, every parameter's change from the initial weights matches the
+    eager model's to 2 fp16 ulps of the weight plus 1 % of the change (the dq accumulation order
+    differs from run to run), and so does each replay's loss (1e-3)."""
+    torch.manual_seed(5)
+    kw = dict(depth=2, dim=128, num_heads=2, cube_m=16, scale=0.5, device=cuda)
+    eager = Encoder(**kw)
+    graphed = Encoder(**kw)
+    graphed.load_state_dict(eager.state_dict())
+    init = {k: v.detach().float().clone() for k, v in eager.named_parameters()}
+    opt_e = torch.optim.SGD(eager.parameters(), lr=0.05, foreach=True)
+    opt_g = torch.optim.SGD(graphed.parameters(), lr=0.05, foreach=True)
+
+    def loss_fn(out, t):
+        return nn.functional.mse_loss(out.float(), t)
+
+    def eager_step(x, t):
+        loss = loss_fn(eager(x), t)
+        opt_e.zero_grad(set_to_none=True)
+        loss.backward()
+        opt_e.step()
+        return loss.detach()
+
+    def check():
+        pe = dict(eager.named_parameters())
+        moved = 0.0
+        for name, p in graphed.named_parameters():
+            a, b = pe[name].detach().float(), p.detach().float()
+            moved = max(moved, (a - init[name]).abs().max().item())
+            # two fp16 ulps of the weight: an update near a rounding boundary may round either way
+            tol = 2.0 ** -9 * a.abs() + 1e-2 * (a - init[name]).abs() + 1e-7
+            assert ((a - b).abs() <= tol).all(), name
+        assert moved > 0
+
+    g = torch.Generator().manual_seed(6)
+    batches = [(torch.randn(2, 50, 128, generator=g).half().to(cuda), torch.randn(2, 50, 128, generator=g).to(cuda))
+               for _ in range(4)]
+    step = GraphedTrainingStep(graphed, loss_fn, opt_g, *batches[0], warmup=3)
+    for _ in range(3):
+        eager_step(*batches[0])
+    torch.cuda.synchronize()
+    check()
+    for x, t in batches[1:]:
+        le = eager_step(x, t)
+        lg = step(x, t)
+        torch.cuda.synchronize()
+        assert abs(lg.item() - le.item()) <= 1e-3 * abs(le.item())
+    check()
