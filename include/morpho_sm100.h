@@ -200,6 +200,9 @@ MORPHO_API int morpho_sm100_last_launch_count(void);
 MORPHO_API void morpho_sm100_profile_enable(int on);
 MORPHO_API int morpho_sm100_profile_collect(char* names, int name_len, float* total_ms, int* counts,
                                             int max_kernels);
+/* Restrict the timing to the launches of one kernel (the name collect() reports, e.g. "attn_bwd"):
+ * the others record no events, so they run as they do unprofiled.  NULL or "" times every launch. */
+MORPHO_API void morpho_sm100_profile_select(const char* kernel_name);
 
 #ifdef __cplusplus
 }

@@ -52,6 +52,7 @@ EXPORTED = (
     "morpho_sm100_selftest_wait_timeout",
     "morpho_sm100_profile_enable",
     "morpho_sm100_profile_collect",
+    "morpho_sm100_profile_select",
 )
 
 
@@ -119,6 +120,8 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_selftest_wait_timeout.restype = i32
     L.morpho_sm100_profile_enable.argtypes = [i32]
     L.morpho_sm100_profile_enable.restype = None
+    L.morpho_sm100_profile_select.argtypes = [ctypes.c_char_p]
+    L.morpho_sm100_profile_select.restype = None
     L.morpho_sm100_profile_collect.argtypes = [ctypes.c_char_p, i32, ctypes.POINTER(ctypes.c_float),
                                                ctypes.POINTER(ctypes.c_int), i32]
     L.morpho_sm100_profile_collect.restype = i32
@@ -292,6 +295,11 @@ def weight_grad_elems(p: MorphoProblem) -> int:
 def profile_enable(on: bool) -> None:
     """Record a CUDA event pair around every kernel launch of the library."""
     lib().morpho_sm100_profile_enable(1 if on else 0)
+
+
+def profile_select(kernel_name: str | None) -> None:
+    """Time only the launches of ``kernel_name`` (a name profile_collect reports); None: all."""
+    lib().morpho_sm100_profile_select(kernel_name.encode() if kernel_name else None)
 
 
 def profile_collect(max_kernels: int = 32) -> dict:

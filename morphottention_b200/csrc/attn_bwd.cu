@@ -632,7 +632,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     auto kern = attn_bwd_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
-    prof_begin(stream);
+    prof_begin(stream, "attn_bwd");
     kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKD, tV, tDO, tL, tQA, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");
     return MORPHO_OK;

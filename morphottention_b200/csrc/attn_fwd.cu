@@ -408,7 +408,7 @@ int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out
     auto kern = attn_fwd_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
-    prof_begin(stream);
+    prof_begin(stream, "attn_fwd");
     kern<<<grid, kFwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, a);
     MORPHO_LAUNCH_CHECK("attn_fwd");
     return MORPHO_OK;

@@ -508,6 +508,8 @@ int morpho_sm100_last_launch_count(void) { return launch_count(); }
 
 void morpho_sm100_profile_enable(int on) { prof_enable(on != 0); }
 
+void morpho_sm100_profile_select(const char* kernel_name) { prof_select(kernel_name); }
+
 int morpho_sm100_profile_collect(char* names, int name_len, float* total_ms, int* counts, int max_kernels) {
     if (names == nullptr || total_ms == nullptr || counts == nullptr || name_len <= 0 || max_kernels <= 0) return 0;
     return prof_collect(names, name_len, total_ms, counts, max_kernels);

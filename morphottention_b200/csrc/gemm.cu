@@ -471,7 +471,7 @@ int run_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap&
     a.splits = splits;
     const int items = a.tiles_m * a.tiles_n * splits;
     const int grid = items < sms ? items : sms;  // persistent: at most one CTA per SM
-    prof_begin(stream);
+    prof_begin(stream, name);
     kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB0, tmB1, a, ep);
     MORPHO_LAUNCH_CHECK(name);
     return MORPHO_OK;

@@ -49,6 +49,7 @@ struct ProfRec {
     cudaEvent_t start, stop;
 };
 bool g_prof_on = false;
+std::string g_prof_only;  // empty: every launch is timed
 thread_local std::vector<ProfRec> t_prof;
 thread_local std::vector<cudaEvent_t> t_event_pool;
 thread_local cudaEvent_t t_pending = nullptr;
@@ -67,8 +68,14 @@ cudaEvent_t take_event() {
 
 void prof_enable(bool on) { g_prof_on = on; }
 
-void prof_begin(cudaStream_t stream) {
+void prof_select(const char* name) { g_prof_only = name ? name : ""; }
+
+void prof_begin(cudaStream_t stream, const char* name) {
     if (!g_prof_on) return;
+    if (!g_prof_only.empty() && (name == nullptr || g_prof_only != name)) {
+        t_pending = nullptr;  // not selected: no events, prof_end records nothing
+        return;
+    }
     t_pending = take_event();
     if (t_pending) cudaEventRecord(t_pending, stream);
 }

@@ -24,9 +24,11 @@ int launch_count();
 
 // Optional per-launch CUDA-event timing (off by default): prof_begin records a start
 // event on the launching stream, prof_end a stop event tagged with the kernel name.
-void prof_begin(cudaStream_t stream);
+void prof_begin(cudaStream_t stream, const char* name);
 void prof_end(const char* name, cudaStream_t stream);
 void prof_enable(bool on);
+// Time only the launches of this kernel name (NULL or "": every launch).
+void prof_select(const char* name);
 // Aggregate the recorded launches per kernel name (synchronises the events) and clear.
 int prof_collect(char* names, int name_len, float* total_ms, int* counts, int max_kernels);
 

@@ -296,7 +296,7 @@ int launch_delta(const Shape& s, const __half* dO, const __half* O, const float*
                  __half* qaug, cudaStream_t stream) {
     const int T = static_cast<int>(s.tokens());
     const int grid = grid_for(T, 8, 148 * 16);
-    prof_begin(stream);
+    prof_begin(stream, "delta");
     delta_kernel<<<grid, 256, 0, stream>>>(dO, O, lse, qb, L, qaug, T, s.N, npad_of(s.N), s.D, s.H, s.hd);
     MORPHO_LAUNCH_CHECK("delta");
     return MORPHO_OK;
@@ -324,7 +324,7 @@ int launch_dz(const Shape& s, const float* phi, const float* dq, const float* dk
                     : (s.proj == kProjSigmoid      ? dz_kernel<false, kProjSigmoid>
                        : s.proj == kProjHardTanh01 ? dz_kernel<false, kProjHardTanh01>
                                                    : dz_kernel<false, kProjIdentity>);
-    prof_begin(stream);
+    prof_begin(stream, "dz");
     kern<<<gate_blocks, dim3(dz_threads(s), kDzLanes), 0, stream>>>(phi, dq, dk, dcb, dqb, gate_q, gate_k, dcat, gate_part, T, s.N,
                                                     npad_of(s.N), s.H, s.m, s.Hp(), s.Cp(), tpb);
     MORPHO_LAUNCH_CHECK("dz");
@@ -337,7 +337,7 @@ int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, cons
     const long long quads = static_cast<long long>(s.D) * (s.Hm() + s.D) / 4;
     const int main_blocks = grid_for(quads, 256, 148 * 8);
     const int gate_warp_blocks = (2 * s.Hm() + 7) / 8;  // one warp per gate output, 8 warps per block
-    prof_begin(stream);
+    prof_begin(stream, "reduce_weights");
     reduce_weights_kernel<<<main_blocks + gate_warp_blocks, 256, 0, stream>>>(
         dw_part, splits, gate_part, gate_blocks, bucket, dW_phi, dW_V, d_gate_q, d_gate_k, s.D, s.Hm(), s.Hp(),
         s.Cp(), main_blocks);
@@ -348,7 +348,7 @@ int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, cons
 int launch_finalize_weights(const Shape& s, const float* bucket, float alpha, __half* dW_phi, __half* dW_V,
                             __half* d_gate_q, __half* d_gate_k, cudaStream_t stream) {
     const long long total = static_cast<long long>(s.D) * (s.Hm() + s.D) + 2LL * s.Hm();
-    prof_begin(stream);
+    prof_begin(stream, "finalize_weights");
     finalize_kernel<<<grid_for(total, 256, 148 * 8), 256, 0, stream>>>(bucket, alpha, dW_phi, dW_V, d_gate_q,
                                                                        d_gate_k, s.D, s.Hm());
     MORPHO_LAUNCH_CHECK("finalize_weights");

@@ -477,7 +477,7 @@ int run_fwd(const SmArgs& a, int BH, cudaStream_t stream) {
     auto kern = soft_morph_fwd_kernel<MC, HD>;
     const size_t smem = fwd_smem<MC, HD>();
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_fwd");
     kern<<<dim3(a.n_tiles, BH), kThreads, smem, stream>>>(a);
     MORPHO_LAUNCH_CHECK("soft_morph_fwd");
     return MORPHO_OK;
@@ -492,10 +492,10 @@ int run_bwd(const SmArgs& a, int BH, cudaStream_t stream) {
     const size_t sq = bwd_q_smem<MC, HD>(), sk = bwd_k_smem<MC, HD>();
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sq)));
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sk)));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_bwd_q");
     kq<<<dim3(a.n_tiles, BH), kThreads, sq, stream>>>(a);
     MORPHO_LAUNCH_CHECK("soft_morph_bwd_q");
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_bwd_k");
     kk<<<dim3(a.n_tiles, BH), kThreads, sk, stream>>>(a);
     MORPHO_LAUNCH_CHECK("soft_morph_bwd_k");
     return MORPHO_OK;

@@ -487,10 +487,10 @@ int run_tc_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, uint32_
     const float sgn = s.score == kScoreErosion ? -1.0f : 1.0f;
     const float kf = sgn * kLog2e / s.tau;
     MORPHO_CUDA_TRY(cudaMemsetAsync(p.smflag, 0, sizeof(uint32_t), stream));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_ev_partial");
     ev_partial_kernel<HD><<<dim3(BH, nvb), 256, 0, stream>>>(p.v, p.vpart, s.N, sgn);
     MORPHO_LAUNCH_CHECK("soft_morph_ev_partial");
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_ev");
     ev_kernel<HD><<<dim3(BH, Npad / 32), 256, 0, stream>>>(p.v, p.vpart, nvb, p.evt, p.rv, s.N, Npad, kf);
     MORPHO_LAUNCH_CHECK("soft_morph_ev");
     CUtensorMap tQ, tK, tE;
@@ -521,7 +521,7 @@ int run_tc_fwd(const Shape& s, const ProjOut& p, __half* out, float* o2, uint32_
     a.status = status;
     auto kern = sm_tc_fwd_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_fwd");
     kern<<<dim3(a.n_qtiles, BH), kThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tE, a);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_fwd");
     return MORPHO_OK;

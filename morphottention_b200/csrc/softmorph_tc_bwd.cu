@@ -758,16 +758,16 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
     const float sgn = s.score == kScoreErosion ? -1.0f : 1.0f;
     const float kf = sgn * 1.4426950408889634f / s.tau;
     const dim3 pre(BH, Npad / 32);
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_g");
     sm_g_kernel<HD><<<pre, 256, 0, stream>>>(dO, o2, p.mrow, p.rv, x.g, x.gt, N, Npad, s.H, s.D);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_g");
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_ev");
     sm_evn_kernel<HD><<<pre, 256, 0, stream>>>(p.v, p.rv, x.evn, N, Npad, kf);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_ev");
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_kd");
     sm_codes_t_kernel<MC, true><<<pre, 256, 0, stream>>>(p.kdq, x.kdt, N, Npad);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_kd");
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_qc");
     sm_codes_t_kernel<MC, false><<<pre, 256, 0, stream>>>(p.qc, x.qct, N, Npad);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_qc");
     CUtensorMap tQ, tK, tG, tEV, tKD, tGT, tQT;
@@ -793,7 +793,7 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
     qa.status = status;
     auto kq = sm_bwd_q_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<MC, HD>::SMEM_BYTES));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_bwd_q");
     kq<<<dim3(n_tiles, BH), kThreads, QCfg<MC, HD>::SMEM_BYTES, stream>>>(tQ, tK, tG, tEV, tKD, qa);
     MORPHO_LAUNCH_CHECK("soft_morph_tc_bwd_q");
     KArgs ka;
@@ -816,7 +816,7 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
     ka.status = status;
     auto kk = sm_bwd_k_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, KCfg<MC, HD>::SMEM_BYTES));
-    prof_begin(stream);
+    prof_begin(stream, "soft_morph_tc_bwd_k");
     // the key side's ring stages hold KCfg::QS queries (Qc and G boxes of that many rows)
     CUtensorMap tQk, tGk;
     MORPHO_TRY(make_tmap_3d_f16(&tQk, p.qc, MC, N, BH, MC, static_cast<uint64_t>(N) * MC, MC, KCfg<MC, HD>::QS));
