@@ -9,6 +9,12 @@ the ``forward_save`` / ``backward_saved`` op pair, which keeps the forward's pro
 (codes, values, biases, phi) for the backward instead of recomputing it.  Gradients are
 bit-identical either way; the kept buffer costs ``morpho_sm100_saved_bytes`` of memory per
 call until the backward runs.
+
+The variant options (gradient mode, cube projection, diagonal mask, score and tau) are
+process-wide settings, read once when a forward runs: the autograd Function stores them with
+the forward and passes them explicitly to its backward, so a backward that runs after the
+settings changed (outside an :func:`attention_options` block, say) still differentiates the
+forward that ran.
 """
 
 from __future__ import annotations
@@ -39,17 +45,20 @@ def _morpho_backward_fake(grad_out, X, W_phi, gate_q, gate_k, W_V, out, lse, H: 
 
 
 @torch.library.register_fake(add_op_namespace_prefix("forward_save"))
-def _morpho_forward_save_fake(X, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool):
+def _morpho_forward_save_fake(X, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool,
+                              projection: int, mask_diag: int, score: int, tau: float):
     from . import capi
     B, N, D = X.shape
-    nbytes = capi.saved_bytes(capi.problem(B, N, D, H, cube_m, scale, causal))
+    nbytes = capi.saved_bytes(capi.problem(B, N, D, H, cube_m, scale, causal, projection=projection,
+                                           mask_diag=mask_diag, score=score, tau=tau))
     return [torch.empty_like(X), X.new_empty((B * H, N), dtype=torch.float32),
             X.new_empty((nbytes,), dtype=torch.uint8)]
 
 
 @torch.library.register_fake(add_op_namespace_prefix("backward_saved"))
 def _morpho_backward_saved_fake(grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H: int, cube_m: int,
-                                scale: float, causal: bool):
+                                scale: float, causal: bool, grad_mode: int, projection: int, mask_diag: int,
+                                score: int, tau: float):
     return [torch.empty_like(X), torch.empty_like(W_phi), torch.empty_like(gate_q), torch.empty_like(gate_k),
             torch.empty_like(W_V)]
 
@@ -123,6 +132,13 @@ def get_score() -> tuple:
     return {v: k for k, v in SCORES.items()}[int(ops.get_score())], float(ops.get_score_tau())
 
 
+def current_options() -> tuple:
+    """The settings the next forward runs with, as the integer codes of the C ABI:
+    ``(grad_mode, projection, mask_diag, score, tau)``."""
+    g, p, m, sc, tau = ops.get_options()
+    return int(g), int(p), int(m), int(sc), float(tau)
+
+
 @contextlib.contextmanager
 def attention_options(projection: str | None = None, mask_diag: bool | None = None, score: str | None = None,
                       tau: float = 1.0):
@@ -159,7 +175,11 @@ class MorphoAttentionFunction(torch.autograd.Function):
             raise ValueError("MorphoAttention expects a CUDA tensor")
         x = x.contiguous()
         if any(ctx.needs_input_grad[:5]):
-            out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
+            # the variant this forward runs is the one its backward differentiates
+            ctx.options = current_options()
+            _g, proj, mdiag, score, tau = ctx.options
+            out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, proj, mdiag,
+                                               score, tau)
             ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
         else:
             out, lse = ops.forward(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
@@ -174,7 +194,8 @@ class MorphoAttentionFunction(torch.autograd.Function):
         x, W_phi, gate_q, gate_k, W_V, out, lse, saved = ctx.saved_tensors
         grad_out = grad_out.contiguous()
         dX, dW_phi, d_gate_q, d_gate_k, dW_V = ops.backward_saved(
-            grad_out, saved, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal)
+            grad_out, saved, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal,
+            *ctx.options)
         return dX, dW_phi, d_gate_q, d_gate_k, dW_V, None, None, None, None
 
 

@@ -9,9 +9,13 @@
 // set_grad_mode / get_grad_mode select full gradients (default) or the reference
 // kernel's gradient semantics; set_cube_projection / set_mask_diag (and their getters)
 // select the reference's compile-time variants (HardTanh01 / Identity projection, the
-// diagonal mask) for the calls that follow; set_score / get_score / get_score_tau select the
-// soft-morphology aggregation (the reference's unused morfology/soft_morph.cuh); forward_save / backward_saved keep the projection of the
-// forward for the backward instead of recomputing it (the autograd Function uses them).
+// diagonal mask); set_score / get_score / get_score_tau select the soft-morphology
+// aggregation (the reference's unused morfology/soft_morph.cuh); get_options returns all of
+// them at once.  These process-wide settings apply to the reference-schema ops `forward` and
+// `backward` at the moment each is called.  forward_save / backward_saved keep the
+// projection of the forward for the backward instead of recomputing it, and take every
+// option as an explicit argument, so a backward always runs the variant its forward ran
+// (the autograd Functions capture the settings when the forward runs).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -36,7 +40,32 @@ void check(const at::Tensor& t, const char* name) {
     TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
 
-morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double scale, bool causal) {
+// Options of one call: the process-wide settings, or explicit values (forward_save /
+// backward_saved).
+struct Options {
+    int grad_mode, projection, mask_diag, score;
+    float tau;
+};
+
+Options current_options() {
+    return {g_grad_mode.load(), g_projection.load(), g_mask_diag.load(), g_score.load(), g_tau.load()};
+}
+
+Options explicit_options(int64_t grad_mode, int64_t projection, int64_t mask_diag, int64_t score, double tau) {
+    TORCH_CHECK(grad_mode == MORPHO_GRAD_FULL || grad_mode == MORPHO_GRAD_REFERENCE,
+                "grad mode must be 0 (full) or 1 (reference)");
+    TORCH_CHECK(projection == MORPHO_PROJ_SIGMOID || projection == MORPHO_PROJ_HARDTANH01 ||
+                    projection == MORPHO_PROJ_IDENTITY,
+                "cube projection must be 0 (sigmoid), 1 (hardtanh01) or 2 (identity)");
+    TORCH_CHECK(mask_diag == 0 || mask_diag == 1, "mask_diag must be 0 or 1");
+    TORCH_CHECK(score == MORPHO_SCORE_SOFTMAX || score == MORPHO_SCORE_DILATION || score == MORPHO_SCORE_EROSION,
+                "score must be 0 (softmax), 1 (dilation) or 2 (erosion)");
+    return {static_cast<int>(grad_mode), static_cast<int>(projection), static_cast<int>(mask_diag),
+            static_cast<int>(score), static_cast<float>(tau)};
+}
+
+morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double scale, bool causal,
+                         const Options& o) {
     morpho_problem_t p;
     p.B = static_cast<int32_t>(X.size(0));
     p.N = static_cast<int32_t>(X.size(1));
@@ -45,11 +74,11 @@ morpho_problem_t problem(const at::Tensor& X, int64_t H, int64_t cube_m, double 
     p.cube_m = static_cast<int32_t>(cube_m);
     p.scale = static_cast<float>(scale);
     p.causal = causal ? 1 : 0;
-    p.grad_mode = g_grad_mode.load();
-    p.projection = g_projection.load();
-    p.mask_diag = g_mask_diag.load();
-    p.score = g_score.load();
-    p.tau = g_tau.load();
+    p.grad_mode = o.grad_mode;
+    p.projection = o.projection;
+    p.mask_diag = o.mask_diag;
+    p.score = o.score;
+    p.tau = o.tau;
     return p;
 }
 
@@ -67,7 +96,7 @@ void check_shapes(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor
 
 std::vector<at::Tensor> forward_impl(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
                                      const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
-                                     double scale, bool causal, bool save) {
+                                     double scale, bool causal, bool save, const Options& opts) {
     check(X, "X");
     check(W_phi, "W_phi");
     check(gate_q, "gate_q");
@@ -78,7 +107,7 @@ std::vector<at::Tensor> forward_impl(const at::Tensor& X, const at::Tensor& W_ph
     const int64_t B = X.size(0), N = X.size(1);
     auto out = at::empty_like(X);
     auto lse = at::empty({B * H, N}, X.options().dtype(at::kFloat));
-    morpho_problem_t p = problem(X, H, cube_m, scale, causal);
+    morpho_problem_t p = problem(X, H, cube_m, scale, causal, opts);
     const size_t ws_bytes = save ? morpho_sm100_saved_bytes(&p) : morpho_sm100_forward_workspace_size(&p);
     TORCH_CHECK(ws_bytes > 0, "morphottention forward: unsupported problem: ", morpho_sm100_last_error());
     auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
@@ -98,21 +127,23 @@ std::vector<at::Tensor> forward_impl(const at::Tensor& X, const at::Tensor& W_ph
 std::vector<at::Tensor> morpho_forward(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
                                        const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H, int64_t cube_m,
                                        double scale, bool causal) {
-    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, false);
+    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, false, current_options());
 }
 
-// As forward, plus a third output: the uint8 buffer of projection outputs that
-// backward_saved reads.
+// As forward, with the options given explicitly, plus a third output: the uint8 buffer of
+// projection outputs that backward_saved reads.
 std::vector<at::Tensor> morpho_forward_save(const at::Tensor& X, const at::Tensor& W_phi, const at::Tensor& gate_q,
                                             const at::Tensor& gate_k, const at::Tensor& W_V, int64_t H,
-                                            int64_t cube_m, double scale, bool causal) {
-    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, true);
+                                            int64_t cube_m, double scale, bool causal, int64_t projection,
+                                            int64_t mask_diag, int64_t score, double tau) {
+    return forward_impl(X, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, true,
+                        explicit_options(MORPHO_GRAD_FULL, projection, mask_diag, score, tau));
 }
 
 std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tensor* saved, const at::Tensor& X,
                                       const at::Tensor& W_phi, const at::Tensor& gate_q, const at::Tensor& gate_k,
                                       const at::Tensor& W_V, const at::Tensor& out, const at::Tensor& lse, int64_t H,
-                                      int64_t cube_m, double scale, bool causal) {
+                                      int64_t cube_m, double scale, bool causal, const Options& opts) {
     TORCH_CHECK(grad_out.is_cuda() && X.is_cuda(), "Gradient output and X must be a CUDA tensors");
     check(grad_out, "grad_out");
     check(X, "X");
@@ -137,7 +168,7 @@ std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tens
     auto d_gate_q = at::empty_like(gate_q);
     auto d_gate_k = at::empty_like(gate_k);
     auto dW_V = at::empty_like(W_V);
-    morpho_problem_t p = problem(X, H, cube_m, scale, causal);
+    morpho_problem_t p = problem(X, H, cube_m, scale, causal, opts);
     if (saved != nullptr) {
         TORCH_CHECK(saved->is_cuda() && saved->scalar_type() == at::kByte && saved->is_contiguous(),
                     "saved must be the contiguous uint8 CUDA tensor forward_save returned");
@@ -169,15 +200,18 @@ std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Te
                                         const at::Tensor& gate_q, const at::Tensor& gate_k, const at::Tensor& W_V,
                                         const at::Tensor& out, const at::Tensor& lse, int64_t H, int64_t cube_m,
                                         double scale, bool causal) {
-    return backward_impl(grad_out, nullptr, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal);
+    return backward_impl(grad_out, nullptr, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal,
+                         current_options());
 }
 
 std::vector<at::Tensor> morpho_backward_saved(const at::Tensor& grad_out, const at::Tensor& saved, const at::Tensor& X,
                                               const at::Tensor& W_phi, const at::Tensor& gate_q,
                                               const at::Tensor& gate_k, const at::Tensor& W_V, const at::Tensor& out,
                                               const at::Tensor& lse, int64_t H, int64_t cube_m, double scale,
-                                              bool causal) {
-    return backward_impl(grad_out, &saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal);
+                                              bool causal, int64_t grad_mode, int64_t projection, int64_t mask_diag,
+                                              int64_t score, double tau) {
+    return backward_impl(grad_out, &saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal,
+                         explicit_options(grad_mode, projection, mask_diag, score, tau));
 }
 
 int64_t set_grad_mode(int64_t mode) {
@@ -214,6 +248,13 @@ int64_t get_score() { return g_score.load(); }
 
 double get_score_tau() { return static_cast<double>(g_tau.load()); }
 
+// [grad_mode, projection, mask_diag, score, tau]: the settings the next forward would run with.
+std::vector<double> get_options() {
+    const Options o = current_options();
+    return {static_cast<double>(o.grad_mode), static_cast<double>(o.projection), static_cast<double>(o.mask_diag),
+            static_cast<double>(o.score), static_cast<double>(o.tau)};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(morphottention, m) {
@@ -225,10 +266,12 @@ TORCH_LIBRARY(morphottention, m) {
         "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
     m.def(
         "forward_save(Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, Tensor W_V, "
-        "int H, int cube_m, float scale, bool causal) -> Tensor[]");
+        "int H, int cube_m, float scale, bool causal, int projection, int mask_diag, int score, "
+        "float tau) -> Tensor[]");
     m.def(
         "backward_saved(Tensor grad_out, Tensor saved, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
-        "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal) -> Tensor[]");
+        "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal, int grad_mode, "
+        "int projection, int mask_diag, int score, float tau) -> Tensor[]");
     m.def("set_grad_mode(int mode) -> int", &set_grad_mode);
     m.def("get_grad_mode() -> int", &get_grad_mode);
     m.def("set_cube_projection(int proj) -> int", &set_cube_projection);
@@ -238,6 +281,7 @@ TORCH_LIBRARY(morphottention, m) {
     m.def("set_score(int score, float tau) -> int", &set_score);
     m.def("get_score() -> int", &get_score);
     m.def("get_score_tau() -> float", &get_score_tau);
+    m.def("get_options() -> float[]", &get_options);
 }
 
 TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {

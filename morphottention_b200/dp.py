@@ -86,26 +86,25 @@ class _DataParallelFunction(torch.autograd.Function):
         if not x.is_cuda:
             raise ValueError("MorphoAttention expects a CUDA tensor")
         x = x.contiguous()
-        from .autograd import CUBE_PROJECTIONS, SCORES, get_cube_projection, get_mask_diag, get_score
-        out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal)
+        from .autograd import current_options
+        # every option (the gradient mode included) as this forward ran, for its backward
+        ctx.options = current_options()
+        _g, proj, mdiag, score, tau = ctx.options
+        out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, proj, mdiag,
+                                           score, tau)
         ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
         ctx.H, ctx.cube_m, ctx.scale, ctx.causal, ctx.group = H, cube_m, scale, causal, group
-        # the options the forward ran with, for the backward's problem
-        ctx.projection = CUBE_PROJECTIONS[get_cube_projection()]
-        ctx.mask_diag = get_mask_diag()
-        name, tau = get_score()
-        ctx.score, ctx.tau = SCORES[name], tau
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
         from . import capi
-        from .autograd import GRAD_MODES, get_grad_mode
         x, W_phi, gate_q, gate_k, W_V, out, lse, saved = ctx.saved_tensors
         grad_out = grad_out.contiguous()
         B, N, D = x.shape
-        p = capi.problem(B, N, D, ctx.H, ctx.cube_m, ctx.scale, ctx.causal, grad_mode=GRAD_MODES[get_grad_mode()],
-                         projection=ctx.projection, mask_diag=ctx.mask_diag, score=ctx.score, tau=ctx.tau)
+        gmode, proj, mdiag, score, tau = ctx.options
+        p = capi.problem(B, N, D, ctx.H, ctx.cube_m, ctx.scale, ctx.causal, grad_mode=gmode, projection=proj,
+                         mask_diag=mdiag, score=score, tau=tau)
         dX = torch.empty_like(x)
         grads = [torch.empty_like(t) for t in (W_phi, gate_q, gate_k, W_V)]
         bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=x.device)

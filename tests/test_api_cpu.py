@@ -69,6 +69,33 @@ def test_fake_kernels():
         assert [t.shape for t in grads] == [x.shape, wp.shape, g.shape, g.shape, wv.shape]
 
 
+def test_training_pair_takes_options_explicitly():
+    """forward_save / backward_saved carry every variant option as an argument (the autograd
+    Function passes the settings captured when its forward ran), and get_options reports the
+    process-wide settings in the C ABI's codes."""
+    fs = str(torch.ops.morphottention.forward_save.default._schema)
+    bs = str(torch.ops.morphottention.backward_saved.default._schema)
+    assert fs.endswith("bool causal, int projection, int mask_diag, int score, float tau) -> Tensor[]")
+    assert bs.endswith("bool causal, int grad_mode, int projection, int mask_diag, int score, float tau) -> Tensor[]")
+    from morphottention_b200.autograd import current_options
+    assert current_options() == (0, 0, 0, 0, 1.0)
+    with M.attention_options(projection="identity", mask_diag=True, score="erosion", tau=0.25):
+        with M.grad_mode("reference"):
+            assert current_options() == (1, 2, 1, 2, 0.25)
+    assert current_options() == (0, 0, 0, 0, 1.0)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty(2, 5, 64, dtype=torch.float16, device="cuda")
+        wp = torch.empty(64, 32, dtype=torch.float16, device="cuda")
+        g = torch.empty(2, 16, dtype=torch.float16, device="cuda")
+        wv = torch.empty(64, 64, dtype=torch.float16, device="cuda")
+        out, lse, saved = torch.ops.morphottention.forward_save(x, wp, g, g, wv, 2, 16, 1.0, False, 1, 1, 1, 0.5)
+        assert saved.dtype == torch.uint8 and saved.dim() == 1
+        grads = torch.ops.morphottention.backward_saved(out, saved, x, wp, g, g, wv, out, lse, 2, 16, 1.0, False,
+                                                        0, 1, 1, 1, 0.5)
+        assert [t.shape for t in grads] == [x.shape, wp.shape, g.shape, g.shape, wv.shape]
+
+
 def test_grad_mode_switch():
     assert M.get_grad_mode() == "full"
     with M.grad_mode("reference"):

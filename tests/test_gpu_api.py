@@ -186,10 +186,11 @@ def test_saved_pair_matches_recompute(cuda, cfg):
     a, b = run(False), run(True)
     for name, u, v in zip(("out", "lse", "dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), a, b):
         assert torch.equal(u, v), name
-    o, l, s = torch.ops.morphottention.forward_save(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    opts = (0, 0, 0, 1.0)  # projection sigmoid, no diagonal mask, softmax score, tau
+    o, l, s = torch.ops.morphottention.forward_save(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, *opts)
     assert torch.equal(o, a[0]) and s.dtype == torch.uint8
     g = torch.ops.morphottention.backward_saved(inp["grad_out"], s, *args, o, l, cfg.H, cfg.cube_m, cfg.scale,
-                                                cfg.causal)
+                                                cfg.causal, 0, *opts)
     for name, u, v in zip(("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V"), a[2:], g):
         assert torch.equal(u, v), name
 

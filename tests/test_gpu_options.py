@@ -95,3 +95,83 @@ def test_invalid_options_are_rejected(cuda):
     with pytest.raises(capi.MorphoError, match="projection"):
         capi.forward(p, x, w, gq, gq, torch.zeros(128, 128, dtype=torch.float16, device=cuda), torch.empty_like(x),
                      torch.empty(2, 128, device=cuda))
+
+
+def _module_with(cfg, inp, cuda):
+    mod = M.MorphoAttention(cfg.D, cfg.H, cfg.cube_m, scale=cfg.scale, causal=cfg.causal, device=cuda)
+    with torch.no_grad():
+        for n in ("W_phi", "W_V", "gate_q", "gate_k"):
+            getattr(mod, n).copy_(inp[n])
+    return mod
+
+
+@pytest.mark.parametrize("opts", [{"score": "dilation", "tau": 0.9}, {"projection": "hardtanh01"},
+                                  {"mask_diag": True}], ids=["dilation", "hardtanh01", "mask_diag"])
+def test_backward_outside_the_options_block(cuda, opts):
+    """The loss is built inside attention_options() and differentiated after the block has
+    restored the defaults: the backward must differentiate the variant the forward ran (the
+    autograd Function captured the options with the forward), matching the oracle's gradients
+    of that variant."""
+    cfg = MorphoConfig("late_bwd", 2, 150, 128, 4, 16, 0.7, True, 36)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    mod = _module_with(cfg, inp, cuda)
+    x = inp["x"].clone().requires_grad_(True)
+    with M.attention_options(**opts):
+        out = mod(x)
+        loss = (out.float() * g.float()).sum()
+    assert M.get_score()[0] == "softmax" and M.get_cube_projection() == "sigmoid" and not M.get_mask_diag()
+    loss.backward()
+    t = {k: v.cpu() for k, v in inp.items()}
+    if "score" in opts:
+        ref = O.soft_morph_forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H,
+                                            cfg.cube_m, cfg.scale, cfg.causal, opts["score"], opts["tau"],
+                                            grad_out=g.cpu())
+    else:
+        ref = run_oracle(cfg, t, grad_out=g.cpu(), projection=opts.get("projection", "sigmoid"),
+                         mask_diag=opts.get("mask_diag", False))
+    ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
+            "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
+    if opts.get("mask_diag"):  # causal + diagonal mask: query 0 has no key (out 0, no gradient there)
+        assert torch.all(out[:, 0] == 0)
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+def test_two_modules_with_different_options_in_one_graph(cuda):
+    """A sigmoid-projection layer feeding a HardTanh01 + diagonal-mask layer, one backward over
+    both after the options block has closed: each layer's gradients are those of its own
+    variant (checked against each layer run alone under its own options)."""
+    cfg = MorphoConfig("two_mods", 1, 128, 128, 2, 16, 0.8, False, 37)
+    inp = inputs(cfg, cuda, random_gates=True)
+    a = _module_with(cfg, inp, cuda)
+    b = _module_with(cfg, inp, cuda)
+    x = inp["x"].clone().requires_grad_(True)
+    h = a(x)
+    with M.attention_options(projection="hardtanh01", mask_diag=True):
+        y = b(h)
+    y.float().sum().backward()
+    grads = {n: getattr(b, n).grad.clone() for n in ("W_phi", "W_V", "gate_q", "gate_k")}
+    # the second layer alone on the same input, differentiated inside its block
+    b.zero_grad(set_to_none=True)
+    h2 = h.detach().clone().requires_grad_(True)
+    with M.attention_options(projection="hardtanh01", mask_diag=True):
+        b(h2).float().sum().backward()
+    for n, gr in grads.items():
+        assert torch.equal(gr, getattr(b, n).grad), n
+
+
+def test_grad_mode_is_bound_to_the_forward(cuda):
+    """grad_mode("reference") around the forward only: the backward still uses the reference
+    semantics (the query path dropped), matching the oracle's reference mode."""
+    cfg = MorphoConfig("late_mode", 2, 130, 128, 2, 16, 1.0, False, 38)
+    inp = inputs(cfg, cuda, random_gates=True)
+    mod = _module_with(cfg, inp, cuda)
+    x = inp["x"].clone().requires_grad_(True)
+    with M.grad_mode("reference"):
+        out = mod(x)
+    assert M.get_grad_mode() == "full"
+    out.float().sum().backward()
+    ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_mode="reference")
+    ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
+            "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
