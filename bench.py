@@ -30,6 +30,25 @@ METRIC = "fused fwd+bwd tokens/sec per B200 and whole-box at 1/2/4/8 GPUs; % of 
 UNIT = "tokens/s"
 
 
+def _load_source(name, relpath):
+    """Import one source file by path, outside its package.  The reference arm and the CPU
+    baseline need the workload configurations (and the encoder's layout) but must not run
+    ``morphottention_b200/__init__.py``, which loads this repository's CUDA libraries."""
+    import importlib.util
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, relpath))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod  # dataclasses look their module up while the class is built
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _configs():
+    """``morphottention_b200/configs.py`` (configurations, seeded inputs), loaded by path."""
+    return _load_source("_morpho_bench_configs", os.path.join("morphottention_b200", "configs.py"))
+
+
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -102,11 +121,11 @@ def cpu_baseline(cfg, seconds: float = 12.0, max_reps: int = 5):
     """Time the fp32 CPU oracle (a restatement of the reference path) on one sequence of
     the workload: forward + backward of out.sum(), all host threads."""
     import torch
-    from morphottention_b200.configs import make_inputs
+
     from oracle import morpho_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     one = cfg.with_(B=1)
-    inp = make_inputs(one)
+    inp = _configs().make_inputs(one)
     times = []
     t_start = time.perf_counter()
     while len(times) < max_reps and (time.perf_counter() - t_start) < seconds or len(times) < 2:
@@ -124,15 +143,16 @@ def cpu_baseline(cfg, seconds: float = 12.0, max_reps: int = 5):
 def run_reference(args):
     """--impl reference: the CPU formulation of the reference path on the host cores."""
     import torch
-    from morphottention_b200.configs import CONFIGS, make_inputs
+
     from oracle import morpho_oracle as O
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cfg = CONFIGS[args.config]
+    C = _configs()
+    cfg = C.CONFIGS[args.config]
     one = cfg.with_(B=1)
     torch.set_num_threads(os.cpu_count() or 1)
-    inp = make_inputs(one)
+    inp = C.make_inputs(one)
 
     def step():
         O.forward_backward(inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], one.H, one.cube_m,
@@ -179,8 +199,7 @@ def _traffic(kernel, config_name, cfg):
             t = json.load(f).get(kernel)
         if t is None or t.get("config") != config_name:
             return None
-        from morphottention_b200.configs import CONFIGS
-        return t["dram_bytes_per_launch"] * cfg.B / CONFIGS[config_name].B
+        return t["dram_bytes_per_launch"] * cfg.B / _configs().CONFIGS[config_name].B
     except Exception:
         return None
 
@@ -195,6 +214,172 @@ def algorithmic_flops(cfg):
             # soft-morphology split path: S (f16) + E_S.E_V / G.E_V^T, dS.kd / E_S^T.G, dS^T.qc (tf32)
             "soft_morph_tc_fwd": 2.0 * nn * (m + hd), "soft_morph_tc_bwd_q": 2.0 * nn * (2 * m + hd),
             "soft_morph_tc_bwd_k": 2.0 * nn * (2 * m + 2 * hd)}
+
+
+def reference_kernel_leg(dev):
+    """The reference's own CUDA kernel (its ``attention.cu`` compiled unmodified for sm_100a by
+    ``oracle/build_ref.py`` into ``oracle/_ref``) timed beside this library on the same GPU, a
+    comparator of the baseline leg: the c3 forward (its backward cannot launch at c3: it asks
+    for 1,005,056 B of shared memory, 232,448 B are allowed) and forward + backward at
+    c3-narrow (B=4, N=4096, D=128, H=2, m=32, scale 0.5), where its backward launches.  CUDA
+    events on the current stream after one warm-up call; this library's side in the
+    reference's gradient semantics (equal work) and with full gradients."""
+    import torch
+
+    from morphottention_b200 import capi
+    from oracle import refkernel
+    C = _configs()
+
+    def time_ms(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    res = {"source": "reference attention.cu built unmodified (oracle/build_ref.py), CUDA events, same GPU"}
+    fwd_cfg = C.CONFIGS["c3"]
+    narrow = fwd_cfg.with_(name="c3_narrow", D=128, H=2)
+    for cfg in (fwd_cfg, narrow):
+        if not refkernel.available(cfg.cube_m, cfg.head_dim, cfg.causal):
+            return {"unavailable": "reference kernel not built in oracle/_ref (oracle/build_ref.py)"}
+    # c3 forward
+    inp = C.make_inputs(fwd_cfg, device=dev)
+    args5 = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    p = capi.problem(fwd_cfg.B, fwd_cfg.N, fwd_cfg.D, fwd_cfg.H, fwd_cfg.cube_m, fwd_cfg.scale, fwd_cfg.causal)
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty(fwd_cfg.B * fwd_cfg.H, fwd_cfg.N, dtype=torch.float32, device=dev)
+    r_ms = time_ms(lambda: refkernel.forward(fwd_cfg, inp), 2)
+    o_ms = time_ms(lambda: capi.forward(p, *args5, out, lse), 10)
+    res["c3_forward"] = {"reference_ms": r_ms, "ours_ms": o_ms, "reference_tokens_per_s": fwd_cfg.tokens / r_ms * 1e3,
+                         "ours_tokens_per_s": fwd_cfg.tokens / o_ms * 1e3, "speedup": r_ms / o_ms,
+                         "ours_api": "morpho_sm100_forward (projection + attention forward)"}
+    res["c3_backward"] = "reference cannot launch: 1,005,056 B dynamic shared memory > 232,448 B"
+    del inp, args5, out, lse
+    # c3-narrow forward + backward
+    inp = C.make_inputs(narrow, device=dev)
+    args5 = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    g = torch.ones_like(inp["x"])
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty(narrow.B * narrow.H, narrow.N, dtype=torch.float32, device=dev)
+    grads = [torch.empty_like(t) for t in args5]
+
+    def ours(mode):
+        q = capi.problem(narrow.B, narrow.N, narrow.D, narrow.H, narrow.cube_m, narrow.scale, narrow.causal, mode)
+        saved = torch.empty(capi.saved_bytes(q), dtype=torch.uint8, device=dev)
+
+        def run():
+            capi.forward_save(q, *args5, out, lse, saved=saved)
+            capi.backward_saved(q, g, saved, *args5, out, lse, *grads)
+        return run
+
+    def ref():
+        o, l_ = refkernel.forward(narrow, inp)
+        refkernel.backward(narrow, inp, o, l_, g)
+
+    r_ms = time_ms(ref, 2)
+    o_ms = time_ms(ours(capi.MORPHO_GRAD_REFERENCE), 10)
+    f_ms = time_ms(ours(capi.MORPHO_GRAD_FULL), 10)
+    res["c3_narrow_fwd_bwd"] = {"shape": "B=4, N=4096, D=128, H=2, cube_m=32, scale 0.5", "reference_ms": r_ms,
+                                "ours_ms": o_ms, "ours_full_gradient_ms": f_ms,
+                                "reference_tokens_per_s": narrow.tokens / r_ms * 1e3,
+                                "ours_tokens_per_s": narrow.tokens / o_ms * 1e3, "speedup": r_ms / o_ms,
+                                "ours_api": "forward_save + backward_saved, grad_mode reference (the reference "
+                                            "kernel's semantics); full-gradient time beside it"}
+    return res
+
+
+def dp_leg(args, world, rank, dev, barrier):
+    """The data-parallel configuration c5 (per rank B=8, N=8192, D=2048, H=16, cube_m=64,
+    causal, scale 1.0; global batch 8 x ranks, weak scaling): the training pair on each rank's
+    own batch shard, the fp32 weight-gradient bucket all-reduced with NCCL on a communication
+    stream overlapped with the dX GEMM, timed on the device as the max over ranks, with the
+    all-reduce's own duration per rank (CUDA events on the communication stream).  Then, once,
+    the collective is checked: every rank's unreduced bucket is all-gathered and their fp64 sum
+    compared with the all-reduced bucket."""
+    import torch
+    import torch.distributed as dist
+
+    from morphottention_b200 import capi, dp
+    from morphottention_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS["c5"]
+    # weights from the configuration's seed (drawn before x, so independent of B and N);
+    # each rank's shard of x from its own seeded device generator
+    w = {k: v.to(dev) for k, v in make_inputs(cfg.with_(B=1, N=1), device="cpu").items() if k != "x"}
+    gen = torch.Generator(device=dev).manual_seed(cfg.seed * 1000 + rank)
+    x = torch.randn(cfg.B, cfg.N, cfg.D, generator=gen, device=dev, dtype=torch.float32).half()
+    args5 = [x, w["W_phi"], w["gate_q"], w["gate_k"], w["W_V"]]
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    grad = torch.ones_like(x)
+    out, dX = torch.empty_like(x), torch.empty_like(x)
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
+    grads = [torch.empty_like(t) for t in args5[1:]]  # W_phi, gate_q, gate_k, W_V
+    saved = torch.empty(capi.saved_bytes(p), dtype=torch.uint8, device=dev)
+    bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev)
+    timing = []
+
+    def step(rec=None):
+        capi.forward_save(p, *args5, out, lse, saved=saved)
+        if world > 1:
+            dp.backward_allreduce(p, grad, saved, *args5, out, lse, dX, grads[0], grads[1], grads[2], grads[3],
+                                  bucket, timing=rec)
+        else:
+            capi.backward_saved(p, grad, saved, *args5, out, lse, dX, grads[0], grads[1], grads[2], grads[3])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    steps = args.steps
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step(timing)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    ar_ms = (sum(a.elapsed_time(b) for a, b in timing) / len(timing)) if timing else 0.0
+    per_rank = torch.tensor([ms.item() / steps, ar_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        gathered = [torch.empty_like(per_rank) for _ in range(world)]
+        dist.all_gather(gathered, per_rank)
+    else:
+        gathered = [per_rank]
+    ms_step = float(ms.item()) / steps
+    check = None
+    if world > 1:
+        step()  # bucket = the sum over ranks
+        local = torch.empty_like(bucket)
+        capi.forward_save(p, *args5, out, lse, saved=saved)
+        capi.backward_saved(p, grad, saved, *args5, out, lse, dX, None, None, None, None, dweights_f32=local)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local)
+        want = torch.stack(parts).double().sum(0)
+        check = {"rel_l2": float((bucket.double() - want).norm() / want.norm()),
+                 "what": "all-reduced fp32 bucket vs the fp64 sum of every rank's unreduced bucket (all-gathered)",
+                 "bucket_elems": bucket.numel()}
+        del parts, want, local
+    peaks = _peaks()
+    tokens = cfg.tokens * world
+    res = {"workload": "c5_dp: causal MorphoAttention layer, per rank B=8, N=8192, D=2048, H=16, cube_m=64, "
+                       "scale 1.0; fwd + backward(out.sum()), weight-gradient bucket all-reduced (NCCL)",
+           "B_per_gpu": cfg.B, "global_batch": cfg.B * world, "n_gpus": world, "steps": steps,
+           "ms_per_step": ms_step, "value": tokens / (ms_step / 1000.0), "unit": UNIT, "scaling": "weak",
+           "timing": "CUDA events around the steps on each rank, max over ranks",
+           "step_roofline_frac": cfg.tensor_flops_fwd_bwd() / (peaks["bf16_tflops_sustained"] * 1e12)
+           / (ms_step / 1000.0),
+           "per_rank_ms_per_step": [float(t[0]) for t in gathered],
+           "allreduce_ms_per_rank": [float(t[1]) for t in gathered] if world > 1 else None,
+           "allreduce_bytes": bucket.numel() * 4 if world > 1 else 0, "dp_check": check}
+    del x, out, dX, grad, saved, bucket, grads, args5
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_ours(args):
@@ -380,6 +565,11 @@ def run_ours(args):
                "loss_read": "step k's loss copied back asynchronously, read on the host during step k+1",
                "value_serial_copy": serial}
 
+    # the data-parallel configuration on every rank (the collective steps are the same on all)
+    dp_res = None
+    if not args.no_dp_leg and args.config != "c5" and args.score == "softmax" and args.batch is None:
+        dp_res = dp_leg(args, world, rank, dev, barrier)
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -421,9 +611,13 @@ def run_ours(args):
             "tensor_tflops_step": cfg.tensor_flops_fwd_bwd() / (ms / args.steps / 1000.0) / 1e12,
             "step_roofline_frac": (cfg.tensor_flops_fwd_bwd() / (peaks["bf16_tflops_sustained"] * 1e12))
             / (ms / args.steps / 1000.0),
-            "device_status": status}
+            "device_status": status, "dp_config": dp_res}
+    # baseline legs (rank 0 at N = 1): the fp32 CPU oracle on the host cores, and the
+    # reference's own CUDA kernel on this GPU
     if world == 1 and not args.no_cpu_baseline and args.score == "softmax":
         line["cpu_baseline"] = cpu_baseline(cfg)
+        if args.config == "c3" and args.batch is None and not args.no_reference_kernel:
+            line["reference_kernel"] = reference_kernel_leg(dev)
     elif args.score != "softmax":  # the fp32 oracle materialises [B, H, N, N, hd]: not at these sizes
         line["cpu_baseline"] = None
     print(json.dumps(line), flush=True)
@@ -443,28 +637,38 @@ def _vit_flops(cfg):
     return VIT_DEPTH * (cfg.tensor_flops_fwd_bwd() + mlp)
 
 
-class _OracleAttention:
-    """CPU attention for the reference arm of the encoder workload (the oracle, fp32)."""
+def _oracle_attention(dim, num_heads, cube_m, scale=1.0, causal=False, dtype=None, device=None):
+    """CPU attention layer for the reference arm of the encoder workload: the module's
+    parameters with its default initialisation, and the fp32 oracle as the forward (autograd
+    through the oracle's torch ops)."""
+    import torch
 
-    def __init__(self, mod):
-        self.mod = mod
+    from oracle import morpho_oracle as O
 
-    def __call__(self, x):
-        from oracle import morpho_oracle as O
-        m = self.mod
-        return O.forward(x, m.W_phi, m.gate_q, m.gate_k, m.W_V, m.num_heads, m.cube_m, m.scale, m.causal)[0]
+    class OracleAttention(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            f32 = dict(dtype=torch.float32, device=device)
+            std = dim ** -0.5
+            self.W_phi = torch.nn.Parameter(torch.empty(dim, num_heads * cube_m, **f32).normal_(0.0, std))
+            self.W_V = torch.nn.Parameter(torch.empty(dim, dim, **f32).normal_(0.0, std))
+            self.gate_q = torch.nn.Parameter(torch.ones(num_heads, cube_m, **f32))
+            self.gate_k = torch.nn.Parameter(torch.ones(num_heads, cube_m, **f32))
+
+        def forward(self, x):
+            return O.forward(x, self.W_phi, self.gate_q, self.gate_k, self.W_V, num_heads, cube_m, scale, causal)[0]
+
+    return OracleAttention()
 
 
 def _vit_cpu_step_seconds(cfg, steps=2, warmup=1):
     """fp32 CPU encoder (oracle attention) on one sequence: seconds per training step."""
     import torch
-    from morphottention_b200.encoder import Encoder
+    Encoder = _load_source("_morpho_bench_encoder", os.path.join("morphottention_b200", "encoder.py")).Encoder
     torch.set_num_threads(os.cpu_count() or 1)
     torch.manual_seed(cfg.seed)
     model = Encoder(depth=VIT_DEPTH, dim=cfg.D, num_heads=cfg.H, cube_m=cfg.cube_m, mlp_ratio=VIT_MLP_RATIO,
-                    scale=cfg.scale, dtype=torch.float32, device="cpu")
-    for blk in model.blocks:
-        blk.attn.forward = _OracleAttention(blk.attn)
+                    scale=cfg.scale, dtype=torch.float32, device="cpu", attention=_oracle_attention)
     g = torch.Generator().manual_seed(cfg.seed)
     x = torch.randn(1, cfg.N, cfg.D, generator=g)
     target = torch.randn(1, cfg.N, cfg.D, generator=g)
@@ -665,8 +869,7 @@ def run_vit_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from morphottention_b200.configs import CONFIGS
-    cfg = CONFIGS["c4"]
+    cfg = _configs().CONFIGS["c4"]
     sec, cores = _vit_cpu_step_seconds(cfg, steps=args.steps, warmup=args.warmup)
     value = cfg.N / sec
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
@@ -689,6 +892,10 @@ def main():
                     help="c1..c5: one MorphoAttention layer; c4vit: the 12-block ViT-B encoder training step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-dp-leg", action="store_true",
+                    help="skip the data-parallel configuration c5 timed after the main workload")
+    ap.add_argument("--no-reference-kernel", action="store_true",
+                    help="skip timing the reference's own CUDA kernel beside ours (N = 1, c3)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (small cases for profiler captures)")
     ap.add_argument("--score", choices=["softmax", "dilation", "erosion"], default="softmax",

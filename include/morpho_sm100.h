@@ -144,8 +144,12 @@ MORPHO_API int morpho_sm100_backward_saved_dp(const morpho_problem_t* p, const v
  * morpho_sm100_forward_noalloc_max_scratch(), 32 MiB), held by every GPU that loads the
  * library until exit.  Problems whose forward workspace exceeds it are rejected with
  * MORPHO_ERR_WORKSPACE.  The first call on each device looks the array's address up
- * (cudaGetSymbolAddress); make it outside any stream capture.  All calls share the array:
- * calls that overlap on the GPU race; calls ordered on one stream are safe. */
+ * (cudaGetSymbolAddress); under CUDA's default lazy module loading that first call also
+ * places the array and the forward's kernels on the device, so it reserves device memory:
+ * make it at start-up, before the code that must not allocate, and outside any stream
+ * capture.  Later calls reserve nothing.  Not usable again after cudaDeviceReset in the
+ * same process.  All calls share the array: calls that overlap on the GPU race; calls
+ * ordered on one stream are safe. */
 MORPHO_API int morpho_sm100_forward_noalloc(const morpho_problem_t* p, const void* X, const void* W_phi,
                                             const void* gate_q, const void* gate_k, const void* W_V, void* out,
                                             float* lse, void* stream);

@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -48,7 +49,11 @@ struct ProfRec {
     const char* name;
     cudaEvent_t start, stop;
 };
-bool g_prof_on = false;
+// The switch and the selection are process-wide and may be changed from any host thread
+// while others launch: the switch is atomic, the selected name is guarded by a mutex (taken
+// only while timing is on).  The records themselves are per host thread.
+std::atomic<bool> g_prof_on{false};
+std::mutex g_prof_mu;
 std::string g_prof_only;  // empty: every launch is timed
 thread_local std::vector<ProfRec> t_prof;
 thread_local std::vector<cudaEvent_t> t_event_pool;
@@ -66,13 +71,21 @@ cudaEvent_t take_event() {
 }
 }  // namespace
 
-void prof_enable(bool on) { g_prof_on = on; }
+void prof_enable(bool on) { g_prof_on.store(on); }
 
-void prof_select(const char* name) { g_prof_only = name ? name : ""; }
+void prof_select(const char* name) {
+    std::lock_guard<std::mutex> lock(g_prof_mu);
+    g_prof_only = name ? name : "";
+}
 
 void prof_begin(cudaStream_t stream, const char* name) {
-    if (!g_prof_on) return;
-    if (!g_prof_only.empty() && (name == nullptr || g_prof_only != name)) {
+    if (!g_prof_on.load(std::memory_order_relaxed)) return;
+    bool selected = true;
+    {
+        std::lock_guard<std::mutex> lock(g_prof_mu);
+        selected = g_prof_only.empty() || (name != nullptr && g_prof_only == name);
+    }
+    if (!selected) {
         t_pending = nullptr;  // not selected: no events, prof_end records nothing
         return;
     }
@@ -81,7 +94,7 @@ void prof_begin(cudaStream_t stream, const char* name) {
 }
 
 void prof_end(const char* name, cudaStream_t stream) {
-    if (!g_prof_on || t_pending == nullptr) return;
+    if (!g_prof_on.load(std::memory_order_relaxed) || t_pending == nullptr) return;
     cudaEvent_t stop = take_event();
     if (stop == nullptr) return;
     cudaEventRecord(stop, stream);

@@ -9,13 +9,19 @@
 // and outputs.
 //
 // The scratch array (kNoAllocScratchBytes, 32 MiB) is a file-scope __device__ object: every
-// GPU that loads this library holds it until the process exits.  Its device address is
-// looked up once per device with cudaGetSymbolAddress, the first time this entry point
-// runs on that device (with that device current); make that first call outside any
-// CUDA stream capture.  All calls share the one array, so two calls whose work overlaps
-// on the GPU (different streams, or different host threads without ordering) race on it;
-// calls issued in order on one stream are safe.  The forward overwrites every scratch
-// byte it later reads, so nothing needs clearing between calls.
+// GPU that loads it holds it until the process exits.  Its device address is looked up once
+// per device with cudaGetSymbolAddress, the first time this entry point runs on that device
+// (with that device current).  Under CUDA's lazy module loading (the default since CUDA
+// 12.2; CUDA_MODULE_LOADING=EAGER turns it off) that first call is also the moment the
+// array and the forward's kernel modules are placed on the device, so it does reserve
+// device memory: make it at start-up, before the code that must not allocate runs, and
+// outside any CUDA stream capture.  Later calls reserve nothing.  The cached address
+// belongs to the device's current context; after cudaDeviceReset this entry point must
+// not be called again in the same process.  All calls share the one array, so two calls
+// whose work overlaps on the GPU (different streams, or different host threads without
+// ordering) race on it; calls issued in order on one stream are safe.  The forward
+// overwrites every scratch byte it later reads (the soft-morphology range flag is cleared
+// by the forward itself), so nothing needs clearing between calls.
 #include <mutex>
 
 #include "host_common.h"
@@ -34,17 +40,21 @@ std::mutex g_scratch_mu;
 int scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // do not leave the failure for the next launch check to report
         return morpho::set_error(MORPHO_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    }
     if (dev < 0 || dev >= kMaxDevices)
         return morpho::set_error(MORPHO_ERR_DEVICE, "device ordinal %d out of range", dev);
     std::lock_guard<std::mutex> lock(g_scratch_mu);
     if (g_scratch_ptr[dev] == nullptr) {
         void* ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess || ptr == nullptr)
+        if (e != cudaSuccess || ptr == nullptr) {
+            cudaGetLastError();  // as above: the error is returned here, not left pending
             return morpho::set_error(MORPHO_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed: %s",
                                      cudaGetErrorString(e));
+        }
         g_scratch_ptr[dev] = ptr;
     }
     *out = g_scratch_ptr[dev];

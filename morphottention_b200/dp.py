@@ -56,12 +56,14 @@ def _comm_stream(device) -> torch.cuda.Stream:
 
 
 def backward_allreduce(p, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, dX, dW_phi, d_gate_q, d_gate_k,
-                       dW_V, bucket, group=None, average: bool = True) -> None:
+                       dW_V, bucket, group=None, average: bool = True, timing: list | None = None) -> None:
     """``capi.backward_saved`` for a data-parallel rank, with the weight-gradient all-reduce
     overlapped with the dX GEMM: the library fills the fp32 ``bucket`` first and records an
     event; a communication stream waits for it and all-reduces the bucket while dX runs on
     the current stream, which then waits for the collective and writes the fp16 weight
-    gradients (divided by the world size when ``average``)."""
+    gradients (divided by the world size when ``average``).  After the call ``bucket`` holds
+    the sum over the ranks.  ``timing`` (a list) receives a ``(start, end)`` pair of timing
+    events recorded on the communication stream around the all-reduce."""
     from . import capi
     cur = torch.cuda.current_stream(X.device)
     comm = _comm_stream(X.device)
@@ -70,7 +72,13 @@ def backward_allreduce(p, grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, l
                            bucket_ready=ready)
     with torch.cuda.stream(comm):
         comm.wait_event(ready)
+        if timing is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(comm)
         dist.all_reduce(bucket, op=dist.ReduceOp.SUM, group=group)
+        if timing is not None:
+            ev[1].record(comm)
+            timing.append(ev)
     cur.wait_stream(comm)
     bucket.record_stream(comm)
     alpha = 1.0 / dist.get_world_size(group) if average else 1.0

@@ -6,6 +6,10 @@ A pre-norm block is ``x + attn(LN(x))`` then ``x + MLP(LN(x))`` with a GELU MLP 
 attention wrapper (``layers/attention/morpho_attention.py:31-41``) adds an output ``Linear``
 after MorphoAttention; the benchmark configuration measured here has none (``out_proj=False``,
 the default), and ``out_proj=True`` restores it.  Everything is fp16, like the attention layer.
+
+``attention`` (optional) builds each block's attention layer from ``(dim, num_heads, cube_m,
+scale=, causal=, dtype=, device=)``; the default is this package's ``MorphoAttention``.  A CPU
+checker passes its own layer, and then this module needs nothing else from the package.
 """
 
 from __future__ import annotations
@@ -13,7 +17,10 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from .autograd import MorphoAttention
+
+def _morpho_attention(dim, num_heads, cube_m, **kw):
+    from .autograd import MorphoAttention
+    return MorphoAttention(dim, num_heads, cube_m, **kw)
 
 
 class MLP(nn.Module):
@@ -29,10 +36,12 @@ class MLP(nn.Module):
 
 class EncoderBlock(nn.Module):
     def __init__(self, dim: int, num_heads: int, cube_m: int, *, mlp_ratio: float = 4.0, scale: float = 1.0,
-                 causal: bool = False, out_proj: bool = False, dtype=torch.float16, device=None) -> None:
+                 causal: bool = False, out_proj: bool = False, dtype=torch.float16, device=None,
+                 attention=None) -> None:
         super().__init__()
         self.norm1 = nn.LayerNorm(dim, dtype=dtype, device=device)
-        self.attn = MorphoAttention(dim, num_heads, cube_m, scale=scale, causal=causal, dtype=dtype, device=device)
+        make = attention or _morpho_attention
+        self.attn = make(dim, num_heads, cube_m, scale=scale, causal=causal, dtype=dtype, device=device)
         self.proj = nn.Linear(dim, dim, dtype=dtype, device=device) if out_proj else None
         self.norm2 = nn.LayerNorm(dim, dtype=dtype, device=device)
         self.mlp = MLP(dim, int(dim * mlp_ratio), dtype=dtype, device=device)
@@ -50,11 +59,11 @@ class Encoder(nn.Module):
 
     def __init__(self, depth: int = 12, dim: int = 768, num_heads: int = 12, cube_m: int = 16, *,
                  mlp_ratio: float = 4.0, scale: float = 1.0, causal: bool = False, out_proj: bool = False,
-                 dtype=torch.float16, device=None) -> None:
+                 dtype=torch.float16, device=None, attention=None) -> None:
         super().__init__()
         self.blocks = nn.ModuleList(
             EncoderBlock(dim, num_heads, cube_m, mlp_ratio=mlp_ratio, scale=scale, causal=causal, out_proj=out_proj,
-                         dtype=dtype, device=device) for _ in range(depth))
+                         dtype=dtype, device=device, attention=attention) for _ in range(depth))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         for blk in self.blocks:

@@ -1,5 +1,9 @@
-"""Loader for the reference's own CUDA kernels built by ``oracle/build_ref.py`` into
-``oracle/_ref`` (test infrastructure: compares our kernels with the reference's)."""
+"""TEST INFRASTRUCTURE ONLY: loader for the reference's own CUDA kernels, built unmodified
+from the reference sources by ``oracle/build_ref.py`` into ``oracle/_ref``.
+
+Used by the tests (our kernels against the reference's on identical inputs) and by the
+baseline leg of ``bench.py`` (the reference kernel timed beside ours as a comparator).  The
+product package never imports it."""
 
 from __future__ import annotations
 
@@ -8,13 +12,11 @@ import os
 
 import torch
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_DIR = os.path.join(ROOT, "oracle", "_ref")
+REF_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref")
 
 # (cube_m, head_dim, causal) -> variant name (compile-time constants of the reference)
 VARIANT_OF = {(16, 32, False): "m16_hd32", (16, 64, False): "m16_hd64", (16, 64, True): "m16_hd64_causal",
               (32, 64, False): "m32_hd64"}
-# variants whose backward fits the 227 KB shared-memory limit only for narrow D
 _cache = {}
 
 

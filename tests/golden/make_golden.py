@@ -26,7 +26,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 from morphottention_b200.configs import CONFIGS, MorphoConfig, make_inputs  # noqa: E402
-from tests import refkernel  # noqa: E402
+from oracle import refkernel  # noqa: E402
 
 CASES = {
     # name: (config, random_gates)

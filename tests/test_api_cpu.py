@@ -129,3 +129,28 @@ def test_graphed_training_step_needs_cuda_inputs():
     opt = torch.optim.SGD(lin.parameters(), lr=0.1)
     with pytest.raises(ValueError, match="CUDA"):
         GraphedTrainingStep(lin, torch.nn.functional.mse_loss, opt, torch.zeros(2, 4), torch.zeros(2, 4))
+
+
+@pytest.mark.parametrize("config", ["c1", "c4vit"])
+def test_reference_arm_loads_no_native_library_of_this_repo(config):
+    """`bench.py --impl reference` times the CPU formulation only: it must not import this
+    package (whose __init__ loads _C.so and libmorpho_sm100.so) nor map either library."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    probe = (
+        "import runpy, sys, json\n"
+        f"sys.argv = ['bench.py', '--impl', 'reference', '--config', '{config}', '--steps', '1', '--warmup', '0']\n"
+        f"runpy.run_path({os.path.join(root, 'bench.py')!r}, run_name='__main__')\n"
+        "mods = [m for m in sys.modules if m.startswith('morphottention_b200')]\n"
+        "maps = [l for l in open('/proc/self/maps') if 'libmorpho_sm100' in l or '_C.so' in l]\n"
+        "print('PROBE', json.dumps({'mods': mods, 'maps': len(maps)}))\n")
+    r = subprocess.run([sys.executable, "-c", probe], capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    import json
+    line = json.loads(r.stdout.splitlines()[0])
+    assert line["impl"] == "reference" and line["value"] > 0
+    probe_out = json.loads(r.stdout.split("PROBE", 1)[1])
+    assert probe_out == {"mods": [], "maps": 0}, probe_out
