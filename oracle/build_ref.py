@@ -19,8 +19,15 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
+# Where the reference checkout lies: the MORPHO_REFERENCE_ROOT environment variable, else the
+# build machine's checkout.  The one place this path is named; every other user reads REF_ROOT.
 REF_ROOT = os.environ.get("MORPHO_REFERENCE_ROOT", "/root/reference")
 CSRC = os.path.join(REF_ROOT, "packages", "morphottention", "csrc")
+PY_PKG = os.path.join(REF_ROOT, "packages", "morphottention", "torch-ext", "morphottention")
+
+
+def sources_present() -> bool:
+    return os.path.isdir(CSRC)
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 # name -> (cube_m, head_dim, causal, extra defines)
