@@ -167,7 +167,9 @@ def grad_mode(mode: str):
 
 
 class MorphoAttentionFunction(torch.autograd.Function):
-    """Bridges the CUDA attention kernels into autograd."""
+    """``torch.autograd.Function`` over the torch ops: the forward keeps what the backward
+    reads (the projection buffer, out, lse, and the variant options of this call), the
+    backward returns the five gradients followed by ``None`` for the four non-tensor arguments."""
 
     @staticmethod
     def forward(ctx, x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float, causal: bool):
@@ -200,13 +202,17 @@ class MorphoAttentionFunction(torch.autograd.Function):
 
 
 class MorphoAttention(nn.Module):
-    """Morphological hypercube attention.
+    """Attention layer whose query-key score is a gated soft-Hamming distance between per-head
+    sigmoid codes in the unit hypercube (no output projection inside the layer).
 
-    :param dim: model dimension ``D`` (must be divisible by ``num_heads``).
-    :param num_heads: number of attention heads ``H``.
-    :param cube_m: hypercube width per head ``m`` (the score-GEMM contraction dim).
-    :param scale: softmax temperature.
-    :param causal: whether to apply causal masking.
+    :param dim: width ``D`` of the token features; ``num_heads`` must divide it.
+    :param num_heads: head count ``H``; each head's values span ``D / H`` features.
+    :param cube_m: code length ``m`` of each head (16, 32 or 64): ``W_phi`` maps ``D`` to
+        ``H * m`` codes.
+    :param scale: factor applied to the score before the softmax.
+    :param causal: drop keys that come after the query.
+    :param dtype: parameter dtype (the kernels take float16).
+    :param device: where the parameters live.
     """
 
     def __init__(self, dim: int, num_heads: int, cube_m: int, *, scale: float = 1.0, causal: bool = False,
@@ -241,9 +247,9 @@ class MorphoAttention(nn.Module):
 
 def morpho_attention(x, W_phi, gate_q, gate_k, W_V, num_heads: int, cube_m: int, *, scale: float = 1.0,
                      causal: bool = False):
-    """Apply the Morphottention attention mechanism with autograd support.
+    """Functional form of :class:`MorphoAttention` with the parameters passed in.
 
-    :param x: input activations of shape (B, N, D) on a CUDA device.
-    :returns: the attention output, differentiable w.r.t. ``x`` and the parameters.
+    :param x: float16 CUDA tensor ``[B, N, D]``.
+    :returns: ``[B, N, D]``; gradients flow to ``x``, ``W_phi``, ``gate_q``, ``gate_k`` and ``W_V``.
     """
     return MorphoAttentionFunction.apply(x, W_phi, gate_q, gate_k, W_V, num_heads, cube_m, scale, causal)
