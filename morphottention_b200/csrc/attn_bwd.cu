@@ -13,7 +13,10 @@
 //   dK += dS^T . Qc_i           (A = dS^T from TMEM, B = Qc MN-major)      TMEM [.., +m)
 //       (centered codes: this is dk + gate_q * dcb, whose cancelling bias term is exact)
 //   dQ_i = dS . Kc              (A = dS from smem, MN-major)               TMEM [.., +m)
-//   dQ warps: dq[b,h,q,:] += 2*scale * dQ_i  (fp32 atomics into a workspace)
+//   dQ warps: dq[b,h,q,:] += 2*scale * dQ_i  (fp32 TMA reduce-add into a workspace: each
+//       warp stages its 32 rows in the shared dS tile, free between the dQ MMA and the next
+//       dS, and issues one bulk tensor reduce per 32-column box; scattered per-thread global
+//       reductions contended with the tensor core's shared-memory operand reads)
 // Scale factors: dL/dS_raw = 2*scale*dS and dL/dcbias = -scale*sum_i dS (attention.cu:425,
 // :436, :442).  Unlike the reference there are no fp16 global atomics: dV and dK are
 // complete per CTA and stored once; only dq is accumulated, in fp32.
@@ -30,11 +33,11 @@ namespace {
 
 constexpr int kBwdThreads = 512;
 constexpr int kTile = 128;
-// Register split (512 threads x 128 at launch = 65536): producer/MMA warpgroup 88, dQ
-// warpgroup 56, the two softmax warpgroups 184 each; 128*88 + 128*56 + 256*184 = 65536.
-constexpr uint32_t kRegsProducer = 88;
-constexpr uint32_t kRegsDq = 56;
-constexpr uint32_t kRegsSoftmax = 184;
+// Register split (512 threads x 128 at launch = 65536): producer/MMA warpgroup 96, dQ
+// warpgroup 64, the two softmax warpgroups 176 each; 128*96 + 128*64 + 256*176 = 65536.
+constexpr uint32_t kRegsProducer = 96;
+constexpr uint32_t kRegsDq = 64;
+constexpr uint32_t kRegsSoftmax = 176;
 static_assert(128 * kRegsProducer + 128 * kRegsDq + 256 * kRegsSoftmax == 65536, "register split");
 
 template <int MC, int HD>
@@ -95,6 +98,7 @@ struct BwdCfg {
     static constexpr uint32_t V_ROW = (HD > 64 ? 64 : HD) * 2;
 
     static_assert(SMEM_BYTES <= 232448, "smem budget");
+    static_assert(OFF_DS % 1024 == 0, "the dS tile (also the dQ staging, 128-byte swizzle) is 1024-byte aligned");
 };
 
 struct BwdArgs {
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const __grid_constant__ CUtensorMap tmKD,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmQaug,
-                    const BwdArgs args) {
+                    const __grid_constant__ CUtensorMap tmDQ, const BwdArgs args) {
     using Cfg = BwdCfg<MC, HD>;
     constexpr int kQStages = Cfg::kQStages;
     extern __shared__ uint8_t smem_raw[];
@@ -550,14 +554,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         regs_dec<kRegsDq>();
         // ---------------- dQ warps (12..15) ----------------
         const int quad = warp & 3;
-        const int r = quad * 32 + lane;  // query row within the tile
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+        // Staging: this warp's 32 rows in the shared dS tile, as DQ_BOXES boxes of 32 rows x
+        // DQ_BOX fp32 columns in the TMA swizzle of the dq tensor map (128 B rows: 16-byte unit
+        // u of row r at u ^ (r & 7); 64 B rows: u ^ ((r >> 1) & 3)).  The tile is free from
+        // dq_full(i) (the dQ MMA has read dS_i) until dq_free(i), which this warpgroup gives
+        // only once the TMA has read the staged rows.
+        constexpr int DQ_BOX = MC < 32 ? MC : 32;
+        constexpr int DQ_BOXES = MC / DQ_BOX;
+        constexpr int DQ_ROWB = DQ_BOX * 4;
+        static_assert(4 * DQ_BOXES * 32 * DQ_ROWB <= Cfg::DS_BYTES, "dQ staging fits the dS tile");
+        const uint32_t stage = smem_u32(smem + Cfg::OFF_DS + quad * (DQ_BOXES * 32 * DQ_ROWB));
+        const uint32_t my_row = stage + lane * DQ_ROWB;
+        const int swz = DQ_ROWB == 128 ? (lane & 7) : ((lane >> 1) & 3);
         for (int it = 0; it < n_it; ++it) {
             if (!mbar_wait_warp(dq_full, it & 1, args.status, K_ATTN_BWD, 14) || *abort_flag) break;
             tc_fence_after();
-            const int q = (i_begin + it) * kTile + r;
-            float* dst = args.dq + (static_cast<size_t>(bh) * args.N + q) * MC;
-#pragma unroll
+            const int q0 = (i_begin + it) * kTile + quad * 32;  // first row of this warp
+#pragma unroll 1
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
                 tmem_ld16(lane_base + Cfg::TM_DQ + c, rr);
@@ -570,19 +584,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 } else {
                     tmem_ld_wait();
                 }
-                if (c + 16 == MC) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(dq_free);
-                }
-                if (q < args.N) {
+                const uint32_t row = my_row + (c / DQ_BOX) * (32 * DQ_ROWB);
+                const int u0 = (c % DQ_BOX) / 4;
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        red_add_v4(dst + c + i, u2f(rr[i]) * args.two_scale, u2f(rr[i + 1]) * args.two_scale,
-                                   u2f(rr[i + 2]) * args.two_scale, u2f(rr[i + 3]) * args.two_scale);
-                }
+                for (int k = 0; k < 4; ++k)
+                    st_shared_v4(row + (((u0 + k) ^ swz) << 4), u2f(rr[4 * k]) * args.two_scale,
+                                 u2f(rr[4 * k + 1]) * args.two_scale, u2f(rr[4 * k + 2]) * args.two_scale,
+                                 u2f(rr[4 * k + 3]) * args.two_scale);
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && q0 < args.N) {  // rows past N are clipped by the TMA
+#pragma unroll
+                for (int bx = 0; bx < DQ_BOXES; ++bx)
+                    tma_reduce_add_3d(&tmDQ, stage + bx * (32 * DQ_ROWB), bx * DQ_BOX, q0, bh);
+                bulk_commit_group();
+                bulk_wait_read_all();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
         }
+        if (lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -598,7 +621,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     using Cfg = BwdCfg<MC, HD>;
     const int BH = s.B * s.H;
     const int Npad = (s.N + kTile - 1) / kTile * kTile;
-    CUtensorMap tQ, tK, tKD, tV, tDO, tL, tQA;
+    CUtensorMap tQ, tK, tKD, tV, tDO, tL, tQA, tDQ;
     if (p.kdq == nullptr || io.qaug == nullptr)
         return set_error(MORPHO_ERR_INVALID, "internal: backward needs the centered key codes and bias slices");
     MORPHO_TRY(make_tmap_3d_f16(&tQ, p.qc, MC, s.N, BH, MC, static_cast<uint64_t>(s.N) * MC, MC, kTile));
@@ -611,6 +634,13 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
                                 HD > 64 ? 64 : HD, kTile));
     MORPHO_TRY(make_tmap_2d_f32(&tL, io.L, BH, Npad, Npad, 1, kTile));
     MORPHO_TRY(make_tmap_3d_f16(&tQA, io.qaug, 16, s.N, BH, 16, static_cast<uint64_t>(s.N) * 16, 16, kTile));
+    {  // dq [BH, N, MC] fp32, reduced into by 32-row boxes of up to 32 columns
+        const uint64_t dims[3] = {static_cast<uint64_t>(MC), static_cast<uint64_t>(s.N), static_cast<uint64_t>(BH)};
+        const uint64_t strides[2] = {static_cast<uint64_t>(MC) * 4, static_cast<uint64_t>(s.N) * MC * 4};
+        const uint32_t box[3] = {MC < 32 ? MC : 32u, 32u, 1u};
+        MORPHO_TRY(make_tmap(&tDQ, io.dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dims, strides, box,
+                             MC < 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B));
+    }
     BwdArgs a;
     a.N = s.N;
     a.Npad = Npad;
@@ -633,7 +663,7 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream, "attn_bwd");
-    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKD, tV, tDO, tL, tQA, a);
+    kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKD, tV, tDO, tL, tQA, tDQ, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");
     return MORPHO_OK;
 }
