@@ -266,7 +266,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp runs this loop (warp-uniform control flow and descriptor arithmetic);
+        // elect.sync inside umma_*_w / umma_commit_w lets one lane issue each instruction.
+        {
             constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);   // S^T, dP^T
             constexpr uint32_t id_dv = make_idesc_f16(128, HD, false, true);    // dV
             constexpr uint32_t id_mc = make_idesc_f16(128, MC, false, true);    // dK (A in TMEM)
@@ -288,27 +290,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const uint32_t sQ = qbuf(it);
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks)
-                    umma_ss(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
+                    umma_ss_w(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
                             id_s, ks > 0 ? 1u : 0u);
-                umma_commit(s_full);
+                umma_commit_w(s_full);
             };
             // dP^T - delta = V . dO^T + [0,0,1,1,..] . [1,1,-delta_hi,-delta_lo,..]^T
             auto issue_dp = [&](int it) {
                 const uint32_t sDO = dobuf(it);
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks)
-                    umma_ss(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
+                    umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
                             id_s, ks > 0 ? 1u : 0u);
-                umma_ss(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_s, 1u);
-                umma_commit(dp_full);
+                umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_s, 1u);
+                umma_commit_w(dp_full);
             };
             // Issue order per query tile i: S_{i+1} (once the softmax warps hold S_i, when P has
             // its own columns), dV_i, [S_{i+1} here instead when P overwrites S], dK_i, dQ_i,
             // dP_{i+1}.  tcgen05.mma from one thread execute in order, so S_{i+1} may overwrite
             // the P_i columns it follows, and dP_{i+1} the dS_i columns.
-            bool ok = mbar_wait(kv_full, 0, args.status, K_ATTN_BWD, 3);
+            bool ok = mbar_wait_warp(kv_full, 0, args.status, K_ATTN_BWD, 3);
             if (ok && n_it > 0) {
-                ok = mbar_wait(q_full0, 0, args.status, K_ATTN_BWD, 4);
+                ok = mbar_wait_warp(q_full0, 0, args.status, K_ATTN_BWD, 4);
                 if (ok) {
                     tc_fence_after();
                     issue_s(0);
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 // means "stage i+1 has landed", ds_full(i) also "dQ_{i-1} has been read".
                 if (Cfg::P_SEP && it + 1 < n_it) {
                     // S_{i+1} as soon as the softmax warps have read S_i
-                    if (!mbar_wait(s_free, it & 1, args.status, K_ATTN_BWD, 15)) {
+                    if (!mbar_wait_warp(s_free, it & 1, args.status, K_ATTN_BWD, 15)) {
                         ok = false;
                         break;
                     }
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     issue_s(it + 1);
                 }
                 // dV += P^T . dO  (P^T of query half w in columns p_col(w) .. +32)
-                if (!mbar_wait(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
+                if (!mbar_wait_warp(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
                     ok = false;
                     break;
                 }
@@ -342,12 +344,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int ks = 0; ks < kTile / 16; ++ks) {
                     const uint32_t a = tmem + (ks < 4 ? Cfg::p_col(0) + ks * 8 : Cfg::p_col(1) + (ks - 4) * 8);
                     const uint64_t bd = make_sdesc(sDO + ks * 16 * Cfg::V_ROW, kTile * 128, 8 * Cfg::V_ROW, v_sw);
-                    umma_ts(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts_w(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
                 }
-                umma_commit(dv_done);
+                umma_commit_w(dv_done);
                 if (!Cfg::P_SEP && it + 1 < n_it) issue_s(it + 1);  // stage i+1 landed (see s_free)
                 // dK += dS^T . Qc ;  dQ = dS . Kc
-                if (!mbar_wait(ds_full, it & 1, args.status, K_ATTN_BWD, 6)) {
+                if (!mbar_wait_warp(ds_full, it & 1, args.status, K_ATTN_BWD, 6)) {
                     ok = false;
                     break;
                 }
@@ -356,7 +358,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int ks = 0; ks < kTile / 16; ++ks) {
                     const uint32_t a = tmem + Cfg::TM_DP + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
                     const uint64_t bd = make_sdesc(sQ + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
-                    umma_ts(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts_w(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
                 }
                 // dQ = dS . (k - gate_k/2) with the fp16 hi + lo parts: one N = 2m MMA whose
                 // column halves the dQ warps add, or two accumulating N = m passes
@@ -367,20 +369,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     for (int ks = 0; ks < kTile / 16; ++ks) {
                         const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
                         const uint64_t bd = make_sdesc(sKd + ks * 16 * Cfg::KD_ROW, 16, 8 * Cfg::KD_ROW, kd_sw);
-                        umma_ss(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
+                        umma_ss_w(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
                     }
                 }
-                umma_commit(dq_full);  // also: the shared dS tile is free again
-                umma_commit(q_empty0 + 8 * s);
+                umma_commit_w(dq_full);  // also: the shared dS tile is free again
+                umma_commit_w(q_empty0 + 8 * s);
                 if (it + 1 < n_it) issue_dp(it + 1);
             }
             if (ok) {
-                umma_commit(all_done);
+                umma_commit_w(all_done);
             } else {
                 *abort_flag = 1u;
-                umma_commit(drain);
-                mbar_wait(drain, 0, args.status, K_ATTN_BWD, 8);
-                umma_commit(all_done);  // release the epilogue waits
+                umma_commit_w(drain);
+                mbar_wait_warp(drain, 0, args.status, K_ATTN_BWD, 8);
+                umma_commit_w(all_done);  // release the epilogue waits
             }
         }
       }
