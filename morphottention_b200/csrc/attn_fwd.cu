@@ -166,7 +166,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         }
       } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp runs this loop (warp-uniform control flow and descriptor arithmetic);
+        // elect.sync inside umma_*_w / umma_commit_w lets one lane issue each instruction.
+        {
             constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
             constexpr uint32_t idesc_pv = make_idesc_f16(128, HD, false, true);
             constexpr uint32_t qk_sw = swizzle_code_for_row_bytes(Cfg::QK_ROW_BYTES);
@@ -174,19 +176,19 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             constexpr uint32_t v_sw = swizzle_code_for_row_bytes(Cfg::V_ROW_BYTES);
             constexpr uint32_t v_sbo = 8 * Cfg::V_ROW_BYTES;
             const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q);
-            bool ok = mbar_wait(q_full, 0, args.status, K_ATTN_FWD, 3);
+            bool ok = mbar_wait_warp(q_full, 0, args.status, K_ATTN_FWD, 3);
             auto issue_s = [&](int j) {
                 const uint32_t sK = smem_u32(smem + Cfg::OFF_K + (j % kKvStages) * Cfg::K_STRIDE);
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks) {
                     const uint64_t ad = make_sdesc(sQ + ks * 32, 16, qk_sbo, qk_sw);
                     const uint64_t bd = make_sdesc(sK + ks * 32, 16, qk_sbo, qk_sw);
-                    umma_ss(tmem + Cfg::TMEM_S, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+                    umma_ss_w(tmem + Cfg::TMEM_S, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
                 }
-                umma_commit(s_full);
+                umma_commit_w(s_full);
             };
             if (ok && n_kv > 0) {
-                ok = mbar_wait(kv_full0, 0, args.status, K_ATTN_FWD, 4);
+                ok = mbar_wait_warp(kv_full0, 0, args.status, K_ATTN_FWD, 4);
                 if (ok) {
                     tc_fence_after();
                     issue_s(0);
@@ -200,15 +202,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                     const int s1 = (j + 1) % kKvStages;
                     // (no abort-flag read here: every shared-memory probe of the MMA thread stalls
                     // it while MMAs are in flight; a failure elsewhere ends its bounded waits)
-                    if (!mbar_wait(s_free, j & 1, args.status, K_ATTN_FWD, 12) ||
-                        !mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
+                    if (!mbar_wait_warp(s_free, j & 1, args.status, K_ATTN_FWD, 12) ||
+                        !mbar_wait_warp(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, j & 1, args.status, K_ATTN_FWD, 5)) {
+                if (!mbar_wait_warp(p_full, j & 1, args.status, K_ATTN_FWD, 5)) {
                     ok = false;
                     break;
                 }
@@ -217,16 +219,16 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 #pragma unroll
                 for (int ks = 0; ks < kTile / 16; ++ks) {
                     const uint64_t bd = make_sdesc(sV + ks * 16 * Cfg::V_ROW_BYTES, kTile * 128, v_sbo, v_sw);
-                    umma_ts(tmem + Cfg::TMEM_O, tmem + Cfg::TMEM_P + ks * 8, bd, idesc_pv,
+                    umma_ts_w(tmem + Cfg::TMEM_O, tmem + Cfg::TMEM_P + ks * 8, bd, idesc_pv,
                             (j > 0 || ks > 0) ? 1u : 0u);
                 }
-                umma_commit(o_done);
-                umma_commit(kv_empty0 + 8 * s);
+                umma_commit_w(o_done);
+                umma_commit_w(kv_empty0 + 8 * s);
             }
             if (!ok) {
                 *abort_flag = 1u;
-                umma_commit(drain);
-                mbar_wait(drain, 0, args.status, K_ATTN_FWD, 7);
+                umma_commit_w(drain);
+                mbar_wait_warp(drain, 0, args.status, K_ATTN_FWD, 7);
             }
         }
       }
