@@ -75,7 +75,8 @@ typedef struct morpho_problem {
                            left with no key gives out = 0, lse = -FLT_MAX and no gradient */
     int32_t score;      /* MORPHO_SCORE_* (0 = softmax attention).  With DILATION / EROSION the
                            forward writes lse = 0 (not defined for them), grad_mode must be FULL,
-                           and tau is a fixed hyper-parameter (no gradient) */
+                           and the backward returns dL/dtau as the last element of the fp32
+                           weight-gradient bucket (see morpho_sm100_backward) */
     float tau;          /* temperature of DILATION / EROSION, > 0 (ignored for SOFTMAX) */
 } morpho_problem_t;
 
@@ -93,7 +94,9 @@ MORPHO_API int morpho_sm100_forward(const morpho_problem_t* p, const void* X, co
  * The outputs are overwritten, not accumulated (no zero-fill needed, unlike
  * attention.cpp:93-98).  If dweights_f32 is non-NULL the weight gradients are written
  * there in fp32 instead -- layout [dW_phi (D*H*m) | dW_V (D*D) | d_gate_q (H*m) |
- * d_gate_k (H*m)] -- and dW_phi/dW_V/d_gate_q/d_gate_k may be NULL; a data-parallel
+ * d_gate_k (H*m)], followed for the DILATION / EROSION scores by one element dL/dtau
+ * (the temperature gradient of the reference's morfology/soft_morph.cuh:67-77, which exists
+ * only in this fp32 form) -- and dW_phi/dW_V/d_gate_q/d_gate_k may be NULL; a data-parallel
  * caller all-reduces that bucket and then calls morpho_sm100_finalize_weight_grads.
  * Replaces attention_backward_kernel_launcher (attention.cu:524-576). */
 MORPHO_API int morpho_sm100_backward(const morpho_problem_t* p, const void* grad_out, const void* X, const void* W_phi,
@@ -171,11 +174,13 @@ MORPHO_API int morpho_sm100_project(const morpho_problem_t* p, const void* X, co
                                     const void* gate_k, const void* W_V, void* qc, void* kc, void* v, float* qb,
                                     float* cb, float* phi, void* stream);
 
-/* Number of fp32 elements of the dweights_f32 bucket for problem p. */
+/* Number of fp32 elements of the dweights_f32 bucket for problem p (one more, dL/dtau, for the
+ * DILATION / EROSION scores). */
 MORPHO_API size_t morpho_sm100_weight_grad_elems(const morpho_problem_t* p);
 
-/* fp16 weight gradients = alpha * bucket (alpha = 1/world for a mean).  No reference
- * counterpart: the reference has no data-parallel path. */
+/* fp16 weight gradients = alpha * bucket (alpha = 1/world for a mean); the bucket's dL/dtau
+ * element, if any, is left as it is.  No reference counterpart: the reference has no
+ * data-parallel path. */
 MORPHO_API int morpho_sm100_finalize_weight_grads(const morpho_problem_t* p, const float* dweights_f32, float alpha,
                                        void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, void* stream);
 

@@ -5,10 +5,12 @@ reference's signatures and call ``torch.ops.morphottention.forward/backward``, w
 backed by hand-written tcgen05/TMA kernels behind the C ABI in ``include/morpho_sm100.h``.
 """
 
-from .autograd import (MorphoAttention, MorphoAttentionFunction, attention_options, get_cube_projection,
-                       get_grad_mode, get_mask_diag, get_score, grad_mode, morpho_attention, set_cube_projection,
-                       set_grad_mode, set_mask_diag, set_score)
+from .autograd import (MorphoAttention, MorphoAttentionFunction, SoftMorphAttention, SoftMorphAttentionFunction,
+                       attention_options, get_cube_projection, get_grad_mode, get_mask_diag, get_score, grad_mode,
+                       morpho_attention, set_cube_projection, set_grad_mode, set_mask_diag, set_score,
+                       soft_morph_attention)
 
 __all__ = ["MorphoAttention", "MorphoAttentionFunction", "morpho_attention", "set_grad_mode", "get_grad_mode",
            "grad_mode", "set_cube_projection", "get_cube_projection", "set_mask_diag", "get_mask_diag",
-           "set_score", "get_score", "attention_options"]
+           "set_score", "get_score", "attention_options", "SoftMorphAttention", "SoftMorphAttentionFunction",
+           "soft_morph_attention"]

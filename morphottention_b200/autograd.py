@@ -63,6 +63,14 @@ def _morpho_backward_saved_fake(grad_out, saved, X, W_phi, gate_q, gate_k, W_V, 
             torch.empty_like(W_V)]
 
 
+@torch.library.register_fake(add_op_namespace_prefix("backward_saved_tau"))
+def _morpho_backward_saved_tau_fake(grad_out, saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H: int, cube_m: int,
+                                    scale: float, causal: bool, grad_mode: int, projection: int, mask_diag: int,
+                                    score: int, tau: float):
+    return [torch.empty_like(X), torch.empty_like(W_phi), torch.empty_like(gate_q), torch.empty_like(gate_k),
+            torch.empty_like(W_V), X.new_empty((), dtype=torch.float32)]
+
+
 def set_grad_mode(mode: str) -> str:
     """Select the backward's gradient semantics process-wide and return the previous one.
 
@@ -253,3 +261,76 @@ def morpho_attention(x, W_phi, gate_q, gate_k, W_V, num_heads: int, cube_m: int,
     :returns: ``[B, N, D]``; gradients flow to ``x``, ``W_phi``, ``gate_q``, ``gate_k`` and ``W_V``.
     """
     return MorphoAttentionFunction.apply(x, W_phi, gate_q, gate_k, W_V, num_heads, cube_m, scale, causal)
+
+
+class SoftMorphAttentionFunction(torch.autograd.Function):
+    """The soft-morphology score (dilation or erosion) with the temperature as a tensor input, so
+    that ``tau`` can be learned: its gradient ``dL/dtau`` comes from the same backward pass
+    (reference ``csrc/cuda/morfology/soft_morph.cuh:67-77``, ``morph_dtau_term``).  The kernels take
+    the temperature's value when the forward runs (read on the host: a CUDA ``tau`` costs one
+    device-to-host copy per call).  The cube projection and diagonal mask are the process-wide
+    settings at forward time, as for :class:`MorphoAttentionFunction`."""
+
+    @staticmethod
+    def forward(ctx, x, W_phi, gate_q, gate_k, W_V, tau, H: int, cube_m: int, scale: float, causal: bool,
+                score: str):
+        if not x.is_cuda:
+            raise ValueError("MorphoAttention expects a CUDA tensor")
+        if score not in ("dilation", "erosion"):
+            raise ValueError("score must be 'dilation' or 'erosion'")
+        tau_value = float(tau)
+        if not tau_value > 0.0:
+            raise ValueError("tau must be positive")
+        x = x.contiguous()
+        _g, proj, mdiag, _score, _tau = current_options()
+        ctx.options = (GRAD_MODES["full"], proj, mdiag, SCORES[score], tau_value)
+        out, lse, saved = ops.forward_save(x, W_phi, gate_q, gate_k, W_V, H, cube_m, scale, causal, proj, mdiag,
+                                           SCORES[score], tau_value)
+        ctx.save_for_backward(x, W_phi, gate_q, gate_k, W_V, out, lse, saved)
+        ctx.H, ctx.cube_m, ctx.scale, ctx.causal = H, cube_m, scale, causal
+        ctx.tau_meta = (tau.dtype, tau.device) if isinstance(tau, torch.Tensor) else None
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, W_phi, gate_q, gate_k, W_V, out, lse, saved = ctx.saved_tensors
+        grad_out = grad_out.contiguous()
+        args = (grad_out, saved, x, W_phi, gate_q, gate_k, W_V, out, lse, ctx.H, ctx.cube_m, ctx.scale, ctx.causal,
+                *ctx.options)
+        d_tau = None
+        if ctx.needs_input_grad[5] and ctx.tau_meta is not None:
+            dX, dW_phi, d_gate_q, d_gate_k, dW_V, dt = ops.backward_saved_tau(*args)
+            dtype, device = ctx.tau_meta
+            d_tau = dt.to(device=device, dtype=dtype)
+        else:
+            dX, dW_phi, d_gate_q, d_gate_k, dW_V = ops.backward_saved(*args)
+        return dX, dW_phi, d_gate_q, d_gate_k, dW_V, d_tau, None, None, None, None, None
+
+
+def soft_morph_attention(x, W_phi, gate_q, gate_k, W_V, tau, num_heads: int, cube_m: int, *,
+                         score: str = "dilation", scale: float = 1.0, causal: bool = False):
+    """:func:`morpho_attention` with the soft-morphology aggregation in place of softmax . V:
+    ``out_ic = sgn * tau * logsumexp_j(sgn * (S_ij + V_jc) / tau)`` (``sgn`` = +1 for
+    ``"dilation"``, -1 for ``"erosion"``).  ``tau`` may be a float or a scalar tensor; a tensor that
+    requires grad receives ``dL/dtau``."""
+    return SoftMorphAttentionFunction.apply(x, W_phi, gate_q, gate_k, W_V, tau, num_heads, cube_m, scale, causal,
+                                            score)
+
+
+class SoftMorphAttention(MorphoAttention):
+    """:class:`MorphoAttention` aggregating with the soft-morphology score and a learnable
+    temperature ``tau`` (an fp32 scalar parameter; ``learn_tau=False`` keeps it fixed)."""
+
+    def __init__(self, dim: int, num_heads: int, cube_m: int, *, score: str = "dilation", tau: float = 1.0,
+                 learn_tau: bool = True, scale: float = 1.0, causal: bool = False,
+                 dtype: torch.dtype = torch.float16, device=None) -> None:
+        super().__init__(dim, num_heads, cube_m, scale=scale, causal=causal, dtype=dtype, device=device)
+        if score not in ("dilation", "erosion"):
+            raise ValueError("score must be 'dilation' or 'erosion'")
+        self.score = score
+        self.tau = nn.Parameter(torch.tensor(float(tau), dtype=torch.float32, device=device),
+                                requires_grad=learn_tau)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return SoftMorphAttentionFunction.apply(x, self.W_phi, self.gate_q, self.gate_k, self.W_V, self.tau,
+                                                self.num_heads, self.cube_m, self.scale, self.causal, self.score)

@@ -125,6 +125,8 @@ struct BwdPlan {
     __half* qaug;
     float* L;
     float* dqb;  // soft-morphology score: dL/dqbias, [B*H, Npad]
+    float* sg;         // soft-morphology score: sum_j S_ij dL/dS_ij per query row, [B*H, Npad]
+    float* dtau_part;  // soft-morphology score: partial sums of dL/dtau
     SmBwdScratch smx;  // soft-morphology tensor-core backward operands
     float* dq;
     float* dk;
@@ -152,6 +154,8 @@ void plan_bwd_rest(Carve& c, const Shape& s, int sms, BwdPlan* b) {
     b->qaug = c.take<__half>(BH * s.N * 16);
     b->L = c.take<float>(BH * Npad);
     b->dqb = s.score != kScoreSoftmax ? c.take<float>(BH * Npad) : nullptr;
+    b->sg = s.score != kScoreSoftmax ? c.take<float>(BH * Npad) : nullptr;
+    b->dtau_part = s.score != kScoreSoftmax ? c.take<float>(soft_morph_dtau_parts(s)) : nullptr;
     if (s.score != kScoreSoftmax) {
         b->smx.g = c.take<float>(BH * s.N * s.hd);
         b->smx.gt = c.take<float>(BH * s.hd * Npad);
@@ -201,6 +205,12 @@ int check_bwd_args(const void* grad_out, const void* X, const void* W_phi, const
     return MORPHO_OK;
 }
 
+// Elements of the fp32 weight-gradient bucket before the optional dL/dtau:
+// [dW_phi | dW_V | d_gate_q | d_gate_k].
+size_t weight_elems(const Shape& s) {
+    return static_cast<size_t>(s.D) * (s.Hm() + s.D) + 2u * static_cast<size_t>(s.Hm());
+}
+
 // Everything of the backward after the projection: delta, attention backward, the
 // sigmoid/gate chain rule, the weight-gradient chain (dW GEMM, reduction) and then the dX
 // GEMM, so that a data-parallel caller can start the all-reduce of the weight gradients
@@ -232,9 +242,14 @@ int run_backward_after_proj(const DeviceInfo& dev, const Shape& s, const BwdPlan
         // soft-morphology score: the forward's m + log2(l) (kept by forward_save, else
         // recomputed), then the two backward kernels
         if (!o2_ready) MORPHO_TRY(launch_soft_morph_fwd_tc(dev, s, b.proj, nullptr, b.proj.o2, st));
+        // the temperature gradient goes to the bucket's last element (no fp16 form)
+        float* dtau = dweights_f32 != nullptr ? dweights_f32 + weight_elems(s) : nullptr;
         MORPHO_TRY(launch_soft_morph_bwd(s, b.proj, b.smx.g != nullptr ? &b.smx : nullptr, dev.status,
-                                         static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb, b.dk, b.dcb,
-                                         b.dcat, st));
+                                         static_cast<const __half*>(grad_out), b.proj.o2, b.dq, b.dqb,
+                                         dtau != nullptr ? b.sg : nullptr, b.dk, b.dcb, b.dcat, st));
+        if (dtau != nullptr)
+            MORPHO_TRY(launch_soft_morph_dtau(s, b.proj, static_cast<const __half*>(grad_out), b.proj.o2, b.sg,
+                                              b.dcat, b.dtau_part, dtau, st));
     }
     MORPHO_TRY(launch_dz(s, b.proj.phi, b.dq, b.dk, b.dcb, b.dqb, gq, gk, b.dcat, b.gate_part, b.gate_blocks, st));
     MORPHO_TRY(launch_dw(dev, s, x, b.dcat, b.dw_part, b.splits, st));
@@ -282,7 +297,7 @@ size_t morpho_sm100_backward_workspace_size(const morpho_problem_t* p) {
 size_t morpho_sm100_weight_grad_elems(const morpho_problem_t* p) {
     Shape s;
     if (validate(p, &s) != MORPHO_OK) return 0;
-    return static_cast<size_t>(s.D) * (s.Hm() + s.D) + 2u * static_cast<size_t>(s.Hm());
+    return weight_elems(s) + (s.score != kScoreSoftmax ? 1u : 0u);  // + dL/dtau
 }
 
 int morpho_sm100_forward(const morpho_problem_t* p, const void* X, const void* W_phi, const void* gate_q,

@@ -132,13 +132,19 @@ struct SmBwdScratch {
     float* qct = nullptr;
 };
 int launch_soft_morph_bwd_tc(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __half* dO,
-                             const float* o2, float* dq, float* dqb, float* dk, float* dcb, __half* dcat,
-                             uint32_t* status, cudaStream_t stream);
+                             const float* o2, float* dq, float* dqb, float* sg, float* dk, float* dcb,
+                             __half* dcat, uint32_t* status, cudaStream_t stream);
 // Soft-morphology backward: the tensor-core split kernels and, gated against them by the forward's
 // range flag, the exact kernels; the exact kernels alone under the MORPHO_SOFT_MORPH_EXACT switch.
+// sg (may be NULL): per query row sum_j S_ij dL/dS_ij [B*H, Npad], for the temperature gradient.
 int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* tcx, uint32_t* status,
-                          const __half* dO, const float* o2, float* dq, float* dqb,
+                          const __half* dO, const float* o2, float* dq, float* dqb, float* sg,
                           float* dk, float* dcb, __half* dcat, cudaStream_t stream);
+// dL/dtau of the soft-morphology score into *dtau (device fp32), after launch_soft_morph_bwd left
+// sg and the dV columns of dcat; part holds soft_morph_dtau_parts(s) floats of partial sums.
+size_t soft_morph_dtau_parts(const Shape& s);
+int launch_soft_morph_dtau(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, const float* sg,
+                           const __half* dcat, float* part, float* dtau, cudaStream_t stream);
 
 // dqb (dL/dqbias, [B*H, Npad]) may be NULL: the softmax score's rows are shift-invariant, so
 // its query-bias gradient is identically 0.

@@ -57,6 +57,7 @@ struct SmArgs {
     float* o2;         // [BH, N, HD]: m + log2(l) per (i, c); +inf for a row without keys
     float* dq;         // [BH, N, MC]
     float* dqb;        // [BH, Npad]
+    float* sg;         // [BH, Npad]: sum_j S_ij dL/dS_ij (for dL/dtau), or NULL
     float* dk;         // [BH, N, MC]
     float* dcb;        // [BH, Npad]
     __half* dcat;      // [B*N, Cp]: dV at columns Hp + h*HD
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
 #pragma unroll
     for (int c = 0; c < MPT; ++c) dq[c] = 0.f;
     float dqb = 0.f;
+    float sdot = 0.f;  // sum_j s_ij dS_ij with s = kf2 (qc_i . k_j), for the temperature gradient
     const int n_kt = a.causal ? qt + 1 : a.n_tiles;
     for (int kt = 0; kt < n_kt; ++kt) {
         const int j0 = kt * kT;
@@ -317,6 +319,7 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
                 part += __shfl_xor_sync(0xffffffffu, part, 1);
                 part += __shfl_xor_sync(0xffffffffu, part, 2);
                 dsv[t] = part;
+                if (s > -INFINITY) sdot = fmaf(s, part, sdot);  // dropped pairs: s = -inf, dS = 0
             }
             __syncwarp();
             // every quarter holds the same sums; quarter t%4 == q4 writes them
@@ -336,7 +339,13 @@ __global__ void __launch_bounds__(kThreads) soft_morph_bwd_q_kernel(const SmArgs
         float* dst = a.dq + (base + i) * MC + q4 * MPT;
 #pragma unroll
         for (int c = 0; c < MPT; ++c) dst[c] = a.two_scale * dq[c];
-        if (q4 == 0) a.dqb[static_cast<size_t>(bh) * a.Npad + i] = a.neg_scale * dqb;
+        if (q4 == 0) {
+            const size_t row = static_cast<size_t>(bh) * a.Npad + i;
+            a.dqb[row] = a.neg_scale * dqb;
+            // S_ij = 2 scale (qc_i . k_j) - scale qbias_i: 2 scale (qc . k) = s * sgn tau ln 2 (= s
+            // * out_mul) and scale qbias = ln 2 * qb
+            if (a.sg != nullptr) a.sg[row] = a.out_mul * sdot - kLn2 * a.qb[row] * dqb;
+        }
     }
 }
 
@@ -541,8 +550,8 @@ int launch_soft_morph_fwd(const Shape& s, const ProjOut& p, __half* out, float* 
 }
 
 int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* tcx, uint32_t* status,
-                          const __half* dO, const float* o2, float* dq, float* dqb, float* dk, float* dcb,
-                          __half* dcat, cudaStream_t stream) {
+                          const __half* dO, const float* o2, float* dq, float* dqb, float* sg, float* dk,
+                          float* dcb, __half* dcat, cudaStream_t stream) {
     if (p.kdq == nullptr)
         return set_error(MORPHO_ERR_INVALID, "internal: soft-morphology backward needs the centered key codes");
     SmArgs a = make_args(s, p);
@@ -550,6 +559,7 @@ int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* 
     a.o2 = const_cast<float*>(o2);
     a.dq = dq;
     a.dqb = dqb;
+    a.sg = sg;
     a.dk = dk;
     a.dcb = dcb;
     a.dcat = dcat;
@@ -558,11 +568,126 @@ int launch_soft_morph_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch* 
         // runs when the flag is clear, the exact pair (below) when it is set
         if (tcx == nullptr)
             return set_error(MORPHO_ERR_INVALID, "internal: soft-morphology backward scratch missing");
-        MORPHO_TRY(launch_soft_morph_bwd_tc(s, p, *tcx, dO, o2, dq, dqb, dk, dcb, dcat, status, stream));
+        MORPHO_TRY(launch_soft_morph_bwd_tc(s, p, *tcx, dO, o2, dq, dqb, sg, dk, dcb, dcat, status, stream));
         a.flag = p.smflag;
         a.run_if_flag = 1;
     }
     return dispatch<Bwd>(s, a, stream);
+}
+
+// ---------------- temperature gradient ----------------
+// dL/dtau = (1/tau) [sum_ic dO_ic out_ic - sum_ij S_ij dL/dS_ij - sum_jc V_jc dL/dV_jc]: the
+// reference's per-(i, c) term (morfology/soft_morph.cuh:67-77) is dtau_ic = (out_ic - sum_j
+// P_ijc (S_ij + V_jc)) / tau with dtau = sum_ic dO_ic dtau_ic, and the sum over j of P (S + V)
+// splits into the score and value gradients the backward already forms (dL/dS_ij = sum_c dO_ic
+// P_ijc, dL/dV_jc = sum_i dO_ic P_ijc).  The query-side kernels leave sum_j S_ij dL/dS_ij per row
+// (sg); the value gradient is dcat's dV.  Two launches, fixed summation order (deterministic).
+namespace {
+
+struct DtauArgs {
+    int N, Npad, H, D, Cp, Hp, chunks;
+    float out_mul;  // sgn * tau * ln 2: out = out_mul * o2 - ln 2 * qb
+    const float* o2;
+    const float* qb;
+    const float* sg;
+    const __half* dO;
+    const __half* v;
+    const __half* dcat;
+    float* part;  // [BH * chunks]
+};
+
+// Block (bh, 32-row chunk), 8 warps; a warp walks rows, its lanes the head's channels.
+template <int HD>
+__global__ void __launch_bounds__(256) soft_morph_dtau_partial_kernel(const DtauArgs a) {
+    __shared__ float red[8];
+    const int bh = blockIdx.x, chunk = blockIdx.y;
+    const int b = bh / a.H, h = bh - b * a.H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float acc = 0.f;
+    for (int rr = warp; rr < 32; rr += 8) {
+        const int i = chunk * 32 + rr;
+        if (i >= a.N) break;
+        const size_t row = static_cast<size_t>(bh) * a.Npad + i;
+        const size_t vrow = (static_cast<size_t>(bh) * a.N + i) * HD;
+        const size_t tok = static_cast<size_t>(b) * a.N + i;
+        const float qbl = kLn2 * a.qb[row];
+        float t = 0.f;
+#pragma unroll
+        for (int c = lane; c < HD; c += 32) {
+            const float o = a.o2[vrow + c];
+            const float out = o == INFINITY ? 0.f : a.out_mul * o - qbl;  // +inf: a row without keys
+            t = fmaf(__half2float(a.dO[tok * a.D + h * HD + c]), out, t);
+            t = fmaf(-__half2float(a.v[vrow + c]), __half2float(a.dcat[tok * a.Cp + a.Hp + h * HD + c]), t);
+        }
+        if (lane == 0) t -= a.sg[row];
+        acc += t;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float sum = 0.f;
+        for (int w = 0; w < 8; ++w) sum += red[w];
+        a.part[static_cast<size_t>(bh) * a.chunks + chunk] = sum;
+    }
+}
+
+__global__ void __launch_bounds__(256) soft_morph_dtau_final_kernel(const float* part, int n, float inv_tau,
+                                                                     float* out) {
+    __shared__ float red[256];
+    float sum = 0.f;
+    for (int k = threadIdx.x; k < n; k += 256) sum += part[k];
+    red[threadIdx.x] = sum;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[0] = red[0] * inv_tau;
+}
+
+}  // namespace
+
+size_t soft_morph_dtau_parts(const Shape& s) {
+    return static_cast<size_t>(s.B) * s.H * ((s.N + 31) / 32);
+}
+
+int launch_soft_morph_dtau(const Shape& s, const ProjOut& p, const __half* dO, const float* o2, const float* sg,
+                           const __half* dcat, float* part, float* dtau, cudaStream_t stream) {
+    if (o2 == nullptr || sg == nullptr || part == nullptr || dtau == nullptr)
+        return set_error(MORPHO_ERR_INVALID, "internal: temperature gradient buffers missing");
+    DtauArgs a;
+    a.N = s.N;
+    a.Npad = (s.N + 127) / 128 * 128;
+    a.H = s.H;
+    a.D = s.D;
+    a.Cp = s.Cp();
+    a.Hp = s.Hp();
+    a.chunks = (s.N + 31) / 32;
+    const float sgn = s.score == kScoreErosion ? -1.0f : 1.0f;
+    a.out_mul = sgn * s.tau * kLn2;
+    a.o2 = o2;
+    a.qb = p.qb;
+    a.sg = sg;
+    a.dO = dO;
+    a.v = p.v;
+    a.dcat = dcat;
+    a.part = part;
+    const dim3 grid(s.B * s.H, a.chunks);
+    prof_begin(stream, "soft_morph_dtau");
+    switch (s.hd) {
+        case 32: soft_morph_dtau_partial_kernel<32><<<grid, 256, 0, stream>>>(a); break;
+        case 64: soft_morph_dtau_partial_kernel<64><<<grid, 256, 0, stream>>>(a); break;
+        case 128: soft_morph_dtau_partial_kernel<128><<<grid, 256, 0, stream>>>(a); break;
+        default: return set_error(MORPHO_ERR_INVALID, "head_dim %d not supported", s.hd);
+    }
+    MORPHO_LAUNCH_CHECK("soft_morph_dtau");
+    prof_begin(stream, "soft_morph_dtau_final");
+    soft_morph_dtau_final_kernel<<<1, 256, 0, stream>>>(part, static_cast<int>(soft_morph_dtau_parts(s)),
+                                                        1.0f / s.tau, dtau);
+    MORPHO_LAUNCH_CHECK("soft_morph_dtau_final");
+    return MORPHO_OK;
 }
 
 }  // namespace morpho

@@ -32,6 +32,7 @@ namespace {
 
 constexpr int kTile = 128;
 constexpr int kThreads = 384;  // warps 0-3: TMA, MMA, 2 idle; 4-11: two exponent warps per TMEM lane quarter
+constexpr float kLn2f = 0.6931471805599453f;
 
 inline int npad_of(int N) { return (N + kTile - 1) / kTile * kTile; }
 
@@ -134,7 +135,7 @@ struct QCfg {
                                   : (OFF_STAGE + 2 * STAGE + 3072 <= 220 * 1024) ? 2
                                                                                  : 1;
     static constexpr int OFF_BAR = OFF_STAGE + STAGES * STAGE;
-    static constexpr int SMEM_BYTES = OFF_BAR + 1024 + 1024;  // barriers, TMEM slot, 128 row sums; alignment
+    static constexpr int SMEM_BYTES = OFF_BAR + 2048 + 1024;  // barriers, TMEM slot, 2 x 128 row sums; alignment
     static constexpr int TX_STAGE = K_BYTES + EV_BYTES + KD_BYTES;
     static constexpr uint32_t TM_S = 0, TM_X = 128, TM_D = 256, TM_DQ = 384;
     static constexpr uint32_t QK_ROW = MC * 2;
@@ -148,6 +149,8 @@ struct QArgs {
     const float* mrow;
     float* dq;    // [BH, N, MC]
     float* dqb;   // [BH, Npad]
+    const float* qb;  // [BH, Npad] scale * log2(e) * qbias
+    float* sg;    // [BH, Npad] sum_j S_ij dL/dS_ij (for dL/dtau), or NULL
     const uint32_t* flag;
     uint32_t* status;
 };
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     //       +6 rs_full (the second exponent half's row sums are in shared memory)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
     float* rs_half = reinterpret_cast<float*>(tmem_slot + 2);  // [128]
+    float* sd_half = rs_half + kTile;                          // [128]
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
@@ -321,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float kf2 = args.kf2;
         float rowsum = 0.f;
+        float sdot = 0.f;  // sum_j (qc_i . k_j) dS_ij, for the temperature gradient
         bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
             const int kv0 = j * kTile;
@@ -346,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const float dd = e * u2f(xv[k]);
                     rowsum += dd;
+                    sdot = fmaf(u2f(sv[k]), dd, sdot);
                     d[c + k] = __float_as_uint(dd);
                 }
             }
@@ -369,12 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the second half hands its row sums to the first, which writes the outputs
         if (half == 1) {
             rs_half[r] = rowsum;
+            sd_half[r] = sdot;
             __syncwarp();
             if (lane == 0) mbar_arrive(rs_full);
         } else if (ok && n_kv > 0 && mbar_wait_warp(dq_done, (n_kv - 1) & 1, args.status, K_SOFT_MORPH, 51) &&
                    mbar_wait_warp(rs_full, 0, args.status, K_SOFT_MORPH, 52)) {
             tc_fence_after();
             rowsum += rs_half[r];
+            sdot += sd_half[r];
             const uint32_t acc_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll
             for (int c = 0; c < MC; c += 16) {
@@ -389,7 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              args.two_scale * u2f(rr[4 * i + 2]), args.two_scale * u2f(rr[4 * i + 3]));
                 }
             }
-            if (q < args.N) args.dqb[static_cast<size_t>(bh) * args.Npad + q] = args.neg_scale * rowsum;
+            if (q < args.N) {
+                const size_t row = static_cast<size_t>(bh) * args.Npad + q;
+                args.dqb[row] = args.neg_scale * rowsum;
+                // S_ij = 2 scale (qc_i . k_j) - scale qbias_i, and scale qbias = ln 2 * qb
+                if (args.sg != nullptr) args.sg[row] = args.two_scale * sdot - kLn2f * args.qb[row] * rowsum;
+            }
         } else if (!ok) {
             *abort_flag = 1u;
         }
@@ -752,7 +765,8 @@ int tmap_f32_3d(CUtensorMap* map, const float* base, uint64_t d0, uint64_t d1, u
 
 template <int MC, int HD, bool CAUSAL>
 int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __half* dO, const float* o2,
-               float* dq, float* dqb, float* dk, float* dcb, __half* dcat, uint32_t* status, cudaStream_t stream) {
+               float* dq, float* dqb, float* sg, float* dk, float* dcb, __half* dcat, uint32_t* status,
+               cudaStream_t stream) {
     const int BH = s.B * s.H;
     const int N = s.N, Npad = npad_of(N), n_tiles = Npad / kTile;
     const float sgn = s.score == kScoreErosion ? -1.0f : 1.0f;
@@ -789,6 +803,8 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
     qa.mrow = p.mrow;
     qa.dq = dq;
     qa.dqb = dqb;
+    qa.qb = p.qb;
+    qa.sg = sg;
     qa.flag = p.smflag;
     qa.status = status;
     auto kq = sm_bwd_q_kernel<MC, HD, CAUSAL>;
@@ -829,15 +845,15 @@ int run_tc_bwd(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __
 }  // namespace
 
 int launch_soft_morph_bwd_tc(const Shape& s, const ProjOut& p, const SmBwdScratch& x, const __half* dO,
-                             const float* o2, float* dq, float* dqb, float* dk, float* dcb, __half* dcat,
-                             uint32_t* status, cudaStream_t st) {
+                             const float* o2, float* dq, float* dqb, float* sg, float* dk, float* dcb,
+                             __half* dcat, uint32_t* status, cudaStream_t st) {
     if (x.g == nullptr || x.gt == nullptr || x.evn == nullptr || x.kdt == nullptr || x.qct == nullptr ||
         p.mrow == nullptr || p.rv == nullptr || p.smflag == nullptr || p.kdq == nullptr)
         return set_error(MORPHO_ERR_INVALID, "internal: soft-morphology tensor-core backward scratch missing");
 #define MORPHO_TCB_CASE(M, HDV)                                                                               \
     if (s.m == M && s.hd == HDV)                                                                              \
-        return s.causal ? run_tc_bwd<M, HDV, true>(s, p, x, dO, o2, dq, dqb, dk, dcb, dcat, status, st)       \
-                        : run_tc_bwd<M, HDV, false>(s, p, x, dO, o2, dq, dqb, dk, dcb, dcat, status, st);
+        return s.causal ? run_tc_bwd<M, HDV, true>(s, p, x, dO, o2, dq, dqb, sg, dk, dcb, dcat, status, st)   \
+                        : run_tc_bwd<M, HDV, false>(s, p, x, dO, o2, dq, dqb, sg, dk, dcb, dcat, status, st);
     MORPHO_TCB_CASE(16, 32) MORPHO_TCB_CASE(16, 64) MORPHO_TCB_CASE(16, 128)
     MORPHO_TCB_CASE(32, 32) MORPHO_TCB_CASE(32, 64) MORPHO_TCB_CASE(32, 128)
     MORPHO_TCB_CASE(64, 32) MORPHO_TCB_CASE(64, 64) MORPHO_TCB_CASE(64, 128)

@@ -15,7 +15,8 @@
 // `backward` at the moment each is called.  forward_save / backward_saved keep the
 // projection of the forward for the backward instead of recomputing it, and take every
 // option as an explicit argument, so a backward always runs the variant its forward ran
-// (the autograd Functions capture the settings when the forward runs).
+// (the autograd Functions capture the settings when the forward runs); backward_saved_tau
+// also returns dL/dtau of the soft-morphology score (a learnable temperature).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -143,7 +144,8 @@ std::vector<at::Tensor> morpho_forward_save(const at::Tensor& X, const at::Tenso
 std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tensor* saved, const at::Tensor& X,
                                       const at::Tensor& W_phi, const at::Tensor& gate_q, const at::Tensor& gate_k,
                                       const at::Tensor& W_V, const at::Tensor& out, const at::Tensor& lse, int64_t H,
-                                      int64_t cube_m, double scale, bool causal, const Options& opts) {
+                                      int64_t cube_m, double scale, bool causal, const Options& opts,
+                                      bool with_dtau = false) {
     TORCH_CHECK(grad_out.is_cuda() && X.is_cuda(), "Gradient output and X must be a CUDA tensors");
     check(grad_out, "grad_out");
     check(X, "X");
@@ -180,12 +182,20 @@ std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tens
     TORCH_CHECK(ws_bytes > 0, "morphottention backward: unsupported problem: ", morpho_sm100_last_error());
     auto ws = at::empty({static_cast<int64_t>(ws_bytes)}, X.options().dtype(at::kByte));
     auto stream = at::cuda::getCurrentCUDAStream(X.device().index());
+    // the temperature gradient exists in the library's fp32 weight-gradient bucket only (its last
+    // element); the fp16 weight gradients are then finalized from the bucket
+    at::Tensor bucket;
+    if (with_dtau) {
+        TORCH_CHECK(p.score != MORPHO_SCORE_SOFTMAX, "the temperature gradient needs the dilation or erosion score");
+        bucket = at::empty({static_cast<int64_t>(morpho_sm100_weight_grad_elems(&p))}, X.options().dtype(at::kFloat));
+    }
+    float* dweights = with_dtau ? bucket.data_ptr<float>() : nullptr;
     const int rc =
         saved != nullptr
             ? morpho_sm100_backward_saved(&p, grad_out.data_ptr(), saved->data_ptr(), saved->numel(), X.data_ptr(),
                                           W_phi.data_ptr(), gate_q.data_ptr(), gate_k.data_ptr(), W_V.data_ptr(),
                                           out.data_ptr(), lse.data_ptr<float>(), dX.data_ptr(), dW_phi.data_ptr(),
-                                          d_gate_q.data_ptr(), d_gate_k.data_ptr(), dW_V.data_ptr(), nullptr,
+                                          d_gate_q.data_ptr(), d_gate_k.data_ptr(), dW_V.data_ptr(), dweights,
                                           ws.data_ptr(), ws_bytes, static_cast<void*>(stream.stream()))
             : morpho_sm100_backward(&p, grad_out.data_ptr(), X.data_ptr(), W_phi.data_ptr(), gate_q.data_ptr(),
                                     gate_k.data_ptr(), W_V.data_ptr(), out.data_ptr(), lse.data_ptr<float>(),
@@ -193,7 +203,12 @@ std::vector<at::Tensor> backward_impl(const at::Tensor& grad_out, const at::Tens
                                     dW_V.data_ptr(), nullptr, ws.data_ptr(), ws_bytes,
                                     static_cast<void*>(stream.stream()));
     TORCH_CHECK(rc == MORPHO_OK, "morphottention backward failed (", rc, "): ", morpho_sm100_last_error());
-    return {dX, dW_phi, d_gate_q, d_gate_k, dW_V};
+    if (!with_dtau) return {dX, dW_phi, d_gate_q, d_gate_k, dW_V};
+    const int rc2 = morpho_sm100_finalize_weight_grads(&p, bucket.data_ptr<float>(), 1.0f, dW_phi.data_ptr(),
+                                                       d_gate_q.data_ptr(), d_gate_k.data_ptr(), dW_V.data_ptr(),
+                                                       static_cast<void*>(stream.stream()));
+    TORCH_CHECK(rc2 == MORPHO_OK, "morphottention backward failed (", rc2, "): ", morpho_sm100_last_error());
+    return {dX, dW_phi, d_gate_q, d_gate_k, dW_V, bucket.narrow(0, bucket.numel() - 1, 1).reshape({})};
 }
 
 std::vector<at::Tensor> morpho_backward(const at::Tensor& grad_out, const at::Tensor& X, const at::Tensor& W_phi,
@@ -212,6 +227,18 @@ std::vector<at::Tensor> morpho_backward_saved(const at::Tensor& grad_out, const 
                                               int64_t score, double tau) {
     return backward_impl(grad_out, &saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal,
                          explicit_options(grad_mode, projection, mask_diag, score, tau));
+}
+
+// backward_saved plus dL/dtau of the soft-morphology score as a sixth output (0-dim fp32).
+std::vector<at::Tensor> morpho_backward_saved_tau(const at::Tensor& grad_out, const at::Tensor& saved,
+                                                  const at::Tensor& X, const at::Tensor& W_phi,
+                                                  const at::Tensor& gate_q, const at::Tensor& gate_k,
+                                                  const at::Tensor& W_V, const at::Tensor& out, const at::Tensor& lse,
+                                                  int64_t H, int64_t cube_m, double scale, bool causal,
+                                                  int64_t grad_mode, int64_t projection, int64_t mask_diag,
+                                                  int64_t score, double tau) {
+    return backward_impl(grad_out, &saved, X, W_phi, gate_q, gate_k, W_V, out, lse, H, cube_m, scale, causal,
+                         explicit_options(grad_mode, projection, mask_diag, score, tau), true);
 }
 
 int64_t set_grad_mode(int64_t mode) {
@@ -272,6 +299,10 @@ TORCH_LIBRARY(morphottention, m) {
         "backward_saved(Tensor grad_out, Tensor saved, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
         "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal, int grad_mode, "
         "int projection, int mask_diag, int score, float tau) -> Tensor[]");
+    m.def(
+        "backward_saved_tau(Tensor grad_out, Tensor saved, Tensor X, Tensor W_phi, Tensor gate_q, Tensor gate_k, "
+        "Tensor W_V, Tensor out, Tensor lse, int H, int cube_m, float scale, bool causal, int grad_mode, "
+        "int projection, int mask_diag, int score, float tau) -> Tensor[]");
     m.def("set_grad_mode(int mode) -> int", &set_grad_mode);
     m.def("get_grad_mode() -> int", &get_grad_mode);
     m.def("set_cube_projection(int proj) -> int", &set_cube_projection);
@@ -289,4 +320,5 @@ TORCH_LIBRARY_IMPL(morphottention, CUDA, m) {
     m.impl("backward", &morpho_backward);
     m.impl("forward_save", &morpho_forward_save);
     m.impl("backward_saved", &morpho_backward_saved);
+    m.impl("backward_saved_tau", &morpho_backward_saved_tau);
 }

@@ -248,14 +248,51 @@ def soft_morph_forward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale
 
 def soft_morph_forward_backward(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
                                 causal: bool = False, score: str = "dilation", tau: float = 1.0, grad_out=None,
-                                dtype=torch.float32, projection: str = "sigmoid", mask_diag: bool = False):
-    """Forward plus the backward of ``sum(out * grad_out)`` for :func:`soft_morph_forward`."""
+                                dtype=torch.float32, projection: str = "sigmoid", mask_diag: bool = False,
+                                tau_grad: bool = False):
+    """Forward plus the backward of ``sum(out * grad_out)`` for :func:`soft_morph_forward`.  With
+    ``tau_grad`` the temperature is a leaf too and ``res["d_tau"]`` is ``dL/dtau``, the sum over
+    (i, c) of ``grad_out_ic (out_ic - sum_j P_ijc (S_ij + V_jc)) / tau``
+    (``csrc/cuda/morfology/soft_morph.cuh:67-77``), here by autograd."""
     leaves = [t.detach().to(dtype).clone().requires_grad_(True) for t in (x, W_phi, gate_q, gate_k, W_V)]
+    tau_t = torch.tensor(float(tau), dtype=dtype, requires_grad=True) if tau_grad else tau
     with torch.enable_grad():
-        out = soft_morph_forward(*leaves, H, cube_m, scale, causal, score, tau, projection, mask_diag)
+        out = soft_morph_forward(*leaves, H, cube_m, scale, causal, score, tau_t, projection, mask_diag)
         g = torch.ones_like(out) if grad_out is None else grad_out.detach().to(dtype)
-        grads = torch.autograd.grad(out, leaves, grad_outputs=g)
-    names = ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V")
+        grads = torch.autograd.grad(out, leaves + ([tau_t] if tau_grad else []), grad_outputs=g)
+    names = ("dX", "dW_phi", "d_gate_q", "d_gate_k", "dW_V") + (("d_tau",) if tau_grad else ())
     res = {"out": out.detach()}
     res.update({n: gr.detach() for n, gr in zip(names, grads)})
     return res
+
+
+def soft_morph_dtau_terms(x, W_phi, gate_q, gate_k, W_V, H: int, cube_m: int, scale: float = 1.0,
+                          causal: bool = False, score: str = "dilation", tau: float = 1.0, grad_out=None,
+                          mask_diag: bool = False, dtype=torch.float64):
+    """The three sums whose difference is ``tau * dL/dtau`` (``soft_morph.cuh:67-77`` regrouped):
+    ``(sum dO.out, sum_ij S_ij dL/dS_ij, sum_jc V_jc dL/dV_jc)``, by autograd through the score
+    and the values.  Tests judge a computed ``dL/dtau`` against the size of these terms, since
+    they cancel (sigmoid projection)."""
+    sgn = 1.0 if score == "dilation" else -1.0
+    args = [t.detach().to(dtype) for t in (x, W_phi, gate_q, gate_k, W_V)]
+    B, N, D = args[0].shape
+    _, q, k, qbias, cbias, v = project(*args, H, cube_m)
+    s = (scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))).detach()
+    v = v.detach()
+    s.requires_grad_(True)
+    v.requires_grad_(True)
+    mask = torch.zeros(N, N, dtype=torch.bool)
+    if causal:
+        mask |= torch.ones(N, N, dtype=torch.bool).triu(1)
+    if mask_diag:
+        mask |= torch.eye(N, dtype=torch.bool)
+    g = torch.ones(B, N, D, dtype=dtype) if grad_out is None else grad_out.detach().to(dtype)
+    with torch.enable_grad():
+        a = sgn * (s.unsqueeze(-1) + v.unsqueeze(-3)) / tau
+        a = a.masked_fill(mask.unsqueeze(-1), float("-inf"))
+        dead = mask.all(dim=-1)
+        a = a.masked_fill(dead.view(N, 1, 1), 0.0)
+        o = (sgn * tau * torch.logsumexp(a, dim=-2)).masked_fill(dead.view(N, 1), 0.0)
+        out = o.permute(0, 2, 1, 3).reshape(B, N, D)
+        gs, gv = torch.autograd.grad(out, (s, v), grad_outputs=g)
+    return (float((g * out).sum()), float((s.masked_fill(mask, 0.0) * gs).sum()), float((v * gv).sum()))

@@ -110,3 +110,12 @@ def test_soft_morph_backward_workspace_holds_tensor_core_operands(H):
     BH, hd, Npad = B * H, D // H, 128
     operands = 4 * (BH * N * hd + 2 * BH * hd * Npad + 2 * BH * m * Npad)
     assert extra >= operands
+
+
+def test_bucket_holds_the_temperature_gradient_for_soft_morphology():
+    """The fp32 weight-gradient bucket gains one last element, dL/dtau, for the dilation and
+    erosion scores (no device needed: sizes only)."""
+    base = capi.weight_grad_elems(capi.problem(2, 64, 128, 2, 16))
+    assert base == 128 * (2 * 16 + 128) + 2 * 2 * 16
+    for score in ("dilation", "erosion"):
+        assert capi.weight_grad_elems(capi.problem(2, 64, 128, 2, 16, score=score, tau=0.5)) == base + 1

@@ -184,3 +184,74 @@ def test_soft_morph_invalid_problems(cuda):
         assert capi.last_error()
     with pytest.raises(ValueError):
         M.set_score("max")
+
+
+def _check_dtau(got, want, cfg, t, g, score, tau, path):
+    """tau dL/dtau = sum dO.out - sum S dL/dS - sum V dL/dV: three sums that cancel (7x in the
+    m = 64 case), so the error is judged against the size of the cancelling terms (their total
+    magnitude / tau).  The exact kernels form dL/dS in fp32 and land within 2e-4 of that size; the
+    split path forms it from a tf32 product G . E_V^T, whose rounding of G_ic is shared by a whole
+    row of dL/dS (it does not average out in sum_j S_ij dL/dS_ij as it does in dq), measured within
+    2.1e-3: bounds 3e-4 (exact) and 4e-3 (split)."""
+    tol = 3e-4 if path == "exact" else 4e-3
+    terms = O.soft_morph_dtau_terms(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m,
+                                    cfg.scale, cfg.causal, score, tau, grad_out=g.cpu())
+    size = sum(abs(v) for v in terms) / tau
+    assert abs((terms[0] - terms[1] - terms[2]) / tau - want) <= 1e-4 * size  # the oracle's own identity
+    assert abs(got - want) <= tol * size, (got, want, size)
+
+
+@pytest.mark.parametrize("cfg,score,tau", [(CASES[1], "dilation", 0.9), (CASES[2], "erosion", 0.6),
+                                           (CASES[5], "dilation", 1.2)], ids=lambda v: getattr(v, "name", str(v)))
+def test_temperature_gradient_through_the_bucket(cuda, path, cfg, score, tau):
+    """dL/dtau (reference soft_morph.cuh:67-77) as the last element of the fp32 weight-gradient
+    bucket, both paths, against the oracle's autograd value (gradient tolerance); the weight
+    gradients finalized from the same bucket match the fp16 backward."""
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score=score, tau=tau)
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty((cfg.B * cfg.H, cfg.N), dtype=torch.float32, device=cuda)
+    capi.forward(p, *args, out, lse)
+    bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=cuda)
+    dX = torch.empty_like(inp["x"])
+    capi.backward(p, g, *args, out, lse, dX, None, None, None, None, dweights_f32=bucket)
+    grads = [torch.empty_like(t) for t in args[1:]]
+    capi.finalize_weight_grads(p, bucket, 1.0, grads[0], grads[1], grads[2], grads[3])
+    torch.cuda.synchronize()
+    assert capi.device_status(reset=True) == 0
+    t = {k: v.cpu() for k, v in inp.items()}
+    ref = O.soft_morph_forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m,
+                                        cfg.scale, cfg.causal, score, tau, grad_out=g.cpu(), tau_grad=True)
+    _check_dtau(float(bucket[-1]), float(ref["d_tau"]), cfg, t, g, score, tau, path)
+    ours = {"out": out, "dX": dX, "dW_phi": grads[0], "d_gate_q": grads[1], "d_gate_k": grads[2], "dW_V": grads[3]}
+    compare(ours, ref, keys=list(ours), tol_gate=gate_tolerance(cfg))
+
+
+def test_learnable_temperature_module(cuda):
+    """SoftMorphAttention: tau is an fp32 parameter whose gradient comes from the backward; one
+    SGD step on tau moves the loss as the gradient predicts."""
+    cfg = MorphoConfig("learn_tau", 2, 100, 128, 4, 16, 1.0, False, 62)
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    mod = M.SoftMorphAttention(cfg.D, cfg.H, cfg.cube_m, score="erosion", tau=0.7, scale=cfg.scale,
+                               causal=cfg.causal, device=cuda)
+    with torch.no_grad():
+        for n in ("W_phi", "W_V", "gate_q", "gate_k"):
+            getattr(mod, n).copy_(inp[n])
+    x = inp["x"].clone().requires_grad_(True)
+    out = mod(x)
+    (out.float() * g.float()).sum().backward()
+    t = {k: v.cpu() for k, v in inp.items()}
+    ref = O.soft_morph_forward_backward(t["x"], t["W_phi"], t["gate_q"], t["gate_k"], t["W_V"], cfg.H, cfg.cube_m,
+                                        cfg.scale, cfg.causal, "erosion", 0.7, grad_out=g.cpu(), tau_grad=True)
+    assert mod.tau.grad is not None and mod.tau.grad.dtype == torch.float32
+    _check_dtau(float(mod.tau.grad), float(ref["d_tau"]), cfg, t, g, "erosion", 0.7, "split")
+    ours = {"out": out.detach(), "dX": x.grad, "dW_phi": mod.W_phi.grad, "d_gate_q": mod.gate_q.grad,
+            "d_gate_k": mod.gate_k.grad, "dW_V": mod.W_V.grad}
+    compare(ours, ref, keys=list(ours), tol_gate=gate_tolerance(cfg))
+    # functional form with a float tau: no temperature gradient, same output
+    y = M.soft_morph_attention(inp["x"], mod.W_phi, mod.gate_q, mod.gate_k, mod.W_V, 0.7, cfg.H, cfg.cube_m,
+                               score="erosion", scale=cfg.scale, causal=cfg.causal)
+    assert torch.equal(y, out.detach())

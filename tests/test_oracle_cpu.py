@@ -196,3 +196,41 @@ def test_soft_morph_split_guard_floor():
     args = (inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], cfg.H, cfg.cube_m)
     _, acc32 = _split_soft_morph(*args, cfg.scale, "dilation", 0.005, torch.float32)
     assert acc32.min() < 2.0 ** -90
+
+
+def test_soft_morph_tau_gradient_pinned():
+    """dL/dtau of the soft-morphology score: the oracle's autograd value against a central finite
+    difference in float64, and the decomposition the kernels use,
+    tau dL/dtau = sum dO.out - sum_ij S_ij dL/dS_ij - sum_jc V_jc dL/dV_jc
+    (dL/dS and dL/dV by autograd through S and V), for dilation and erosion, causal."""
+    import torch
+
+    from morphottention_b200.configs import MorphoConfig, make_inputs
+    from oracle import morpho_oracle as O
+    cfg = MorphoConfig("tau", 1, 24, 32, 2, 16, 0.7, True, 61)
+    inp = {k: v.double() for k, v in make_inputs(cfg, random_gates=True, with_grad_out=True).items()}
+    g = inp.pop("grad_out")
+    args = [inp[k] for k in ("x", "W_phi", "gate_q", "gate_k", "W_V")]
+    for score, tau in (("dilation", 0.8), ("erosion", 1.3)):
+        r = O.soft_morph_forward_backward(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score, tau, grad_out=g,
+                                          dtype=torch.float64, tau_grad=True)
+        h = 1e-5
+        fp = (O.soft_morph_forward(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score, tau + h) * g).sum()
+        fm = (O.soft_morph_forward(*args, cfg.H, cfg.cube_m, cfg.scale, cfg.causal, score, tau - h) * g).sum()
+        fd = float((fp - fm) / (2 * h))
+        assert abs(float(r["d_tau"]) - fd) <= 1e-6 * max(1.0, abs(fd)), (score, float(r["d_tau"]), fd)
+        # the decomposition through the score and value gradients
+        sgn = 1.0 if score == "dilation" else -1.0
+        B, N, D = args[0].shape
+        _, q, k, qbias, cbias, v = O.project(*args, cfg.H, cfg.cube_m)
+        s = (cfg.scale * (2.0 * (q @ k.transpose(-1, -2)) - qbias.unsqueeze(-1) - cbias.unsqueeze(-2))).detach()
+        v = v.detach()
+        s.requires_grad_(True)
+        v.requires_grad_(True)
+        a = sgn * (s.unsqueeze(-1) + v.unsqueeze(-3)) / tau
+        mask = torch.ones(N, N, dtype=torch.bool).triu(1)
+        a = a.masked_fill(mask.unsqueeze(-1), float("-inf"))
+        out = (sgn * tau * torch.logsumexp(a, dim=-2)).permute(0, 2, 1, 3).reshape(B, N, D)
+        gs, gv = torch.autograd.grad(out, (s, v), grad_outputs=g)
+        decomposed = ((g * out).sum() - (s.masked_fill(mask, 0.0) * gs).sum() - (v * gv).sum()) / tau
+        assert abs(float(decomposed) - float(r["d_tau"])) <= 1e-9 * max(1.0, abs(fd)), score
