@@ -882,6 +882,65 @@ def run_vit_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_score_probe(args):
+    """--probe score: the design comparison behind running the morphological score on the tensor
+    cores.  On the configuration's codes (this library's projection), times the packed-half2
+    CUDA-core score probe (every pair's qc . k with HFMA2, row maxima with HMNMX2) and this
+    library's forward, whose attention kernel issues the same score as tcgen05 MMAs next to the
+    softmax and P.V; prints one JSON line with both rates (not the benchmark contract line)."""
+    import torch
+
+    from morphottention_b200 import capi
+    from morphottention_b200.configs import CONFIGS, make_inputs
+    cfg = CONFIGS[args.config if args.config in CONFIGS else "c3"]
+    if args.batch is not None:
+        cfg = cfg.with_(B=args.batch)
+    dev = torch.device("cuda", 0)
+    inp = make_inputs(cfg, device=dev)
+    p = capi.problem(cfg.B, cfg.N, cfg.D, cfg.H, cfg.cube_m, cfg.scale, cfg.causal)
+    o = capi.project(p, inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], with_phi=False)
+    rowmax = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
+    out = torch.empty_like(inp["x"])
+    lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
+
+    def timed(fn, reps):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    probe_ms = timed(lambda: capi.score_probe_half2(o["qc"], o["kc"], rowmax), args.steps)
+    capi.profile_select("attn_fwd")
+    capi.profile_enable(True)
+    timed(lambda: capi.forward(p, inp["x"], inp["W_phi"], inp["gate_q"], inp["gate_k"], inp["W_V"], out, lse),
+          args.steps)
+    prof = capi.profile_collect()
+    capi.profile_enable(False)
+    capi.profile_select(None)
+    fwd_ms = prof["attn_fwd"][0] / prof["attn_fwd"][1]
+    pairs = cfg.pairs()
+    score_flops = 2.0 * cfg.cube_m * pairs
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    line = {"probe": "score", "config": cfg.name, "B": cfg.B, "N": cfg.N, "H": cfg.H, "cube_m": cfg.cube_m,
+            "pairs": pairs,
+            "half2_score_probe": {"ms": probe_ms, "score_tflops": score_flops / probe_ms / 1e9,
+                                  # HFMA2: 64 thread instructions per clock per SM (ncu's
+                                  # sm__sass_thread_inst_executed_op_hfma_pred_on peak), 2 FMAs each
+                                  "fp16_cuda_core_peak_tflops": sms * 64 * 2 * 2 * 1.965e9 / 1e12,
+                                  "work": "qc . k with HFMA2 (fp16 accumulation) and the row maximum (HMNMX2)"},
+            "tcgen05_attn_fwd": {"ms": fwd_ms, "score_tflops": score_flops / fwd_ms / 1e9,
+                                 "all_tensor_tflops": 2.0 * (cfg.cube_m + cfg.head_dim) * pairs / fwd_ms / 1e9,
+                                 "work": "S = qc . k^T (tcgen05), exact online softmax (ex2), P . V (tcgen05)"},
+            "speedup_of_tensor_core_forward_over_half2_score_alone": probe_ms / fwd_ms}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -901,6 +960,8 @@ def main():
     ap.add_argument("--score", choices=["softmax", "dilation", "erosion"], default="softmax",
                     help="the attention score: softmax (the reference's), or the soft-morphology aggregation")
     ap.add_argument("--tau", type=float, default=1.0, help="temperature of the soft-morphology score")
+    ap.add_argument("--probe", choices=["score"], default=None,
+                    help="score: time the packed-half2 CUDA-core score probe against the tcgen05 forward")
     ap.add_argument("--eager", action="store_true",
                     help="c4vit: run the training step eagerly instead of replaying it as a CUDA graph")
     args = ap.parse_args()
@@ -908,7 +969,9 @@ def main():
         raise SystemExit("--score applies to the single-layer configurations of --impl ours")
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.config == "c4vit":
+    if args.probe == "score":
+        run_score_probe(args)
+    elif args.config == "c4vit":
         run_vit_reference(args) if args.impl == "reference" else run_vit(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -198,6 +198,14 @@ MORPHO_API int morpho_sm100_device_status(void* stream, int reset, uint32_t* sta
  * the word with morpho_sm100_device_status. */
 MORPHO_API int morpho_sm100_selftest_wait_timeout(uint32_t limit_us, void* stream);
 
+/* Design probe (no reference counterpart): the score the attention kernels issue as tcgen05
+ * MMAs, computed instead on packed half2 CUDA-core math -- for every query row of every (batch,
+ * head) the maximum over all keys of qc_i . k_j (cube_m/2 HFMA2 per pair, fp16 accumulation,
+ * HMNMX2 row maxima).  qc, kc: fp16 [BH, N, cube_m] (the layouts of morpho_sm100_project);
+ * rowmax: fp32 [BH, N].  Used to measure that alternative against the tensor-core kernels. */
+MORPHO_API int morpho_sm100_score_probe_half2(const void* qc, const void* kc, int32_t BH, int32_t N, int32_t cube_m,
+                                              float* rowmax, void* stream);
+
 /* Number of kernels the last forward / backward call on this thread launched. */
 MORPHO_API int morpho_sm100_last_launch_count(void);
 

@@ -53,6 +53,7 @@ EXPORTED = (
     "morpho_sm100_profile_enable",
     "morpho_sm100_profile_collect",
     "morpho_sm100_profile_select",
+    "morpho_sm100_score_probe_half2",
 )
 
 
@@ -125,6 +126,8 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_profile_collect.argtypes = [ctypes.c_char_p, i32, ctypes.POINTER(ctypes.c_float),
                                                ctypes.POINTER(ctypes.c_int), i32]
     L.morpho_sm100_profile_collect.restype = i32
+    L.morpho_sm100_score_probe_half2.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp]
+    L.morpho_sm100_score_probe_half2.restype = i32
     _lib = L
     return L
 
@@ -314,6 +317,13 @@ def profile_collect(max_kernels: int = 32) -> dict:
         nm = names.raw[i * name_len:(i + 1) * name_len].split(b"\0", 1)[0].decode()
         out[nm] = (float(ms[i]), int(cnt[i]))
     return out
+
+
+def score_probe_half2(qc, kc, rowmax, stream=None) -> None:
+    """Row maxima of qc . k^T over all keys on packed half2 CUDA-core math (the design probe
+    ``morpho_sm100_score_probe_half2``); qc, kc fp16 [BH, N, m], rowmax fp32 [BH, N]."""
+    BH, N, m = qc.shape
+    _check(lib().morpho_sm100_score_probe_half2(_ptr(qc), _ptr(kc), BH, N, m, _ptr(rowmax), _stream(stream)))
 
 
 def selftest_wait_timeout(limit_us: int = 20000, stream=None) -> None:
