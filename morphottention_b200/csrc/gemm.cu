@@ -470,7 +470,11 @@ int run_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap&
     a.tiles_n = (args.N + BN - 1) / BN;
     a.splits = splits;
     const int items = a.tiles_m * a.tiles_n * splits;
-    const int grid = items < sms ? items : sms;  // persistent: at most one CTA per SM
+    // Persistent CTAs, at most one per SM, dealt the items round-robin: as few CTAs as keep the
+    // largest per-CTA count (the kernel's length) leaves the other SMs free for concurrent work,
+    // e.g. the data-parallel all-reduce beside the dX GEMM (c3: 512 tiles on 128 of 148 SMs).
+    const int per_cta = (items + sms - 1) / sms;
+    const int grid = (items + per_cta - 1) / per_cta;
     prof_begin(stream, name);
     kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB0, tmB1, a, ep);
     MORPHO_LAUNCH_CHECK(name);
