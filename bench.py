@@ -425,11 +425,13 @@ def run_ours(args):
     # module's autograd Function does)
     saved = torch.empty(capi.saved_bytes(p), dtype=torch.uint8, device=dev)
 
-    def step():
+    ar_timing = []  # (start, end) events of each timed all-reduce, on the communication stream
+
+    def step(rec=None):
         capi.forward_save(p, x, W_phi, gq, gk, W_V, out, lse, saved=saved)
         if world > 1:  # weight-gradient all-reduce overlapped with the dX GEMM
             dp.backward_allreduce(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V,
-                                  bucket)
+                                  bucket, timing=rec)
         else:
             capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
 
@@ -462,11 +464,20 @@ def run_ours(args):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
-        step()
+        step(ar_timing)
     ev1.record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
+    allreduce = None
+    if world > 1:
+        ar = torch.tensor([sum(a.elapsed_time(b) for a, b in ar_timing) / len(ar_timing)], device=dev,
+                          dtype=torch.float64)
+        ars = [torch.empty_like(ar) for _ in range(world)]
+        dist.all_gather(ars, ar)
+        allreduce = {"ms_per_rank": [float(t.item()) for t in ars], "bytes": bucket.numel() * 4,
+                     "nccl_max_nchannels": os.environ.get("NCCL_MAX_NCHANNELS"),
+                     "timing": "CUDA events around each step's all-reduce on the communication stream"}
     prof_live = capi.profile_collect()
     capi.profile_enable(False)
     capi.profile_select(None)
@@ -611,7 +622,7 @@ def run_ours(args):
             "tensor_tflops_step": cfg.tensor_flops_fwd_bwd() / (ms / args.steps / 1000.0) / 1e12,
             "step_roofline_frac": (cfg.tensor_flops_fwd_bwd() / (peaks["bf16_tflops_sustained"] * 1e12))
             / (ms / args.steps / 1000.0),
-            "device_status": status, "dp_config": dp_res}
+            "device_status": status, "dp_config": dp_res, "allreduce": allreduce}
     # baseline legs (rank 0 at N = 1): the fp32 CPU oracle on the host cores, and the
     # reference's own CUDA kernel on this GPU
     if world == 1 and not args.no_cpu_baseline and args.score == "softmax":
