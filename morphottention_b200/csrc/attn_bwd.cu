@@ -50,12 +50,19 @@ struct BwdStages {
     static constexpr int VB = kTile * HD * 2;
     static constexpr int FIXED = 3 * KCS + VB + 2 * kTile * 128 + kTile * 32 + kTile * 4 + 256 + 1024;
     static constexpr int STAGE = KCS + VB + kTile * 32 + kTile * 4;
-    static constexpr int value = FIXED + 4 * STAGE <= 232448 ? 4 : (FIXED + 3 * STAGE <= 232448 ? 3 : 2);
+    // A second dS tile (32 KB) where it fits beside at least two stages: then the two query
+    // halves never wait for each other's dQ (see the dQ staging and dq_free below).
+    static constexpr int DS2_EXTRA = 2 * kTile * 128;
+    static constexpr bool ds2 = FIXED + DS2_EXTRA + 2 * STAGE <= 232448;
+    static constexpr int FIX = FIXED + (ds2 ? DS2_EXTRA : 0);
+    static constexpr int value = FIX + 4 * STAGE <= 232448 ? 4 : (FIX + 3 * STAGE <= 232448 ? 3 : 2);
 };
 
 template <int MC, int HD>
 struct BwdCfg {
     static constexpr int kQStages = BwdStages<MC, HD>::value;
+    static constexpr bool DS2 = BwdStages<MC, HD>::ds2;  // two dS tiles, alternating per query tile
+    static constexpr int N_DS = DS2 ? 2 : 1;
     static constexpr int KC_BYTES = kTile * MC * 2;  // one code tile (K or Q)
     static constexpr int V_BYTES = kTile * HD * 2;   // one V or dO tile
     static constexpr int KC_STRIDE = (KC_BYTES + 1023) / 1024 * 1024;
@@ -72,7 +79,7 @@ struct BwdCfg {
     static constexpr int OFF_DS = OFF_DO + kQStages * V_BYTES;  // 2 chunks x 128 rows x 128 B
     static constexpr int DS_BYTES = 2 * kTile * 128;
     static constexpr int AUG_BYTES = kTile * 16 * 2;  // one 16-column bias slice
-    static constexpr int OFF_VAUG = OFF_DS + DS_BYTES;
+    static constexpr int OFF_VAUG = OFF_DS + N_DS * DS_BYTES;
     static constexpr int OFF_QAUG = OFF_VAUG + AUG_BYTES;
     static constexpr int OFF_L = OFF_QAUG + kQStages * AUG_BYTES;
     static constexpr int OFF_DCB = OFF_L + kQStages * kTile * 4;
@@ -137,10 +144,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    // bars: [0,S) q_full, [S,2S) q_empty, then kv_full, s_full, dp_full, p_full, ds_full,
-    //       dq_full, dq_free, (unused), all_done, drain, s_free, dv_done; TMEM slot after
-    //       them (256 B total)
-    constexpr int NB = 2 * kQStages + 12;
+    // bars: [0,S) q_full, [S,2S) q_empty, kv_full, then per query half h (two each): s_full,
+    //       dp_full, p_full, ds_full, s_free, dv_done; then dq_full, dq_free (one per dS tile),
+    //       all_done, drain; TMEM slot and abort flag after them (256 B total)
+    constexpr int NB = 2 * kQStages + 18;
     static_assert(NB * 8 + 8 <= 256, "barrier block");
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NB);
     volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -158,16 +165,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t q_full0 = smem_u32(bars);
     const uint32_t q_empty0 = smem_u32(bars + kQStages);
     const uint32_t kv_full = smem_u32(bars + 2 * kQStages);
-    const uint32_t s_full = kv_full + 8;
-    const uint32_t dp_full = kv_full + 16;
-    const uint32_t p_full = kv_full + 24;
-    const uint32_t ds_full = kv_full + 32;
-    const uint32_t dq_full = kv_full + 40;
-    const uint32_t dq_free = kv_full + 48;
-    const uint32_t all_done = kv_full + 64;
-    const uint32_t drain = kv_full + 72;
-    const uint32_t s_free = kv_full + 80;   // the softmax warps hold S_i in registers
-    const uint32_t dv_done = kv_full + 88;  // dV_i has read P_i
+    // Per query half h (queries 64h .. 64h+63 of a tile, softmax warpgroup h): the two halves run
+    // as separate pipelines half a tile apart, so that on every SM sub-partition one warpgroup's
+    // exponentials overlap the other's dS phase.
+    auto s_full = [&](int h) { return kv_full + 8 * (1 + h); };    // S_h ready
+    auto dp_full = [&](int h) { return kv_full + 8 * (3 + h); };   // dP_h ready
+    auto p_full = [&](int h) { return kv_full + 8 * (5 + h); };    // P_h in TMEM, dP_h read
+    auto ds_full = [&](int h) { return kv_full + 8 * (7 + h); };   // dS_h in TMEM and shared memory
+    auto s_free = [&](int h) { return kv_full + 8 * (9 + h); };    // S_h read (and the next stage landed)
+    auto dv_done = [&](int h) { return kv_full + 8 * (11 + h); };  // dV_h has read P_h
+    const uint32_t dq_full = kv_full + 8 * 13;
+    // dq_free(b): the dQ warps have read dQ_i out of TMEM and the TMA has read the rows they staged
+    // in dS tile b = i % N_DS, so tile b and the dQ accumulator are free again
+    auto dq_free = [&](int b) { return kv_full + 8 * (14 + b); };
+    const uint32_t all_done = kv_full + 8 * 16;
+    const uint32_t drain = kv_full + 8 * 17;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kQStages; ++s) {
@@ -175,16 +187,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             mbar_init(q_empty0 + 8 * s, 1);
         }
         mbar_init(kv_full, 1);
-        mbar_init(s_full, 1);
-        mbar_init(dp_full, 1);
-        mbar_init(p_full, 8);
-        mbar_init(ds_full, 8);
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(s_full(h), 1);
+            mbar_init(dp_full(h), 1);
+            mbar_init(p_full(h), 4);
+            mbar_init(ds_full(h), 4);
+            mbar_init(s_free(h), 4);
+            mbar_init(dv_done(h), 1);
+        }
         mbar_init(dq_full, 1);
-        mbar_init(dq_free, 4);
+        mbar_init(dq_free(0), 4);
+        mbar_init(dq_free(1), 4);
         mbar_init(all_done, 1);
         mbar_init(drain, 1);
-        mbar_init(s_free, 8);
-        mbar_init(dv_done, 1);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -269,7 +284,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // The whole warp runs this loop (warp-uniform control flow and descriptor arithmetic);
         // elect.sync inside umma_*_w / umma_commit_w lets one lane issue each instruction.
         {
-            constexpr uint32_t id_s = make_idesc_f16(128, 128, false, false);   // S^T, dP^T
             constexpr uint32_t id_dv = make_idesc_f16(128, HD, false, true);    // dV
             constexpr uint32_t id_mc = make_idesc_f16(128, MC, false, true);    // dK (A in TMEM)
             constexpr uint32_t id_dq = make_idesc_f16(128, Cfg::DQ_COLS, true, true);  // dQ (A MN-major smem)
@@ -282,99 +296,137 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const uint32_t sDS = smem_u32(smem + Cfg::OFF_DS);
             auto qbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_Q + (it % kQStages) * Cfg::KC_STRIDE); };
             auto dobuf = [&](int it) { return smem_u32(smem + Cfg::OFF_DO + (it % kQStages) * Cfg::V_BYTES); };
-            // S^T = Kc . Qc^T
             auto augbuf = [&](int it) { return smem_u32(smem + Cfg::OFF_QAUG + (it % kQStages) * Cfg::AUG_BYTES); };
             const uint32_t sVaug = smem_u32(smem + Cfg::OFF_VAUG);
-            // S^T = Kc . Qc^T = k.q - cb/2 (centered query codes)
-            auto issue_s = [&](int it) {
-                const uint32_t sQ = qbuf(it);
+            constexpr uint32_t id_h = make_idesc_f16(128, 64, false, false);  // S_h^T, dP_h^T (64 queries)
+            // S_h^T = Kc . Qc_h^T = k.q - cb/2 (centered query codes), into TM_S + 64h
+            auto issue_s = [&](int it, int h) {
+                const uint32_t sQ = qbuf(it) + 64 * h * Cfg::KC_ROW;
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks)
-                    umma_ss_w(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
-                            id_s, ks > 0 ? 1u : 0u);
-                umma_commit_w(s_full);
+                    umma_ss_w(tmem + Cfg::TM_S + 64 * h, kmajor_desc<Cfg::KC_ROW>(sK, ks),
+                              kmajor_desc<Cfg::KC_ROW>(sQ, ks), id_h, ks > 0 ? 1u : 0u);
+                umma_commit_w(s_full(h));
             };
-            // dP^T - delta = V . dO^T + [0,0,1,1,..] . [1,1,-delta_hi,-delta_lo,..]^T
-            auto issue_dp = [&](int it) {
-                const uint32_t sDO = dobuf(it);
+            // dP_h^T - delta = V . dO_h^T + [0,0,1,1,..] . [1,1,-delta_hi,-delta_lo,..]^T, into TM_DP + 64h
+            auto issue_dp = [&](int it, int h) {
+                const uint32_t sDO = dobuf(it) + 64 * h * Cfg::V_ROW;
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks)
-                    umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
-                            id_s, ks > 0 ? 1u : 0u);
-                umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_s, 1u);
-                umma_commit_w(dp_full);
+                    umma_ss_w(tmem + Cfg::TM_DP + 64 * h, kmajor_desc<Cfg::V_ROW>(sV, ks),
+                              kmajor_desc<Cfg::V_ROW>(sDO, ks), id_h, ks > 0 ? 1u : 0u);
+                umma_ss_w(tmem + Cfg::TM_DP + 64 * h, kmajor_desc<32>(sVaug, 0),
+                          kmajor_desc<32>(augbuf(it) + 64 * h * 32, 0), id_h, 1u);
+                umma_commit_w(dp_full(h));
             };
-            // Issue order per query tile i: S_{i+1} (once the softmax warps hold S_i, when P has
-            // its own columns), dV_i, [S_{i+1} here instead when P overwrites S], dK_i, dQ_i,
-            // dP_{i+1}.  tcgen05.mma from one thread execute in order, so S_{i+1} may overwrite
-            // the P_i columns it follows, and dP_{i+1} the dS_i columns.
-            bool ok = mbar_wait_warp(kv_full, 0, args.status, K_ATTN_BWD, 3);
-            if (ok && n_it > 0) {
-                ok = mbar_wait_warp(q_full0, 0, args.status, K_ATTN_BWD, 4);
-                if (ok) {
-                    tc_fence_after();
-                    issue_s(0);
-                    issue_dp(0);
-                }
-            }
-            for (int it = 0; ok && it < n_it; ++it) {
-                const int s = it % kQStages;
-                const uint32_t sQ = qbuf(it);
+            // dV += P_h^T . dO_h   (P^T of query half h in columns p_col(h) .. +32)
+            auto issue_dv = [&](int it, int h) {
                 const uint32_t sDO = dobuf(it);
-                // The MMA thread waits on as few barriers as possible: each probe of shared memory
-                // it makes while MMAs are in flight stalls it for about an MMA latency.  The
-                // softmax warps fold the other conditions into their arrivals: s_free(i) also
-                // means "stage i+1 has landed", ds_full(i) also "dQ_{i-1} has been read".
-                if (Cfg::P_SEP && it + 1 < n_it) {
-                    // S_{i+1} as soon as the softmax warps have read S_i
-                    if (!mbar_wait_warp(s_free, it & 1, args.status, K_ATTN_BWD, 15)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    issue_s(it + 1);
-                }
-                // dV += P^T . dO  (P^T of query half w in columns p_col(w) .. +32)
-                if (!mbar_wait_warp(p_full, it & 1, args.status, K_ATTN_BWD, 5)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
 #pragma unroll
-                for (int ks = 0; ks < kTile / 16; ++ks) {
-                    const uint32_t a = tmem + (ks < 4 ? Cfg::p_col(0) + ks * 8 : Cfg::p_col(1) + (ks - 4) * 8);
+                for (int k = 0; k < 4; ++k) {
+                    const int ks = 4 * h + k;
                     const uint64_t bd = make_sdesc(sDO + ks * 16 * Cfg::V_ROW, kTile * 128, 8 * Cfg::V_ROW, v_sw);
-                    umma_ts_w(tmem + Cfg::TM_DV, a, bd, id_dv, (it > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts_w(tmem + Cfg::TM_DV, tmem + Cfg::p_col(h) + k * 8, bd, id_dv,
+                              (it > 0 || ks > 0) ? 1u : 0u);
                 }
-                umma_commit_w(dv_done);
-                if (!Cfg::P_SEP && it + 1 < n_it) issue_s(it + 1);  // stage i+1 landed (see s_free)
-                // dK += dS^T . Qc ;  dQ = dS . Kc
-                if (!mbar_wait_warp(ds_full, it & 1, args.status, K_ATTN_BWD, 6)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                umma_commit_w(dv_done(h));
+            };
+            // dK += dS_h^T . Qc_h   (dS_h^T in the first 32 dP_h columns)
+            //   (centered codes: this is dk + gate_q * dcb, whose cancelling bias term is exact)
+            auto issue_dk = [&](int it, int h) {
+                const uint32_t sQ = qbuf(it);
 #pragma unroll
-                for (int ks = 0; ks < kTile / 16; ++ks) {
-                    const uint32_t a = tmem + Cfg::TM_DP + (ks < 4 ? ks * 8 : 64 + (ks - 4) * 8);
+                for (int k = 0; k < 4; ++k) {
+                    const int ks = 4 * h + k;
                     const uint64_t bd = make_sdesc(sQ + ks * 16 * Cfg::KC_ROW, 16, 8 * Cfg::KC_ROW, kc_sw);
-                    umma_ts_w(tmem + Cfg::TM_DK, a, bd, id_mc, (it > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts_w(tmem + Cfg::TM_DK, tmem + Cfg::TM_DP + 64 * h + k * 8, bd, id_mc,
+                              (it > 0 || ks > 0) ? 1u : 0u);
                 }
-                // dQ = dS . (k - gate_k/2) with the fp16 hi + lo parts: one N = 2m MMA whose
-                // column halves the dQ warps add, or two accumulating N = m passes
+            };
+            // dQ = dS . (k - gate_k/2) with the fp16 hi + lo parts (A = both halves of the shared dS
+            // tile, MN-major): one N = 2m MMA whose column halves the dQ warps add, or two
+            // accumulating N = m passes; then the tile's stage is free
+            auto issue_dq = [&](int it) {
+                const uint32_t sDSi = sDS + (it % Cfg::N_DS) * Cfg::DS_BYTES;
 #pragma unroll
                 for (int part = 0; part < (Cfg::DQ_MERGED ? 1 : 2); ++part) {
                     const uint32_t sKd = sKD + part * Cfg::KC_STRIDE;
 #pragma unroll
                     for (int ks = 0; ks < kTile / 16; ++ks) {
-                        const uint64_t ad = make_sdesc(sDS + ks * 2048, kTile * 128, 1024, SW_128);
+                        const uint64_t ad = make_sdesc(sDSi + ks * 2048, kTile * 128, 1024, SW_128);
                         const uint64_t bd = make_sdesc(sKd + ks * 16 * Cfg::KD_ROW, 16, 8 * Cfg::KD_ROW, kd_sw);
                         umma_ss_w(tmem + Cfg::TM_DQ, ad, bd, id_dq, (part > 0 || ks > 0) ? 1u : 0u);
                     }
                 }
                 umma_commit_w(dq_full);  // also: the shared dS tile is free again
-                umma_commit_w(q_empty0 + 8 * s);
-                if (it + 1 < n_it) issue_dp(it + 1);
+                umma_commit_w(q_empty0 + 8 * (it % kQStages));
+            };
+            auto wait = [&](uint32_t bar, int phase, uint32_t site) {
+                if (!mbar_wait_warp(bar, static_cast<uint32_t>(phase) & 1u, args.status, K_ATTN_BWD, site))
+                    return false;
+                tc_fence_after();
+                return true;
+            };
+            // Issue order per iteration i (half 1 runs half a tile behind half 0; tcgen05.mma from
+            // one thread execute in order):
+            //   A  dV_1(i-1)                      [then S_1(i) when P shares S's columns]
+            //   B  S_0(i+1) once half 0 holds S_0(i)          (P in its own columns)
+            //   C  dK_1(i-1), dQ(i-1), dP_1(i)   (dP_1 overwrites dS_1 after dK_1 read it)
+            //   D  dV_0(i)                        [then S_0(i+1) when P shares S's columns]
+            //   E  S_1(i+1) once half 1 holds S_1(i)           (P in its own columns)
+            //   F  dK_0(i), dP_0(i+1)
+            // S_h(i+1) is issued only once stage i+1 has landed (waited for here; the softmax warps'
+            // arrivals do not imply it), and every later use of that stage follows in issue order.
+            // With fewer than 3 stages, stage i+1 is the one C releases (tile i-1), so C goes first.
+            constexpr bool kCFirst = kQStages < 3;
+            auto stage_landed = [&](int it2) { return wait(q_full0 + 8 * (it2 % kQStages), it2 / kQStages, 17); };
+            bool ok = wait(kv_full, 0, 3);
+            if (ok && n_it > 0) {
+                ok = wait(q_full0, 0, 4);
+                if (ok) {
+                    issue_s(0, 0);
+                    issue_s(0, 1);
+                    issue_dp(0, 0);
+                    issue_dp(0, 1);
+                }
+            }
+            for (int it = 0; ok && it <= n_it; ++it) {
+                const bool cur = it < n_it, nxt = it + 1 < n_it, prev = it > 0;
+                if (prev) {  // A
+                    if (!(ok = wait(p_full(1), it - 1, 5))) break;
+                    issue_dv(it - 1, 1);
+                    if (!Cfg::P_SEP && cur) issue_s(it, 1);
+                }
+                auto step_c = [&]() {
+                    if (!wait(ds_full(1), it - 1, 6)) return false;
+                    issue_dk(it - 1, 1);
+                    // with two dS tiles the softmax warps no longer wait for dQ_{i-2} to be read out
+                    // of TMEM before writing dS_{i-1}: the dQ accumulator's release is waited for here
+                    if (Cfg::DS2 && it >= 2 && !wait(dq_free((it - 2) % 2), (it - 2) / 2, 19)) return false;
+                    issue_dq(it - 1);
+                    if (cur) issue_dp(it, 1);
+                    return true;
+                };
+                if (kCFirst && prev && !(ok = step_c())) break;
+                if (Cfg::P_SEP && nxt) {  // B
+                    if (!(ok = wait(s_free(0), it, 15) && stage_landed(it + 1))) break;
+                    issue_s(it + 1, 0);
+                }
+                if (!kCFirst && prev && !(ok = step_c())) break;  // C
+                if (!cur) break;
+                if (!(ok = wait(p_full(0), it, 5))) break;  // D
+                issue_dv(it, 0);
+                if (!Cfg::P_SEP && nxt) {
+                    if (!(ok = stage_landed(it + 1))) break;
+                    issue_s(it + 1, 0);
+                }
+                if (Cfg::P_SEP && nxt) {  // E
+                    if (!(ok = wait(s_free(1), it, 15))) break;
+                    issue_s(it + 1, 1);
+                }
+                if (!(ok = wait(ds_full(0), it, 6))) break;  // F
+                issue_dk(it, 0);
+                if (nxt) issue_dp(it + 1, 0);
             }
             if (ok) {
                 umma_commit_w(all_done);
@@ -400,13 +452,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int sw = j & 7;
         float dcb = 0.f;
         bool ok = true;
-        for (int it = 0; it < n_it; ++it) {
+        // half 1 starts half a tile behind half 0 (once half 0 has its first P), so that the two
+        // warpgroups' exponential and dS phases alternate on every sub-partition
+        if (wg == 1 && n_it > 1 && !mbar_wait_warp(p_full(0), 0, args.status, K_ATTN_BWD, 18)) ok = false;
+        for (int it = 0; ok && it < n_it; ++it) {
             const int s = it % kQStages;
             const int q0 = (i_begin + it) * kTile;
             const int qc0 = q0 + wg * 64;  // first query of this warp group's half
-            // stage i has landed: waited for as "stage i+1" in the previous iteration
-            if (!mbar_wait_warp(s_full, it & 1, args.status, K_ATTN_BWD, 9) ||
-                (it == 0 && !mbar_wait_warp(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 10))) {
+            // S_h(i) ready; stage i landed (the MMA thread waited for it before issuing S_h(i), so
+            // this returns at once; it orders this warp's reads of L_i after the TMA's write)
+            if (!mbar_wait_warp(s_full(wg), it & 1, args.status, K_ATTN_BWD, 9) ||
+                !mbar_wait_warp(q_full0 + 8 * s, (it / kQStages) & 1, args.status, K_ATTN_BWD, 10)) {
                 ok = false;
                 break;
             }
@@ -421,16 +477,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64, rr);
                 tmem_ld32(lane_base + Cfg::TM_S + wg * 64 + 32, rr + 32);
                 tmem_ld_wait();
-                // s_free(i) tells the MMA thread both that S_{i+1} may overwrite the S columns
-                // and that the next stage has landed
-                if (it + 1 < n_it && !mbar_wait_warp(q_full0 + 8 * ((it + 1) % kQStages), ((it + 1) / kQStages) & 1,
-                                                     args.status, K_ATTN_BWD, 17)) {
-                    ok = false;
-                    break;
-                }
+                // s_free_h(i): S_h(i+1) may overwrite these columns
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(s_free);
+                if (lane == 0) mbar_arrive(s_free(wg));
 #pragma unroll
                 for (int i = 0; i < 64; i += 4) {
                     const float4 L = Lv[i / 4];
@@ -449,7 +499,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
             }
             if (Cfg::P_SEP && it > 0) {  // the P columns hold P_{i-1} until dV_{i-1} has read it
-                if (!mbar_wait_warp(dv_done, (it - 1) & 1, args.status, K_ATTN_BWD, 16)) {
+                if (!mbar_wait_warp(dv_done(wg), (it - 1) & 1, args.status, K_ATTN_BWD, 16)) {
                     ok = false;
                     break;
                 }
@@ -465,9 +515,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full(wg));
 
-            if (!mbar_wait_warp(dp_full, it & 1, args.status, K_ATTN_BWD, 11)) {
+            if (!mbar_wait_warp(dp_full(wg), it & 1, args.status, K_ATTN_BWD, 11)) {
                 ok = false;
                 break;
             }
@@ -488,24 +538,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64, pk);
                 tmem_st16(lane_base + Cfg::TM_DP + wg * 64 + 16, pk + 16);
-                // smem copy for the dQ MMA: row j, 16-byte units u = 0..7, 128-byte swizzle, once
-                // the dQ warps have read dQ_{i-1} (dq_free(i-1), which ds_full(i) then tells the
-                // MMA thread).  They arrive only after dq_full(i-1), so dQ_{i-1} is also done
-                // with the tile.
-                if (it > 0 && !mbar_wait_warp(dq_free, (it - 1) & 1, args.status, K_ATTN_BWD, 7)) {
+                // smem copy for the dQ MMA into dS tile b = i % N_DS: row j, 16-byte units u = 0..7,
+                // 128-byte swizzle, once the tile's previous user (query tile i - N_DS) is done:
+                // dq_free(b) comes after the dQ MMA read it, the dQ warps read that dQ out of TMEM
+                // and the TMA read what they staged there.  (With one tile that is dQ_{i-1}, and
+                // ds_full(i) then also tells the MMA thread that the dQ accumulator is free.)
+                const int b = it % Cfg::N_DS;
+                if (it >= Cfg::N_DS &&
+                    !mbar_wait_warp(dq_free(b), (it / Cfg::N_DS - 1) & 1, args.status, K_ATTN_BWD, 7)) {
                     ok = false;
                     break;
                 }
+                uint8_t* ds_dst = ds_row + b * Cfg::DS_BYTES;
 #pragma unroll
                 for (int u = 0; u < 8; ++u)
-                    *reinterpret_cast<uint4*>(ds_row + ((u ^ sw) << 4)) =
+                    *reinterpret_cast<uint4*>(ds_dst + ((u ^ sw) << 4)) =
                         make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
             }
             tmem_st_wait();
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(ds_full);
+            if (lane == 0) mbar_arrive(ds_full(wg));
         }
         // ---- epilogue: dV (group 0), dK + dcb (group 1)
         float* dcb_x = reinterpret_cast<float*>(smem + Cfg::OFF_DCB);
@@ -566,13 +620,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         constexpr int DQ_BOXES = MC / DQ_BOX;
         constexpr int DQ_ROWB = DQ_BOX * 4;
         static_assert(4 * DQ_BOXES * 32 * DQ_ROWB <= Cfg::DS_BYTES, "dQ staging fits the dS tile");
-        const uint32_t stage = smem_u32(smem + Cfg::OFF_DS + quad * (DQ_BOXES * 32 * DQ_ROWB));
-        const uint32_t my_row = stage + lane * DQ_ROWB;
+        const uint32_t stage0 = smem_u32(smem + Cfg::OFF_DS + quad * (DQ_BOXES * 32 * DQ_ROWB));
         const int swz = DQ_ROWB == 128 ? (lane & 7) : ((lane >> 1) & 3);
         for (int it = 0; it < n_it; ++it) {
             if (!mbar_wait_warp(dq_full, it & 1, args.status, K_ATTN_BWD, 14) || *abort_flag) break;
             tc_fence_after();
             const int q0 = (i_begin + it) * kTile + quad * 32;  // first row of this warp
+            const uint32_t stage = stage0 + (it % Cfg::N_DS) * Cfg::DS_BYTES;  // the dS tile dQ_i read
+            const uint32_t my_row = stage + lane * DQ_ROWB;
 #pragma unroll 1
             for (int c = 0; c < MC; c += 16) {
                 uint32_t rr[16];
@@ -605,7 +660,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
+            if (lane == 0) mbar_arrive(dq_free(it % Cfg::N_DS));
         }
         if (lane == 0) bulk_wait_all();
     }
