@@ -1,14 +1,16 @@
 // attn_bwd.cu -- MorphoAttention attention backward on sm_100a, KV-stationary.
 //
 // One CTA = one 128-key tile (kv0 .. kv0+127) of one (batch, head); it loops over the
-// query tiles.  TMEM lane j = key row j.  Per query tile i:
-//   S^T  = Kc . Qc_i^T          (M=128 keys, N=128 queries, K=cube_m)   TMEM [0,128)
+// query tiles.  TMEM lane j = key row j.  Per query tile i (each product per query half
+// h = 0, 1 where it depends on one half, see below):
+//   S^T  = Kc . Qc_i^T          (M=128 keys, N=64 queries per half, K=cube_m)  TMEM [0,128)
 //       (centered query codes: S = k.q - cb_j/2)
-//   dP^T = V . dO_i^T           (K=head_dim)                              TMEM [128,256)
+//   dP^T = V . dO_i^T           (K=head_dim, N=64 per half)                  TMEM [P_SEP ? 192 : 128, +128)
 //   softmax warps: P^T = 2^(2*scale*log2e*S - cb'_j - L_i), L = lse + qb' (recompute
-//       from lse as attention.cu:351-368 does), written back as fp16 into the S columns;
+//       from lse as attention.cu:351-368 does), written back as fp16 into TMEM (own columns
+//       where they fit, else over S);
 //       dS^T = P^T (dP^T - delta_i) (attention.cu:409-421), fp16 into the dP columns and
-//       into a 128B-swizzled shared buffer; dcb_j += sum_i dS (attention.cu:430-437).
+//       into a 128B-swizzled shared dS tile; dcb_j += sum_i dS (attention.cu:430-437).
 //   dV += P^T . dO_i            (A = P^T from TMEM)                       TMEM [256, +hd)
 //   dK += dS^T . Qc_i           (A = dS^T from TMEM, B = Qc MN-major)      TMEM [.., +m)
 //       (centered codes: this is dk + gate_q * dcb, whose cancelling bias term is exact)
@@ -17,13 +19,19 @@
 //       warp stages its 32 rows in the shared dS tile, free between the dQ MMA and the next
 //       dS, and issues one bulk tensor reduce per 32-column box; scattered per-thread global
 //       reductions contended with the tensor core's shared-memory operand reads)
+// The two softmax warpgroups (query halves h = 0, 1 of each tile) run as two pipelines half a
+// tile apart, so that on every SM sub-partition one warpgroup's exponentials overlap the other's
+// dS phase: every MMA that depends on one half is issued per half (S_h and dP_h as N = 64, dV_h
+// and dK_h as K = 64; dQ whole, once both halves of dS are in shared memory), with per-half
+// barriers, by one warp-converged MMA warp in a fixed interleaved order (see the issuer).  Where
+// shared memory allows, the dS tile is double-buffered, so neither half waits for the other's dQ.
 // Scale factors: dL/dS_raw = 2*scale*dS and dL/dcbias = -scale*sum_i dS (attention.cu:425,
 // :436, :442).  Unlike the reference there are no fp16 global atomics: dV and dK are
 // complete per CTA and stored once; only dq is accumulated, in fp32.
 //
 // Warps (512 threads, four warpgroups): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer (warps 2-3 idle), warps 4..7 softmax for queries [0,64) of the tile, 8..11 softmax
-// for queries [64,128), 12..15 dQ epilogue.  setmaxnreg moves registers from the producer
+// issuer (warps 2-3 idle), warps 4..7 softmax for queries [0,64) of the tile (half 0), 8..11
+// softmax for queries [64,128) (half 1), 12..15 dQ epilogue.  setmaxnreg moves registers from the producer
 // and dQ warpgroups to the two softmax warpgroups.
 #include "kernels.h"
 #include "sm100.cuh"
