@@ -140,7 +140,7 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int ks) {
     return make_sdesc(addr, 16, 8 * ROW_BYTES, sw);
 }
 
-template <int MC, int HD, bool CAUSAL>
+template <int MC, int HD, bool CAUSAL, bool SPLIT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmKD,
@@ -327,6 +327,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                           kmajor_desc<32>(augbuf(it) + 64 * h * 32, 0), id_h, 1u);
                 umma_commit_w(dp_full(h));
             };
+            // Lockstep mode: S and dP of both halves as one N = 128 product each, every per-half
+            // barrier of the pair committed
+            constexpr uint32_t id_full = make_idesc_f16(128, 128, false, false);
+            auto issue_s_all = [&](int it) {
+                const uint32_t sQ = qbuf(it);
+#pragma unroll
+                for (int ks = 0; ks < MC / 16; ++ks)
+                    umma_ss_w(tmem + Cfg::TM_S, kmajor_desc<Cfg::KC_ROW>(sK, ks), kmajor_desc<Cfg::KC_ROW>(sQ, ks),
+                              id_full, ks > 0 ? 1u : 0u);
+                umma_commit_w(s_full(0));
+                umma_commit_w(s_full(1));
+            };
+            auto issue_dp_all = [&](int it) {
+                const uint32_t sDO = dobuf(it);
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ++ks)
+                    umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<Cfg::V_ROW>(sV, ks), kmajor_desc<Cfg::V_ROW>(sDO, ks),
+                              id_full, ks > 0 ? 1u : 0u);
+                umma_ss_w(tmem + Cfg::TM_DP, kmajor_desc<32>(sVaug, 0), kmajor_desc<32>(augbuf(it), 0), id_full, 1u);
+                umma_commit_w(dp_full(0));
+                umma_commit_w(dp_full(1));
+            };
             // dV += P_h^T . dO_h   (P^T of query half h in columns p_col(h) .. +32)
             auto issue_dv = [&](int it, int h) {
                 const uint32_t sDO = dobuf(it);
@@ -391,14 +413,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             bool ok = wait(kv_full, 0, 3);
             if (ok && n_it > 0) {
                 ok = wait(q_full0, 0, 4);
-                if (ok) {
+                if (ok && SPLIT) {
                     issue_s(0, 0);
                     issue_s(0, 1);
                     issue_dp(0, 0);
                     issue_dp(0, 1);
+                } else if (ok) {
+                    issue_s_all(0);
+                    issue_dp_all(0);
                 }
             }
-            for (int it = 0; ok && it <= n_it; ++it) {
+            // Lockstep mode (few query tiles per CTA, or one dS tile, where the halves would not
+            // stay apart): per tile i, S_{i+1} once both halves hold S_i, dV_i once both P halves
+            // are in TMEM, then dK_i, dQ_i and dP_{i+1} once both dS halves are written.
+            for (int it = 0; !SPLIT && ok && it < n_it; ++it) {
+                const bool nxt = it + 1 < n_it;
+                if (Cfg::P_SEP && nxt) {
+                    if (!(ok = wait(s_free(0), it, 15) && wait(s_free(1), it, 15) && stage_landed(it + 1))) break;
+                    issue_s_all(it + 1);
+                }
+                if (!(ok = wait(p_full(0), it, 5) && wait(p_full(1), it, 5))) break;
+                issue_dv(it, 0);
+                issue_dv(it, 1);
+                if (!Cfg::P_SEP && nxt) {
+                    if (!(ok = stage_landed(it + 1))) break;
+                    issue_s_all(it + 1);
+                }
+                if (!(ok = wait(ds_full(0), it, 6) && wait(ds_full(1), it, 6))) break;
+                issue_dk(it, 0);
+                issue_dk(it, 1);
+                if (Cfg::DS2 && it >= 1 && !(ok = wait(dq_free((it - 1) % 2), (it - 1) / 2, 19))) break;
+                issue_dq(it);
+                if (nxt) issue_dp_all(it + 1);
+            }
+            for (int it = 0; SPLIT && ok && it <= n_it; ++it) {
                 const bool cur = it < n_it, nxt = it + 1 < n_it, prev = it > 0;
                 if (prev) {  // A
                     if (!(ok = wait(p_full(1), it - 1, 5))) break;
@@ -462,7 +510,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bool ok = true;
         // half 1 starts half a tile behind half 0 (once half 0 has its first P), so that the two
         // warpgroups' exponential and dS phases alternate on every sub-partition
-        if (wg == 1 && n_it > 1 && !mbar_wait_warp(p_full(0), 0, args.status, K_ATTN_BWD, 18)) ok = false;
+        if (SPLIT && wg == 1 && n_it > 1 && !mbar_wait_warp(p_full(0), 0, args.status, K_ATTN_BWD, 18)) ok = false;
         for (int it = 0; ok && it < n_it; ++it) {
             const int s = it % kQStages;
             const int q0 = (i_begin + it) * kTile;
@@ -724,7 +772,11 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     a.dcb = io.dcb;
     a.dq = io.dq;
     a.status = dev.status;
-    auto kern = attn_bwd_kernel<MC, HD, CAUSAL>;
+    // The half-tile pipelines pay for their split MMAs only where the halves stay apart: with two
+    // dS tiles and enough query tiles per CTA to amortise the offset start; else lockstep.
+    constexpr int kSplitMinTiles = 16;
+    const bool split = Cfg::DS2 && a.n_qtiles >= kSplitMinTiles;
+    auto kern = split ? attn_bwd_kernel<MC, HD, CAUSAL, true> : attn_bwd_kernel<MC, HD, CAUSAL, false>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     dim3 grid(a.n_qtiles, BH);
     prof_begin(stream, "attn_bwd");

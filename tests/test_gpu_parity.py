@@ -4,7 +4,10 @@ every gradient.
 
 Cases cover each supported (cube_m, head_dim) pair, causal and non-causal, sequence
 lengths that are not a multiple of the 128-row tile (197, 1, 15, 129), a single tile,
-random gates, random grad_out, and both gradient modes.
+random gates, random grad_out, and both gradient modes.  The LONG cases have at least 16
+query tiles, where the backward kernel runs its two softmax warpgroups half a tile apart
+(every head shape whose shared-memory budget holds two dS tiles), causal ones included so
+that the last key tiles see one or two query tiles.
 """
 
 import pytest
@@ -30,6 +33,15 @@ SMALL = [
     MorphoConfig("hd32_m64", 1, 129, 128, 4, 64, 1.0, False, 10),      # hd 32 with m 64
 ]
 
+LONG = [
+    MorphoConfig("long_m16_hd64_causal", 1, 2100, 128, 2, 16, 1.0, True, 11),   # ragged last tile
+    MorphoConfig("long_m32_hd64", 1, 2048, 128, 2, 32, 0.5, False, 12),         # c3 head shape
+    MorphoConfig("long_m64_hd64_causal", 1, 2200, 128, 2, 64, 1.0, True, 13),
+    MorphoConfig("long_m16_hd128", 1, 2049, 128, 1, 16, 1.0, False, 14),        # one row past 16 tiles
+    MorphoConfig("long_m32_hd32_causal", 2, 2304, 64, 2, 32, 0.7, True, 15),
+    MorphoConfig("long_m64_hd128_causal", 1, 2048, 256, 2, 64, 1.0, True, 16),  # one dS tile: lockstep
+]
+
 
 @pytest.mark.parametrize("cfg", SMALL, ids=lambda c: c.name)
 @pytest.mark.parametrize("random_gates", [False, True], ids=["gates1", "gatesR"])
@@ -38,6 +50,15 @@ def test_parity_small(cuda, cfg, random_gates):
     g = inp.pop("grad_out", None)
     ours = run_cuda(cfg, inp, grad_out=g)
     ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_out=None if g is None else g.cpu())
+    compare(ours, ref, tol_gate=gate_tolerance(cfg))
+
+
+@pytest.mark.parametrize("cfg", LONG, ids=lambda c: c.name)
+def test_parity_long(cuda, cfg):
+    inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
+    g = inp.pop("grad_out")
+    ours = run_cuda(cfg, inp, grad_out=g)
+    ref = run_oracle(cfg, {k: v.cpu() for k, v in inp.items()}, grad_out=g.cpu())
     compare(ours, ref, tol_gate=gate_tolerance(cfg))
 
 
