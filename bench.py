@@ -319,16 +319,21 @@ def dp_leg(args, world, rank, dev, barrier):
     lse = torch.empty(cfg.B * cfg.H, cfg.N, dtype=torch.float32, device=dev)
     grads = [torch.empty_like(t) for t in args5[1:]]  # W_phi, gate_q, gate_k, W_V
     saved = torch.empty(capi.saved_bytes(p), dtype=torch.uint8, device=dev)
-    bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev)
+    n_bucket = capi.weight_grad_elems(p)
+    exchange = dp.peer_exchange(n_bucket, device=dev) if world > 1 else None
+    own_bucket = torch.empty(n_bucket, dtype=torch.float32, device=dev) if exchange is None else None
     timing = []
 
     def step(rec=None):
+        """One training step; returns the bucket that holds the all-reduced sum (world > 1)."""
         capi.forward_save(p, *args5, out, lse, saved=saved)
         if world > 1:
+            b = exchange.bucket() if exchange is not None else own_bucket
             dp.backward_allreduce(p, grad, saved, *args5, out, lse, dX, grads[0], grads[1], grads[2], grads[3],
-                                  bucket, timing=rec)
-        else:
-            capi.backward_saved(p, grad, saved, *args5, out, lse, dX, grads[0], grads[1], grads[2], grads[3])
+                                  b, timing=rec, exchange=exchange)
+            return b
+        capi.backward_saved(p, grad, saved, *args5, out, lse, dX, grads[0], grads[1], grads[2], grads[3])
+        return None
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -354,21 +359,25 @@ def dp_leg(args, world, rank, dev, barrier):
     ms_step = float(ms.item()) / steps
     check = None
     if world > 1:
-        step()  # bucket = the sum over ranks
-        local = torch.empty_like(bucket)
+        bucket = step()  # the sum over ranks
+        torch.cuda.synchronize()
+        local = torch.empty(n_bucket, dtype=torch.float32, device=dev)
         capi.forward_save(p, *args5, out, lse, saved=saved)
         capi.backward_saved(p, grad, saved, *args5, out, lse, dX, None, None, None, None, dweights_f32=local)
         parts = [torch.empty_like(local) for _ in range(world)]
         dist.all_gather(parts, local)
         want = torch.stack(parts).double().sum(0)
         check = {"rel_l2": float((bucket.double() - want).norm() / want.norm()),
-                 "what": "all-reduced fp32 bucket vs the fp64 sum of every rank's unreduced bucket (all-gathered)",
-                 "bucket_elems": bucket.numel()}
-        del parts, want, local
+                 "what": "all-reduced fp32 bucket vs the fp64 sum of every rank's unreduced bucket (all-gathered; "
+                         "recomputed, so it differs from the step's own in the last bits: dq is accumulated by "
+                         "TMA reduce-adds in no fixed order)",
+                 "bucket_elems": n_bucket}
+        del parts, want, local, bucket
     peaks = _peaks()
     tokens = cfg.tokens * world
     res = {"workload": "c5_dp: causal MorphoAttention layer, per rank B=8, N=8192, D=2048, H=16, cube_m=64, "
-                       "scale 1.0; fwd + backward(out.sum()), weight-gradient bucket all-reduced (NCCL)",
+                       "scale 1.0; fwd + backward(out.sum()), weight-gradient bucket all-reduced "
+                       + ("(peer-memory kernel over NVLink)" if exchange is not None else "(NCCL)"),
            "B_per_gpu": cfg.B, "global_batch": cfg.B * world, "n_gpus": world, "steps": steps,
            "ms_per_step": ms_step, "value": tokens / (ms_step / 1000.0), "unit": UNIT, "scaling": "weak",
            "timing": "CUDA events around the steps on each rank, max over ranks",
@@ -376,8 +385,8 @@ def dp_leg(args, world, rank, dev, barrier):
            / (ms_step / 1000.0),
            "per_rank_ms_per_step": [float(t[0]) for t in gathered],
            "allreduce_ms_per_rank": [float(t[1]) for t in gathered] if world > 1 else None,
-           "allreduce_bytes": bucket.numel() * 4 if world > 1 else 0, "dp_check": check}
-    del x, out, dX, grad, saved, bucket, grads, args5
+           "allreduce_bytes": n_bucket * 4 if world > 1 else 0, "dp_check": check}
+    del x, out, dX, grad, saved, own_bucket, grads, args5
     torch.cuda.empty_cache()
     return res
 
@@ -419,7 +428,11 @@ def run_ours(args):
     dX = torch.empty_like(x)
     dW_phi, dW_V = torch.empty_like(W_phi), torch.empty_like(W_V)
     dgq, dgk = torch.empty_like(gq), torch.empty_like(gk)
-    bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev) if world > 1 else None
+    # data parallel: the peer-memory all-reduce where the GPUs allow it (else NCCL)
+    exchange = dp.peer_exchange(capi.weight_grad_elems(p), device=dev) if world > 1 else None
+    bucket = None
+    if world > 1 and exchange is None:
+        bucket = torch.empty(capi.weight_grad_elems(p), dtype=torch.float32, device=dev)
 
     # the training pair: the forward keeps its projection for the backward (as the
     # module's autograd Function does)
@@ -430,8 +443,9 @@ def run_ours(args):
     def step(rec=None):
         capi.forward_save(p, x, W_phi, gq, gk, W_V, out, lse, saved=saved)
         if world > 1:  # weight-gradient all-reduce overlapped with the dX GEMM
+            b = exchange.bucket() if exchange is not None else bucket
             dp.backward_allreduce(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V,
-                                  bucket, timing=rec)
+                                  b, timing=rec, exchange=exchange)
         else:
             capi.backward_saved(p, grad, saved, x, W_phi, gq, gk, W_V, out, lse, dX, dW_phi, dgq, dgk, dW_V)
 
@@ -475,7 +489,9 @@ def run_ours(args):
                           dtype=torch.float64)
         ars = [torch.empty_like(ar) for _ in range(world)]
         dist.all_gather(ars, ar)
-        allreduce = {"ms_per_rank": [float(t.item()) for t in ars], "bytes": bucket.numel() * 4,
+        allreduce = {"ms_per_rank": [float(t.item()) for t in ars], "bytes": capi.weight_grad_elems(p) * 4,
+                     "collective": "peer_allreduce kernel (NVLink peer loads, fused fp16 finalize)"
+                     if exchange is not None else "NCCL all_reduce + finalize kernel",
                      "nccl_max_nchannels": os.environ.get("NCCL_MAX_NCHANNELS"),
                      "timing": "CUDA events around each step's all-reduce on the communication stream"}
     prof_live = capi.profile_collect()
@@ -583,6 +599,7 @@ def run_ours(args):
 
     if rank != 0:
         if world > 1:
+            dp.close_exchanges()
             dist.destroy_process_group()
         return
 
@@ -633,6 +650,7 @@ def run_ours(args):
         line["cpu_baseline"] = None
     print(json.dumps(line), flush=True)
     if world > 1:
+        dp.close_exchanges()
         dist.destroy_process_group()
 
 

@@ -43,6 +43,7 @@ extern "C" {
 #define MORPHO_ERR_WORKSPACE 3 /* workspace_bytes smaller than the *_workspace_size() answer */
 #define MORPHO_ERR_DEVICE 4    /* current device is not sm_100 */
 #define MORPHO_ERR_TIMEOUT 5   /* a kernel's bounded wait expired (see morpho_sm100_device_status) */
+#define MORPHO_ERR_UNSUPPORTED 6 /* not available between these GPUs (e.g. no peer access) */
 
 /* Hypercube projection phi = proj(z), z = X @ W_phi (reference morfology/cube.cuh:10-45, a
  * compile-time choice there, a run-time field here). */
@@ -183,6 +184,36 @@ MORPHO_API size_t morpho_sm100_weight_grad_elems(const morpho_problem_t* p);
  * data-parallel path. */
 MORPHO_API int morpho_sm100_finalize_weight_grads(const morpho_problem_t* p, const float* dweights_f32, float alpha,
                                        void* dW_phi, void* d_gate_q, void* d_gate_k, void* dW_V, void* stream);
+
+/* Peer-memory all-reduce of the data-parallel bucket, fused with the finalize (no reference
+ * counterpart: the reference has no multi-GPU code).  One process per GPU of one node, every
+ * pair of GPUs with peer access.  Each rank creates a group (its exchange region: a signal
+ * block and two buckets of bucket_elems fp32, zero-filled, in its own device memory, exported
+ * as a CUDA IPC handle of MORPHO_PEER_HANDLE_BYTES and identified by its GPU's PCI bus id, a
+ * string of at most MORPHO_PEER_PCI_ID_BYTES), the caller exchanges the handles and ids between
+ * the ranks (in rank order, world entries each) and every rank connects.  Per step: the
+ * backward writes morpho_sm100_peer_bucket(g) -- the bucket of the next all-reduce, alternating
+ * between the two -- then morpho_sm100_peer_allreduce_finalize enqueues ONE kernel on `stream`
+ * that sums the ranks' buckets over NVLink (reduce-scatter, then all-gather, each rank summing
+ * in rank order 0..world-1, so every rank gets the same bits), leaves the sum in that bucket and
+ * writes the fp16 gradients alpha * sum, as morpho_sm100_finalize_weight_grads does.  Every rank
+ * must call it the same number of times, and its stream must have waited for the bucket to be
+ * complete.  The kernel needs no SM of its own (no shared memory): it runs beside a concurrent
+ * kernel such as the dX GEMM.  Its waits for the other ranks are bounded (1 s); on expiry it
+ * records MORPHO_ERR_TIMEOUT in the device status word and the group must be destroyed.
+ * Destroy only when no rank can still be in an all-reduce (after a barrier).  connect returns
+ * MORPHO_ERR_UNSUPPORTED when a peer's GPU is not visible or not peer-accessible (use NCCL). */
+#define MORPHO_PEER_HANDLE_BYTES 64
+#define MORPHO_PEER_PCI_ID_BYTES 32
+typedef struct morpho_peer_group morpho_peer_group_t;
+MORPHO_API int morpho_sm100_peer_create(int32_t rank, int32_t world, int64_t bucket_elems, void* handle_out,
+                                        char* pci_bus_id_out, morpho_peer_group_t** group);
+MORPHO_API int morpho_sm100_peer_connect(morpho_peer_group_t* group, const void* handles, const char* pci_bus_ids);
+MORPHO_API float* morpho_sm100_peer_bucket(const morpho_peer_group_t* group);
+MORPHO_API int morpho_sm100_peer_allreduce_finalize(morpho_peer_group_t* group, const morpho_problem_t* p,
+                                                    float alpha, void* dW_phi, void* d_gate_q, void* d_gate_k,
+                                                    void* dW_V, void* stream);
+MORPHO_API int morpho_sm100_peer_destroy(morpho_peer_group_t* group);
 
 /* Message of the last failure on the calling thread ("" if none). */
 MORPHO_API const char* morpho_sm100_last_error(void);

@@ -33,7 +33,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I" + INCLUDE]
-CU_SOURCES = ["host_common.cu", "gemm.cu", "attn_fwd.cu", "attn_bwd.cu", "softmorph.cu", "softmorph_tc.cu", "softmorph_tc_bwd.cu", "pointwise.cu", "capi.cu", "noalloc.cu", "selftest.cu", "score_probe.cu"]
+CU_SOURCES = ["host_common.cu", "gemm.cu", "attn_fwd.cu", "attn_bwd.cu", "softmorph.cu", "softmorph_tc.cu", "softmorph_tc_bwd.cu", "pointwise.cu", "capi.cu", "noalloc.cu", "selftest.cu", "score_probe.cu", "peer.cu"]
 
 
 def _headers():

@@ -19,6 +19,9 @@ MORPHO_ERR_CUDA = 2
 MORPHO_ERR_WORKSPACE = 3
 MORPHO_ERR_DEVICE = 4
 MORPHO_ERR_TIMEOUT = 5
+MORPHO_ERR_UNSUPPORTED = 6
+PEER_HANDLE_BYTES = 64
+PEER_PCI_ID_BYTES = 32
 MORPHO_GRAD_FULL = 0
 MORPHO_GRAD_REFERENCE = 1
 MORPHO_PROJ_SIGMOID = 0
@@ -54,6 +57,11 @@ EXPORTED = (
     "morpho_sm100_profile_collect",
     "morpho_sm100_profile_select",
     "morpho_sm100_score_probe_half2",
+    "morpho_sm100_peer_create",
+    "morpho_sm100_peer_connect",
+    "morpho_sm100_peer_bucket",
+    "morpho_sm100_peer_allreduce_finalize",
+    "morpho_sm100_peer_destroy",
 )
 
 
@@ -128,6 +136,17 @@ def lib() -> ctypes.CDLL:
     L.morpho_sm100_profile_collect.restype = i32
     L.morpho_sm100_score_probe_half2.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, vp, vp]
     L.morpho_sm100_score_probe_half2.restype = i32
+    L.morpho_sm100_peer_create.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, vp, ctypes.c_char_p,
+                                           ctypes.POINTER(vp)]
+    L.morpho_sm100_peer_create.restype = i32
+    L.morpho_sm100_peer_connect.argtypes = [vp, ctypes.c_char_p, ctypes.c_char_p]
+    L.morpho_sm100_peer_connect.restype = i32
+    L.morpho_sm100_peer_bucket.argtypes = [vp]
+    L.morpho_sm100_peer_bucket.restype = vp
+    L.morpho_sm100_peer_allreduce_finalize.argtypes = [vp, P, ctypes.c_float, vp, vp, vp, vp, vp]
+    L.morpho_sm100_peer_allreduce_finalize.restype = i32
+    L.morpho_sm100_peer_destroy.argtypes = [vp]
+    L.morpho_sm100_peer_destroy.restype = i32
     _lib = L
     return L
 
@@ -317,6 +336,45 @@ def profile_collect(max_kernels: int = 32) -> dict:
         nm = names.raw[i * name_len:(i + 1) * name_len].split(b"\0", 1)[0].decode()
         out[nm] = (float(ms[i]), int(cnt[i]))
     return out
+
+
+class _DeviceArray:
+    """A raw fp32 device buffer seen by torch through the CUDA array interface (no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2,
+                                         "strides": None, "stream": None}
+
+
+def peer_create(rank: int, world: int, bucket_elems: int):
+    """Create this rank's peer-exchange region; returns (group handle, IPC handle bytes, PCI bus id bytes)."""
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    pci = ctypes.create_string_buffer(PEER_PCI_ID_BYTES)
+    g = ctypes.c_void_p()
+    _check(lib().morpho_sm100_peer_create(rank, world, bucket_elems, h, pci, ctypes.byref(g)))
+    return g.value, h.raw, pci.raw
+
+
+def peer_connect(group: int, handles: list, pci_ids: list) -> None:
+    """Map every rank's region (``handles`` and ``pci_ids`` in rank order, as peer_create gave them)."""
+    _check(lib().morpho_sm100_peer_connect(group, b"".join(handles), b"".join(pci_ids)))
+
+
+def peer_bucket(group: int, n: int, device) -> torch.Tensor:
+    """The fp32 bucket of the group's next all-reduce as a tensor view (``n`` elements)."""
+    import torch
+    ptr = lib().morpho_sm100_peer_bucket(group)
+    return torch.as_tensor(_DeviceArray(ptr, n), device=device)
+
+
+def peer_allreduce_finalize(group: int, p: MorphoProblem, alpha: float, dW_phi, d_gate_q, d_gate_k, dW_V,
+                            stream=None) -> None:
+    _check(lib().morpho_sm100_peer_allreduce_finalize(group, ctypes.byref(p), alpha, _ptr(dW_phi), _ptr(d_gate_q),
+                                                      _ptr(d_gate_k), _ptr(dW_V), _stream(stream)))
+
+
+def peer_destroy(group: int) -> None:
+    _check(lib().morpho_sm100_peer_destroy(group))
 
 
 def score_probe_half2(qc, kc, rowmax, stream=None) -> None:

@@ -72,3 +72,75 @@ def test_dp_allreduce_equals_full_batch():
     for n, k in (("W_phi", "dW_phi"), ("W_V", "dW_V"), ("gate_q", "d_gate_q"), ("gate_k", "d_gate_k")):
         assert O.rel_l2(got[n], full[k]) < 1e-5, n
     assert got["tmax"] == float(world)
+
+
+def _peer_setup_worker(rank, world, port, q, mode):
+    """Peer-exchange set-up where it cannot work: every rank must give up together (the same
+    RuntimeError everywhere, no rank left waiting in an exchange round)."""
+    from morphottention_b200 import capi
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        destroyed = []
+        if mode == "rank1_fails":  # rank 0's region is created, rank 1's is not
+            def create(r, w, n):
+                if r == 1:
+                    raise capi.MorphoError(capi.MORPHO_ERR_CUDA, "fake: no device memory")
+                return 1234, b"h" * capi.PEER_HANDLE_BYTES, b"p" * capi.PEER_PCI_ID_BYTES
+            capi.peer_create = create
+            capi.peer_destroy = destroyed.append
+        elif mode == "connect_fails":  # both regions exist, rank 0 cannot map rank 1's
+            capi.peer_create = lambda r, w, n: (100 + r, b"h" * capi.PEER_HANDLE_BYTES, b"p" * capi.PEER_PCI_ID_BYTES)
+
+            def connect(g, handles, ids):
+                assert len(handles) == world and len(ids) == world
+                if g == 100:
+                    raise capi.MorphoError(capi.MORPHO_ERR_UNSUPPORTED, "fake: no peer access")
+            capi.peer_connect = connect
+            capi.peer_destroy = destroyed.append
+        err = None
+        try:
+            dp.PeerExchange(1000, device="cuda:0")
+        except RuntimeError as e:
+            err = str(e)
+        cached = dp.peer_exchange(1000, device="cuda:0")
+        dp.set_collective("nccl")
+        off = dp.peer_exchange(1000, device="cuda:0")
+        dp.set_collective("peer")
+        t = torch.ones(1)
+        dist.all_reduce(t)  # the ranks are still in step
+        q.put((rank, err, cached, off, t.item(), destroyed))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_setup_fails_on_every_rank_together():
+    world = 2
+    ctx = mp.get_context("spawn")
+    for mode in ("no_gpu", "rank1_fails", "connect_fails"):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_peer_setup_worker, args=(r, world, port, q, mode)) for r in range(world)]
+        for p in procs:
+            p.start()
+        got = sorted(q.get(timeout=120) for _ in range(world))
+        for p in procs:
+            p.join(timeout=60)
+        assert all(p.exitcode == 0 for p in procs), (mode, [p.exitcode for p in procs])
+        for rank, err, cached, off, total, destroyed in got:
+            assert err is not None and err.startswith("peer all-reduce unavailable"), (mode, rank, err)
+            assert cached is None and off is None, (mode, rank)
+            assert total == world, (mode, rank)
+            # two set-ups per rank (direct, then through the cache): each frees what it created
+            if mode == "rank1_fails":
+                assert destroyed == ([1234, 1234] if rank == 0 else []), (mode, rank, destroyed)
+            if mode == "connect_fails":
+                assert destroyed == [100 + rank] * 2, (mode, rank, destroyed)
+
+
+def test_set_collective_rejects_unknown_names():
+    import pytest
+    with pytest.raises(ValueError):
+        dp.set_collective("mpi")
+    assert dp.get_collective() == "peer"
