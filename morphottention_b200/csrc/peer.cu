@@ -122,6 +122,29 @@ __device__ __forceinline__ void emit(const PeerArgs& a, long long u, float4 v) {
     *reinterpret_cast<uint2*>(dst) = pk;
 }
 
+// Sum of unit u over the W buckets in rank order: all W loads are issued before the adds (W is a
+// compile-time constant where it can be: 2, 4, 8; 0 = the group's size at run time).
+template <int W>
+__device__ __forceinline__ float4 rank_order_sum(const PeerArgs& a, long long u) {
+    if constexpr (W > 0) {
+        float4 x[W];
+#pragma unroll
+        for (int r = 0; r < W; ++r) x[r] = __ldcg(reinterpret_cast<const float4*>(a.buf[r]) + u);
+        float4 s = x[0];
+#pragma unroll
+        for (int r = 1; r < W; ++r) s = make_float4(s.x + x[r].x, s.y + x[r].y, s.z + x[r].z, s.w + x[r].w);
+        return s;
+    } else {  // a load per step: few registers, so the kernel still fits beside the dX GEMM
+        float4 s = __ldcg(reinterpret_cast<const float4*>(a.buf[0]) + u);
+        for (int r = 1; r < a.world; ++r) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(a.buf[r]) + u);
+            s = make_float4(s.x + x.x, s.y + x.y, s.z + x.z, s.w + x.w);
+        }
+        return s;
+    }
+}
+
+template <int W>
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const PeerArgs a) {
     // A: this rank's bucket is complete (stream order); publish, then wait for every rank's
     if (blockIdx.x == 0) publish(a, kReadyOff);
@@ -131,18 +154,15 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const Peer
     const long long c0 = static_cast<long long>(a.rank) * a.chunk4;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < a.chunk4; i += 2 * stride) {
-        const long long u0 = c0 + i, u1 = c0 + i + stride;
         const bool has1 = i + stride < a.chunk4;
-        float4 s0 = __ldcg(reinterpret_cast<const float4*>(a.buf[0]) + u0);
-        float4 s1 = has1 ? __ldcg(reinterpret_cast<const float4*>(a.buf[0]) + u1) : make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 1; r < a.world; ++r) {
-            const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a.buf[r]) + u0);
-            const float4 x1 = has1 ? __ldcg(reinterpret_cast<const float4*>(a.buf[r]) + u1) : s1;
-            s0 = make_float4(s0.x + x0.x, s0.y + x0.y, s0.z + x0.z, s0.w + x0.w);
-            if (has1) s1 = make_float4(s1.x + x1.x, s1.y + x1.y, s1.z + x1.z, s1.w + x1.w);
+        const float4 s0 = rank_order_sum<W>(a, c0 + i);
+        if (has1) {
+            const float4 s1 = rank_order_sum<W>(a, c0 + i + stride);
+            emit(a, c0 + i, s0);
+            emit(a, c0 + i + stride, s1);
+        } else {
+            emit(a, c0 + i, s0);
         }
-        emit(a, u0, s0);
-        if (has1) emit(a, u1, s1);
     }
     // the last CTA to finish its part publishes "chunk done" (every CTA's stores are ordered
     // before its counter increment by a system-scope fence)
@@ -159,20 +179,27 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const Peer
     __syncthreads();
     if (last) publish(a, kDoneOff);
 
-    // C: gather the other ranks' reduced chunks
+    // C: gather the other ranks' reduced chunks: one flat index space over the W - 1 chunks,
+    // four units per thread per pass with their loads in flight together
     if (!wait_slots(a, kDoneOff, 2)) return;
-    for (int k = 1; k < a.world; ++k) {
-        const int r = (a.rank + k) % a.world;  // start at different peers on different ranks
-        const long long base = static_cast<long long>(r) * a.chunk4;
-        const float4* src = reinterpret_cast<const float4*>(a.buf[r]);
-        for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < a.chunk4;
-             i += 2 * stride) {
-            const bool has1 = i + stride < a.chunk4;
-            const float4 x0 = __ldcg(src + base + i);
-            const float4 x1 = has1 ? __ldcg(src + base + i + stride) : x0;
-            emit(a, base + i, x0);
-            if (has1) emit(a, base + i + stride, x1);
+    const long long total = static_cast<long long>(a.world - 1) * a.chunk4;
+    for (long long j0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; j0 < total; j0 += 4 * stride) {
+        long long unit[4];
+        float4 v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const long long j = j0 + q * stride;
+            unit[q] = -1;
+            if (j < total) {
+                const long long k = j / a.chunk4;
+                const int r = static_cast<int>((a.rank + 1 + k) % a.world);  // peers in a rotated order
+                unit[q] = static_cast<long long>(r) * a.chunk4 + (j - k * a.chunk4);
+                v[q] = __ldcg(reinterpret_cast<const float4*>(a.buf[r]) + unit[q]);
+            }
         }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (unit[q] >= 0) emit(a, unit[q], v[q]);
     }
 }
 
@@ -316,7 +343,12 @@ extern "C" MORPHO_API int morpho_sm100_peer_allreduce_finalize(morpho_peer_group
     a.status = dev.status;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_arg);
     prof_begin(stream, "peer_allreduce");
-    peer_allreduce_kernel<<<kPeerCtas, kPeerThreads, 0, stream>>>(a);
+    switch (g->world) {
+        case 2: peer_allreduce_kernel<2><<<kPeerCtas, kPeerThreads, 0, stream>>>(a); break;
+        case 4: peer_allreduce_kernel<4><<<kPeerCtas, kPeerThreads, 0, stream>>>(a); break;
+        case 8: peer_allreduce_kernel<8><<<kPeerCtas, kPeerThreads, 0, stream>>>(a); break;
+        default: peer_allreduce_kernel<0><<<kPeerCtas, kPeerThreads, 0, stream>>>(a); break;
+    }
     MORPHO_LAUNCH_CHECK("peer_allreduce");
     g->epoch = e;
     return MORPHO_OK;
