@@ -34,6 +34,10 @@ constexpr int kGemmThreads = 320;  // producer, MMA, 8 epilogue warps
 
 enum BMode : int { B_SINGLE = 0, B_SPLIT_N = 1, B_SPLIT_K = 2 };
 
+// Epilogue staging: 4 KB of shared memory per epilogue warp (32 rows of up to 128 bytes), through
+// which each warp turns its row-per-lane results into coalesced global stores (store_rows32).
+constexpr int kEpiStageBytes = 4096;
+
 template <int BN>
 struct GemmCfg {
     static constexpr int A_BYTES = BM * BK * 2;
@@ -41,7 +45,10 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);  // <= 192 KB of ring
     static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
-    static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024;  // barriers + 1 KB alignment slack
+    static constexpr int EPI_OFFSET = BAR_OFFSET + 256;
+    // ring + barriers + 8 epilogue staging buffers + 1 KB alignment slack
+    static constexpr int SMEM_BYTES = EPI_OFFSET + 8 * kEpiStageBytes + 1024;
+    static_assert(SMEM_BYTES <= 232448, "smem budget");
     static constexpr uint32_t TMEM_COLS = 2 * BN;                 // double-buffered accumulator
     static_assert(TMEM_COLS <= 512, "TMEM");
 };
@@ -96,10 +103,14 @@ template <int MC>
 struct EpiProj {
     using Params = ProjParams;
     template <int BN>
-    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/) {
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/, uint32_t stage, int lane) {
         const bool live = row < p.T;
         const int b = live ? row / p.N : 0;
         const int n = live ? row - b * p.N : 0;
+        // the warp's 32 rows are consecutive tokens of one sequence: coalesced stores through the
+        // staging buffer (warp-uniform), else each lane stores its own row
+        const int r0 = row - lane;
+        const bool coal = r0 + 31 < p.T && r0 / p.N == (r0 + 31) / p.N;
         if (n0 < p.Hp) {
 #pragma unroll 1
             for (int hc = 0; hc < BN / MC; ++hc) {
@@ -136,7 +147,28 @@ struct EpiProj {
                         hpk[c / 2] = *reinterpret_cast<const uint32_t*>(&hi);
                         lpk[c / 2] = pack_half2(c0 - hf.x, c1 - hf.y);
                     }
-                    if (live) {
+                    if (coal) {
+                        const size_t b0 = base - lane;
+                        auto u4 = [](const uint32_t* a, int g) { return make_uint4(a[4 * g], a[4 * g + 1], a[4 * g + 2], a[4 * g + 3]); };
+                        store_rows32<CW * 2>(stage, lane, [&](int g) { return u4(qpk, g); },
+                                             reinterpret_cast<uint8_t*>(p.o.qc + b0 * MC + q * CW), MC * 2);
+                        store_rows32<CW * 2>(stage, lane, [&](int g) { return u4(kpk, g); },
+                                             reinterpret_cast<uint8_t*>(p.o.kc + b0 * MC + q * CW), MC * 2);
+                        if (p.o.kdq != nullptr) {
+                            store_rows32<CW * 2>(stage, lane, [&](int g) { return u4(hpk, g); },
+                                                 reinterpret_cast<uint8_t*>(p.o.kdq + b0 * (2 * MC) + q * CW), MC * 4);
+                            store_rows32<CW * 2>(stage, lane, [&](int g) { return u4(lpk, g); },
+                                                 reinterpret_cast<uint8_t*>(p.o.kdq + b0 * (2 * MC) + MC + q * CW),
+                                                 MC * 4);
+                        }
+                        if (p.o.phi != nullptr)
+                            store_rows32<CW * 4>(stage, lane,
+                                                 [&](int g) {
+                                                     return make_uint4(__float_as_uint(zr[4 * g]), __float_as_uint(zr[4 * g + 1]),
+                                                                       __float_as_uint(zr[4 * g + 2]), __float_as_uint(zr[4 * g + 3]));
+                                                 },
+                                                 reinterpret_cast<uint8_t*>(p.o.phi + b0 * MC + q * CW), MC * 4);
+                    } else if (live) {
                         uint4* dq = reinterpret_cast<uint4*>(p.o.qc + base * MC + q * CW);
                         uint4* dk = reinterpret_cast<uint4*>(p.o.kc + base * MC + q * CW);
 #pragma unroll
@@ -178,7 +210,19 @@ struct EpiProj {
                 if (g >= p.D) break;
                 const uint32_t* r = rb[cc & 1];
                 if (cc + 1 < BN / 32 && g + 32 < p.D) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
-                if (live) {
+                if (coal) {
+                    const int h = g / p.hd;
+                    const int e = g - h * p.hd;
+                    const size_t b0 = static_cast<size_t>(b * p.H + h) * p.N + n - lane;
+                    store_rows32<64>(stage, lane,
+                                     [&](int i) {
+                                         return make_uint4(pack_half2(u2f(r[8 * i]), u2f(r[8 * i + 1])),
+                                                           pack_half2(u2f(r[8 * i + 2]), u2f(r[8 * i + 3])),
+                                                           pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
+                                                           pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
+                                     },
+                                     reinterpret_cast<uint8_t*>(p.o.v + b0 * p.hd + e), static_cast<size_t>(p.hd) * 2);
+                } else if (live) {
                     const int h = g / p.hd;
                     const int e = g - h * p.hd;
                     uint4* dv = reinterpret_cast<uint4*>(p.o.v + (static_cast<size_t>(b * p.H + h) * p.N + n) * p.hd + e);
@@ -203,7 +247,8 @@ struct HalfParams {
 struct EpiHalf {
     using Params = HalfParams;
     template <int BN>
-    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/) {
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/, uint32_t stage, int lane) {
+        const bool coal = row - lane + 31 < p.M;  // warp-uniform: all 32 rows exist
         // the next 32-column chunk's TMEM load is in flight while this one is stored
         uint32_t rb[2][32];
         tmem_ld32(tacc, rb[0]);
@@ -214,7 +259,17 @@ struct EpiHalf {
             if (col >= p.N) break;
             const uint32_t* r = rb[cc & 1];
             if (cc + 1 < BN / 32 && col + 32 < p.N) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
-            if (row < p.M) {
+            if (coal) {
+                store_rows32<64>(stage, lane,
+                                 [&](int i) {
+                                     return make_uint4(pack_half2(u2f(r[8 * i]), u2f(r[8 * i + 1])),
+                                                       pack_half2(u2f(r[8 * i + 2]), u2f(r[8 * i + 3])),
+                                                       pack_half2(u2f(r[8 * i + 4]), u2f(r[8 * i + 5])),
+                                                       pack_half2(u2f(r[8 * i + 6]), u2f(r[8 * i + 7])));
+                                 },
+                                 reinterpret_cast<uint8_t*>(p.out + static_cast<size_t>(row - lane) * p.ld + col),
+                                 static_cast<size_t>(p.ld) * 2);
+            } else if (row < p.M) {
                 uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ld + col);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
@@ -236,7 +291,8 @@ struct F32Params {
 struct EpiF32 {
     using Params = F32Params;
     template <int BN>
-    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int z) {
+    __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int z, uint32_t stage, int lane) {
+        const bool coal = row - lane + 31 < p.M;  // warp-uniform: all 32 rows exist
         // the next 32-column chunk's TMEM load is in flight while this one is stored
         uint32_t rb[2][32];
         tmem_ld32(tacc, rb[0]);
@@ -247,7 +303,12 @@ struct EpiF32 {
             if (col >= p.N) break;
             const uint32_t* r = rb[cc & 1];
             if (cc + 1 < BN / 32 && col + 32 < p.N) tmem_ld32(tacc + (cc + 1) * 32, rb[(cc + 1) & 1]);
-            if (row < p.M) {
+            if (coal) {
+                store_rows32<128>(stage, lane,
+                                  [&](int i) { return make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]); },
+                                  reinterpret_cast<uint8_t*>(p.out + (static_cast<size_t>(z) * p.M + row - lane) * p.ld + col),
+                                  static_cast<size_t>(p.ld) * 4);
+            } else if (row < p.M) {
                 float4* dst = reinterpret_cast<float4*>(p.out + (static_cast<size_t>(z) * p.M + row) * p.ld + col);
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
@@ -380,7 +441,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // The whole warp runs this loop (warp-uniform control flow and descriptor arithmetic);
+        // elect.sync inside umma_ss_w / umma_commit_w lets one lane issue each instruction, so the
+        // issuer is not a divergent lane beside the epilogue warps of its sub-partition.
+        {
             constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN);
             bool ok = true;
             int g = 0;  // K blocks consumed so far
@@ -392,7 +456,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int nkb = min(args.k_blocks, kb0 + args.kb_per_split) - kb0;
                 const int a = j & 1;
                 // the epilogue warps have drained this buffer (its previous use, item j - 2)
-                if (j >= 2 && !mbar_wait(acc_empty0 + 8 * a, ((j >> 1) & 1) ^ 1, args.status, K_GEMM, 6)) {
+                if (j >= 2 && !mbar_wait_warp(acc_empty0 + 8 * a, ((j >> 1) & 1) ^ 1, args.status, K_GEMM, 6)) {
                     ok = false;
                     break;
                 }
@@ -400,7 +464,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint32_t dacc = tmem + a * BN;
                 for (int i = 0; i < nkb; ++i, ++g) {
                     const int s = g % STAGES;
-                    if (!mbar_wait(full0 + 8 * s, (g / STAGES) & 1, args.status, K_GEMM, 3)) {
+                    if (!mbar_wait_warp(full0 + 8 * s, (g / STAGES) & 1, args.status, K_GEMM, 3)) {
                         ok = false;
                         break;
                     }
@@ -413,19 +477,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                                  : make_sdesc(sA + ks * 32, 16, 1024, SW_128);
                         const uint64_t bd = B_MN ? make_sdesc(sB + ks * 2048, 64 * 128, 1024, SW_128)
                                                  : make_sdesc(sB + ks * 32, 16, 1024, SW_128);
-                        umma_ss(dacc, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+                        umma_ss_w(dacc, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
                     }
-                    umma_commit(empty0 + 8 * s);
+                    umma_commit_w(empty0 + 8 * s);
                 }
-                if (ok) umma_commit(acc_full0 + 8 * a);
+                if (ok) umma_commit_w(acc_full0 + 8 * a);
             }
             if (!ok) {
                 *abort_flag = 1u;
-                umma_commit(drain_bar);
-                mbar_wait(drain_bar, 0, args.status, K_GEMM, 4);
+                umma_commit_w(drain_bar);
+                mbar_wait_warp(drain_bar, 0, args.status, K_GEMM, 4);
                 // release the epilogue warps' next wait on either buffer
-                umma_commit(acc_full0);
-                umma_commit(acc_full0 + 8);
+                umma_commit_w(acc_full0);
+                umma_commit_w(acc_full0 + 8);
             }
         }
     } else if (warp - 2 < kEpiWarps) {
@@ -433,6 +497,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quad = warp & 3;
         const int half = (warp - 2) >> 2;  // column half of the tile
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        const uint32_t estage = smem_u32(smem + Cfg::EPI_OFFSET + (warp - 2) * kEpiStageBytes);
         int j = 0;
         for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++j) {
             int m0, n0, z;
@@ -444,7 +509,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             Epi::template run<kEpiCols>(ep, tmem + a * BN + half * kEpiCols + lane_off, m0 + quad * 32 + lane,
-                                        n0 + half * kEpiCols, z);
+                                        n0 + half * kEpiCols, z, estage, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty0 + 8 * a);

@@ -151,6 +151,43 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
                  : "memory");
 }
 
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Warp-cooperative store of a block of 32 rows of RB bytes (RB = 32, 64 or 128; lane r holds row
+// r, granule g (16 bytes) given by get(g)); row r goes to dst + r * pitch (16-byte aligned).  The
+// rows pass through this warp's shared staging buffer `stage` (32 * RB bytes), XOR-swizzled so
+// that both the row-wise writes and the transposed reads are free of bank conflicts, and each
+// global store instruction then writes 512 / RB rows' segments whole -- full 32-byte sectors, 512
+// contiguous bytes when pitch == RB -- instead of one 16-byte piece of each of 32 rows.
+template <int RB, class Get>
+__device__ __forceinline__ void store_rows32(uint32_t stage, int lane, Get get, uint8_t* dst, size_t pitch) {
+    static_assert(RB == 32 || RB == 64 || RB == 128, "row bytes");
+    constexpr int G = RB / 16;     // granules per row
+    constexpr int RPL = 128 / RB;  // rows per 128-byte bank line
+    auto phys = [](int r, int g) { return static_cast<uint32_t>(r * RB + ((g ^ ((r / RPL) & (G - 1))) << 4)); };
+#pragma unroll
+    for (int g = 0; g < G; ++g) st_shared_u4(stage + phys(lane, g), get(g));
+    __syncwarp();
+    constexpr int RPI = 32 / G;  // rows per store instruction
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+        const int r = i * RPI + lane / G, g = lane % G;
+        const uint4 x = ld_shared_u4(stage + phys(r, g));
+        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pitch + g * 16) = x;
+    }
+    __syncwarp();
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until this thread's committed bulk groups have read their shared-memory sources
