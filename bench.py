@@ -376,8 +376,10 @@ def dp_leg(args, world, rank, dev, barrier):
     peaks = _peaks()
     tokens = cfg.tokens * world
     res = {"workload": "c5_dp: causal MorphoAttention layer, per rank B=8, N=8192, D=2048, H=16, cube_m=64, "
-                       "scale 1.0; fwd + backward(out.sum()), weight-gradient bucket all-reduced "
-                       + ("(peer-memory kernel over NVLink)" if exchange is not None else "(NCCL)"),
+                       "scale 1.0; fwd + backward(out.sum()), "
+                       + ("weight-gradient bucket all-reduced (peer-memory kernel over NVLink)" if exchange is not None
+                          else "weight-gradient bucket all-reduced (NCCL)" if world > 1
+                          else "one GPU: no all-reduce"),
            "B_per_gpu": cfg.B, "global_batch": cfg.B * world, "n_gpus": world, "steps": steps,
            "ms_per_step": ms_step, "value": tokens / (ms_step / 1000.0), "unit": UNIT, "scaling": "weak",
            "timing": "CUDA events around the steps on each rank, max over ranks",
