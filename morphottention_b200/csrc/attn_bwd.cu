@@ -118,6 +118,7 @@ struct BwdCfg {
 
 struct BwdArgs {
     int N, Npad, H, D, Hp, Cp, n_qtiles;
+    int BH, band;   // causal launch order (causal_order)
     int mask_diag;  // also drop key j == query i
     float c2;     // 2 * scale * log2(e)
     float two_scale;
@@ -162,8 +163,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
-    const int kt = blockIdx.x;
-    const int bh = blockIdx.y;
+    int kt, bh;
+    if (CAUSAL) {  // key tile kt meets n_qtiles - kt query tiles: heaviest first
+        causal_order(static_cast<int>(blockIdx.x), args.n_qtiles, args.BH, args.band, kt, bh);
+    } else {
+        kt = static_cast<int>(blockIdx.x);
+        bh = static_cast<int>(blockIdx.y);
+    }
     const int b = bh / args.H;
     const int h = bh - b * args.H;
     const int kv0 = kt * kTile;
@@ -778,7 +784,9 @@ int run_bwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, const AttnB
     const bool split = Cfg::DS2 && a.n_qtiles >= kSplitMinTiles;
     auto kern = split ? attn_bwd_kernel<MC, HD, CAUSAL, true> : attn_bwd_kernel<MC, HD, CAUSAL, false>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    dim3 grid(a.n_qtiles, BH);
+    a.BH = BH;
+    a.band = causal_band(static_cast<long long>(s.N) * (2 * MC + 2 * HD + 36), BH, a.n_qtiles);
+    const dim3 grid = CAUSAL ? dim3(a.n_qtiles * BH, 1) : dim3(a.n_qtiles, BH);
     prof_begin(stream, "attn_bwd");
     kern<<<grid, kBwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tKD, tV, tDO, tL, tQA, tDQ, a);
     MORPHO_LAUNCH_CHECK("attn_bwd");

@@ -60,6 +60,7 @@ struct FwdCfg {
 
 struct FwdArgs {
     int N, Npad, H, D, n_qtiles;
+    int BH, band;   // causal launch order (causal_order)
     int mask_diag;  // also drop key j == query i
     float c2;  // 2 * scale * log2(e)
     const float* qb;
@@ -83,8 +84,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
     const int warp = warp_id();
     const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qt = CAUSAL ? (args.n_qtiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+    int qt, bh;
+    if (CAUSAL) {  // query tile qt meets qt + 1 key tiles: heaviest (last) first
+        int t;
+        causal_order(static_cast<int>(blockIdx.x), args.n_qtiles, args.BH, args.band, t, bh);
+        qt = args.n_qtiles - 1 - t;
+    } else {
+        qt = static_cast<int>(blockIdx.x);
+        bh = static_cast<int>(blockIdx.y);
+    }
     const int q0 = qt * kTile;
     const int n_kv_all = (args.N + kTile - 1) / kTile;
     const int n_kv = CAUSAL ? min(n_kv_all, qt + 1) : n_kv_all;
@@ -409,7 +417,9 @@ int run_fwd(const DeviceInfo& dev, const Shape& s, const ProjOut& p, __half* out
     a.status = dev.status;
     auto kern = attn_fwd_kernel<MC, HD, CAUSAL>;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    dim3 grid(a.n_qtiles, BH);
+    a.BH = BH;
+    a.band = causal_band(static_cast<long long>(s.N) * (2 * MC + 2 * HD), BH, a.n_qtiles);
+    const dim3 grid = CAUSAL ? dim3(a.n_qtiles * BH, 1) : dim3(a.n_qtiles, BH);
     prof_begin(stream, "attn_fwd");
     kern<<<grid, kFwdThreads, Cfg::SMEM_BYTES, stream>>>(tQ, tK, tV, a);
     MORPHO_LAUNCH_CHECK("attn_fwd");

@@ -159,6 +159,14 @@ int launch_reduce_weights(const Shape& s, const float* dw_part, int splits, cons
                           float* bucket, __half* dW_phi, __half* dW_V, __half* d_gate_q, __half* d_gate_k,
                           cudaStream_t stream);
 
+// Band width of the causal launch order (causal_order in sm100.cuh): 1 (longest first) when the
+// BH streams of `bytes_per_bh` each fit comfortably in L2 together; else all n_t tiles of a
+// (batch, head) in turn, so that the CTAs running together share few streams (at c5, bands of 8
+// tiles were 1.5 % slower than this, from the extra L2 misses, although they shorten the tail).
+inline int causal_band(long long bytes_per_bh, int BH, int n_t) {
+    return bytes_per_bh * BH <= (48ll << 20) ? 1 : n_t;
+}
+
 // fp16 outputs = alpha * bucket.
 int launch_finalize_weights(const Shape& s, const float* bucket, float alpha, __half* dW_phi, __half* dW_V,
                             __half* d_gate_q, __half* d_gate_k, cudaStream_t stream);

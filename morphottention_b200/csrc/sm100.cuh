@@ -458,6 +458,20 @@ __device__ __forceinline__ bool elect_one() {
     return pred != 0;
 }
 
+// Launch order of a causal attention grid (one CTA per (tile, batch*head), tile 0 the one with
+// the most work): linear block L -> (t, bh), the heaviest tiles first, in bands of `band` tile
+// indices taken for every bh in turn -- band 1 is pure longest-first, whose partial last wave
+// holds the lightest CTAs instead of the heavy tiles of the last heads; band n_t is the plain
+// (batch, head)-major order, whose concurrent CTAs share few (batch, head) streams in L2.
+__device__ __forceinline__ void causal_order(int L, int n_t, int BH, int band, int& t, int& bh) {
+    const int per = BH * band;
+    const int bi = L / per;
+    const int rem = L - bi * per;
+    const int gb = min(band, n_t - bi * band);
+    bh = rem / gb;
+    t = bi * band + (rem - bh * gb);
+}
+
 __device__ __forceinline__ int warp_id() { return __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x) >> 5, 0); }
 
 }  // namespace morpho
