@@ -34,26 +34,34 @@ constexpr uint32_t kRegsProducer = 56;
 constexpr uint32_t kRegsSoftmax = 200;
 static_assert(128 * kRegsProducer + 128 * kRegsSoftmax == kFwdThreads * 128, "register split");
 constexpr int kTile = 128;
-constexpr int kKvStages = 3;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int MC, int HD>
 struct FwdCfg {
+    // hd = 128: P (fp16, 64 columns) is written over the first half of S, which the softmax warps
+    // hold in registers by then, so S + O fit 256 TMEM columns and, with two K/V stages and no
+    // alignment slack, two CTAs share an SM as they do at hd <= 64.  S(j+1) is then issued after
+    // P.V(j) (in issue order it cannot overwrite P(j) before that MMA read it) instead of as soon as
+    // S(j) is read; the other CTA of the SM covers that wait.
+    static constexpr bool P_IN_S = HD > 64;
+    static constexpr int KV_STAGES = P_IN_S ? 2 : 3;
     static constexpr int Q_BYTES = kTile * MC * 2;
     static constexpr int K_BYTES = kTile * MC * 2;
     static constexpr int V_BYTES = kTile * HD * 2;
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = (Q_BYTES + 1023) / 1024 * 1024;
     static constexpr int K_STRIDE = (K_BYTES + 1023) / 1024 * 1024;
-    static constexpr int OFF_V = OFF_K + kKvStages * K_STRIDE;
-    static constexpr int OFF_BAR = OFF_V + kKvStages * V_BYTES;
+    static constexpr int OFF_V = OFF_K + KV_STAGES * K_STRIDE;
+    static constexpr int OFF_BAR = OFF_V + KV_STAGES * V_BYTES;
     static constexpr int USED = OFF_BAR + 256;
-    // hd = 128 needs 512 TMEM columns: keep those CTAs alone on their SM.
-    static constexpr int SMEM_BYTES = (HD > 64 && USED + 1024 < 120 * 1024) ? 120 * 1024 : USED + 1024;
+    // (P_IN_S: the dynamic shared memory is declared 1024-byte aligned, checked at run time,
+    // instead of 1 KB of slack, so that two CTAs of m = 64 fit an SM)
+    static constexpr int SMEM_BYTES = P_IN_S ? USED : USED + 1024;
+    static_assert(!P_IN_S || 2 * (SMEM_BYTES + 1024) <= 233472, "two CTAs per SM");
     static constexpr uint32_t TMEM_S = 0;
-    static constexpr uint32_t TMEM_P = 128;
-    static constexpr uint32_t TMEM_O = HD > 64 ? 256 : 192;
-    static constexpr uint32_t TMEM_COLS = HD > 64 ? 512 : 256;
+    static constexpr uint32_t TMEM_P = P_IN_S ? 0 : 128;
+    static constexpr uint32_t TMEM_O = P_IN_S ? 128 : 192;
+    static constexpr uint32_t TMEM_COLS = 256;
     static constexpr uint32_t QK_ROW_BYTES = MC * 2;
     static constexpr uint32_t V_ROW_BYTES = (HD > 64 ? 64 : HD) * 2;
 };
@@ -74,12 +82,16 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdArgs args) {
     using Cfg = FwdCfg<MC, HD>;
-    extern __shared__ uint8_t smem_raw[];
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if (Cfg::P_IN_S && (smem_u32(smem_raw) & 1023u) != 0u) {  // no slack to align in: refuse
+        if (threadIdx.x == 0) report_timeout(args.status, K_ATTN_FWD, 30);
+        return;
+    }
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     // bars: [0,S) kv_full, [S,2S) kv_empty, 2S q_full, 2S+1 s_full, 2S+2 p_full, 2S+3 o_done, 2S+4 drain,
     //       2S+5 s_free
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kKvStages + 6);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::KV_STAGES + 6);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int warp = warp_id();
@@ -98,8 +110,8 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     const int n_kv = CAUSAL ? min(n_kv_all, qt + 1) : n_kv_all;
 
     const uint32_t kv_full0 = smem_u32(bars);
-    const uint32_t kv_empty0 = smem_u32(bars + kKvStages);
-    const uint32_t q_full = smem_u32(bars + 2 * kKvStages);
+    const uint32_t kv_empty0 = smem_u32(bars + Cfg::KV_STAGES);
+    const uint32_t q_full = smem_u32(bars + 2 * Cfg::KV_STAGES);
     const uint32_t s_full = q_full + 8;
     const uint32_t p_full = q_full + 16;
     const uint32_t o_done = q_full + 24;
@@ -107,7 +119,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     const uint32_t s_free = q_full + 40;  // the softmax warps hold S_j in registers
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kKvStages; ++s) {
+        for (int s = 0; s < Cfg::KV_STAGES; ++s) {
             mbar_init(kv_full0 + 8 * s, 1);
             mbar_init(kv_empty0 + 8 * s, 1);  // released by the MMA commit after P.V
         }
@@ -144,9 +156,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
             int issued = 0;
             for (int j = 0; j < n_kv; ++j) {
-                const int s = j % kKvStages;
-                if (j >= kKvStages &&
-                    !mbar_wait(kv_empty0 + 8 * s, ((j / kKvStages) & 1) ^ 1, args.status, K_ATTN_FWD, 1)) {
+                const int s = j % Cfg::KV_STAGES;
+                if (j >= Cfg::KV_STAGES &&
+                    !mbar_wait(kv_empty0 + 8 * s, ((j / Cfg::KV_STAGES) & 1) ^ 1, args.status, K_ATTN_FWD, 1)) {
                     *abort_flag = 1u;
                     break;
                 }
@@ -168,8 +180,8 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             // Bounded drain of loads still in flight (abort path, and the Q tile).
             mbar_wait(q_full, 0, args.status, K_ATTN_FWD, 2);
             if (*abort_flag) {
-                for (int i = max(0, issued - kKvStages); i < issued; ++i)
-                    mbar_wait(kv_full0 + 8 * (i % kKvStages), (i / kKvStages) & 1, args.status, K_ATTN_FWD, 2);
+                for (int i = max(0, issued - Cfg::KV_STAGES); i < issued; ++i)
+                    mbar_wait(kv_full0 + 8 * (i % Cfg::KV_STAGES), (i / Cfg::KV_STAGES) & 1, args.status, K_ATTN_FWD, 2);
             }
         }
       } else if (warp == 1) {
@@ -186,7 +198,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
             const uint32_t sQ = smem_u32(smem + Cfg::OFF_Q);
             bool ok = mbar_wait_warp(q_full, 0, args.status, K_ATTN_FWD, 3);
             auto issue_s = [&](int j) {
-                const uint32_t sK = smem_u32(smem + Cfg::OFF_K + (j % kKvStages) * Cfg::K_STRIDE);
+                const uint32_t sK = smem_u32(smem + Cfg::OFF_K + (j % Cfg::KV_STAGES) * Cfg::K_STRIDE);
 #pragma unroll
                 for (int ks = 0; ks < MC / 16; ++ks) {
                     const uint64_t ad = make_sdesc(sQ + ks * 32, 16, qk_sbo, qk_sw);
@@ -203,15 +215,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 }
             }
             for (int j = 0; ok && j < n_kv; ++j) {
-                const int s = j % kKvStages;
+                const int s = j % Cfg::KV_STAGES;
                 // S_{j+1} as soon as the softmax warps have read S_j (its columns are free),
                 // so the next scores are ready when they finish P_j
-                if (j + 1 < n_kv) {
-                    const int s1 = (j + 1) % kKvStages;
+                if (!Cfg::P_IN_S && j + 1 < n_kv) {
+                    const int s1 = (j + 1) % Cfg::KV_STAGES;
                     // (no abort-flag read here: every shared-memory probe of the MMA thread stalls
                     // it while MMAs are in flight; a failure elsewhere ends its bounded waits)
                     if (!mbar_wait_warp(s_free, j & 1, args.status, K_ATTN_FWD, 12) ||
-                        !mbar_wait_warp(kv_full0 + 8 * s1, ((j + 1) / kKvStages) & 1, args.status, K_ATTN_FWD, 6)) {
+                        !mbar_wait_warp(kv_full0 + 8 * s1, ((j + 1) / Cfg::KV_STAGES) & 1, args.status, K_ATTN_FWD, 6)) {
                         ok = false;
                         break;
                     }
@@ -232,6 +244,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                 }
                 umma_commit_w(o_done);
                 umma_commit_w(kv_empty0 + 8 * s);
+                if (Cfg::P_IN_S && j + 1 < n_kv) {  // S(j+1) over P(j), which P.V(j) has read (issue order)
+                    const int s1 = (j + 1) % Cfg::KV_STAGES;
+                    if (!mbar_wait_warp(kv_full0 + 8 * s1, ((j + 1) / Cfg::KV_STAGES) & 1, args.status, K_ATTN_FWD, 6)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
             }
             if (!ok) {
                 *abort_flag = 1u;
