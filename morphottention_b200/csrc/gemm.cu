@@ -34,11 +34,11 @@ constexpr int kGemmThreads = 320;  // producer, MMA, 8 epilogue warps
 
 enum BMode : int { B_SINGLE = 0, B_SPLIT_N = 1, B_SPLIT_K = 2 };
 
-// Epilogue staging: 4 KB of shared memory per epilogue warp (32 rows of up to 128 bytes), through
-// which each warp turns its row-per-lane results into coalesced global stores (store_rows32).
-constexpr int kEpiStageBytes = 4096;
-
-template <int BN>
+// Epilogue staging: per epilogue warp 32 rows of its widest store (Epi::kStageBytes: 4 KB for
+// 128-byte fp32 rows, 2 KB for the fp16 dX rows), through which each warp turns its row-per-lane
+// results into coalesced global stores (store_rows32).  The dX GEMM keeps its footprint small so
+// that the data-parallel all-reduce kernel, which runs beside it, still finds room on its SMs.
+template <int BN, int EPI_STAGE>
 struct GemmCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
@@ -47,7 +47,7 @@ struct GemmCfg {
     static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int EPI_OFFSET = BAR_OFFSET + 256;
     // ring + barriers + 8 epilogue staging buffers + 1 KB alignment slack
-    static constexpr int SMEM_BYTES = EPI_OFFSET + 8 * kEpiStageBytes + 1024;
+    static constexpr int SMEM_BYTES = EPI_OFFSET + 8 * EPI_STAGE + 1024;
     static_assert(SMEM_BYTES <= 232448, "smem budget");
     static constexpr uint32_t TMEM_COLS = 2 * BN;                 // double-buffered accumulator
     static_assert(TMEM_COLS <= 512, "TMEM");
@@ -102,6 +102,7 @@ struct ProjParams {
 template <int MC>
 struct EpiProj {
     using Params = ProjParams;
+    static constexpr int kStageBytes = 4096;  // phi rows: 32 fp32
     template <int BN>
     __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/, uint32_t stage, int lane) {
         const bool live = row < p.T;
@@ -246,6 +247,7 @@ struct HalfParams {
 
 struct EpiHalf {
     using Params = HalfParams;
+    static constexpr int kStageBytes = 2048;  // 32 fp16 columns
     template <int BN>
     __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int /*z*/, uint32_t stage, int lane) {
         const bool coal = row - lane + 31 < p.M;  // warp-uniform: all 32 rows exist
@@ -290,6 +292,7 @@ struct F32Params {
 
 struct EpiF32 {
     using Params = F32Params;
+    static constexpr int kStageBytes = 4096;  // 32 fp32 columns
     template <int BN>
     __device__ static void run(const Params& p, uint32_t tacc, int row, int n0, int z, uint32_t stage, int lane) {
         const bool coal = row - lane + 31 < p.M;  // warp-uniform: all 32 rows exist
@@ -327,7 +330,7 @@ template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                 const __grid_constant__ CUtensorMap tmB1, const GemmArgs args, const typename Epi::Params ep) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, Epi::kStageBytes>;
     constexpr int STAGES = Cfg::STAGES;
     // epilogue warps 2..9; with BN >= 128 each of the two warpgroups takes half the columns,
     // with BN = 64 only warps 2..5 work
@@ -497,7 +500,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quad = warp & 3;
         const int half = (warp - 2) >> 2;  // column half of the tile
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-        const uint32_t estage = smem_u32(smem + Cfg::EPI_OFFSET + (warp - 2) * kEpiStageBytes);
+        const uint32_t estage = smem_u32(smem + Cfg::EPI_OFFSET + (warp - 2) * Epi::kStageBytes);
         int j = 0;
         for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++j) {
             int m0, n0, z;
@@ -528,7 +531,7 @@ template <int BN, bool A_MN, bool B_MN, int BMODE, class Epi>
 int run_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1, const GemmArgs& args,
              const typename Epi::Params& ep, int splits, int sms, cudaStream_t stream, const char* name) {
     auto kern = gemm_kernel<BN, A_MN, B_MN, BMODE, Epi>;
-    constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+    constexpr int smem = GemmCfg<BN, Epi::kStageBytes>::SMEM_BYTES;
     MORPHO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     GemmArgs a = args;
     a.tiles_m = (args.M + BM - 1) / BM;
