@@ -28,7 +28,10 @@ namespace morpho {
 namespace {
 
 constexpr int kPeerMaxWorld = 16;
-constexpr int kPeerThreads = 256;
+// 128 threads: one warp per SM sub-partition, whose register share still fits beside the dX GEMM's
+// three warps there (registers are allocated per sub-partition); with two warps there it did not,
+// and the CTAs waited for the GEMM's SMs to empty.
+constexpr int kPeerThreads = 128;
 constexpr int kPeerCtas = 128;
 constexpr uint32_t K_PEER = 5;  // status-word kernel id (site: 1 ready, 2 done)
 // Region layout: signal block (ready[16], done[16], local CTA counter), then two buckets.
