@@ -53,7 +53,10 @@ def _compare_masked(ours, ref, cfg):
     return errs
 
 
-@pytest.mark.parametrize("cfg", CASES + [MorphoConfig("n15_causal", 2, 15, 64, 2, 32, 2.0, True, 34)],
+@pytest.mark.parametrize("cfg", CASES + [MorphoConfig("n15_causal", 2, 15, 64, 2, 32, 2.0, True, 34),
+                                         # hd 128 forward (P over S, two K/V stages): causal, ragged,
+                                         # three key tiles, a dead first row
+                                         MorphoConfig("hd128_causal", 1, 290, 256, 2, 32, 0.5, True, 39)],
                          ids=lambda c: c.name)
 def test_mask_diag_parity(cuda, cfg):
     inp = inputs(cfg, cuda, random_gates=True, with_grad_out=True)
